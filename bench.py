@@ -1,0 +1,353 @@
+"""Decode benchmark: batch-1 greedy decode tokens/s and % of the HBM roofline at 4k context.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (BASELINE config 2 at "4k ctx"): the 36-layer Qwen3-8B-architecture model with seeded random-init
+FP8 weights (E4M3, per-output-channel fp32 scales), bf16 embeddings, FP8 per-channel lm_head (151936 rows),
+a bf16 KV cache sized for 4096 tokens pre-filled with N(0,1) up to position 4096-K, then K greedy decode
+steps under one CUDA graph (ctx 4096-K .. 4095). One step = one token. Every step reads ~8.2 GB (weights +
+KV), far more than the 126 MB L2, so no L2 flush is needed between steps.
+
+Timing: W untimed warm-up steps, state reset, then exactly K graph replays between CUDA events on the
+replay stream, with a synchronize (and for N>1 a barrier) on both sides; max over ranks. `e2e` repeats the
+K steps through the public engine API with, every step, the input token copied from pinned host memory
+and the output token read back to pinned host memory (host-synchronous streaming decode).
+
+N > 1: tensor parallelism is not wired into this arm yet, so each rank decodes its own full replica
+(scaling "weak", no collective); rank 0 prints the aggregate.
+
+--impl reference: the reference engine's CPU path (its `model.forward` math restated in oracle/, run on the
+host cores with all threads), one decoder layer per step at the same context plus the lm_head, reported as
+tokens/s of the full 36-layer step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(REPO, "inferencekit-engines_b200")
+for _p in (REPO, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+
+METRIC = "batch-1 decode tokens/s at 4k ctx (Qwen3-8B FP8, per-channel scales, FP8 lm_head)"
+UNIT = "tokens/s"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples while the timed region runs."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.gpu), "-lms", "50"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            time.sleep(0.3)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.out = ""
+        if self.proc is not None:
+            time.sleep(0.1)
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+
+    def summary(self):
+        rows = [r.split(", ") for r in (self.out or "").strip().splitlines() if r.count(",") >= 8]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no nvidia-smi samples"]}
+        sm = [float(r[1]) for r in rows]
+        smax = float(rows[0][2])
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for n, v in zip(names, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(n)
+        under = [s for s in sm if s > 0.5 * smax] or sm
+        return {"sm_mhz": statistics.median(under), "sm_max_mhz": smax, "samples": len(sm),
+                "power_w_max": max(float(r[3]) for r in rows), "reasons": sorted(reasons)}
+
+
+def step_bytes(m, ctx_lo, ctx_hi):
+    """Algorithmic bytes per token, averaged over the contexts the timed steps see."""
+    wb = m.weight_bytes()
+    fixed = sum(wb.values())
+    kv = m.kv_bytes_per_token((ctx_lo + ctx_hi) / 2.0)
+    return fixed + kv, wb
+
+
+def gate_up_kernel_timing(eng, reps):
+    """The dominant kernel (gate_up GEMV, 52% of the step's weight bytes) timed alone with CUDA events on
+    the launching stream, cycling through the 36 layers' weights (3.6 GB, no L2 reuse)."""
+    m = eng.m
+    s = torch.cuda.current_stream()
+    for L in m.layers[:4]:
+        eng._gemv(2, L.gu, eng.resid, L.ln2, eng.h)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = 0
+    e0.record(s)
+    for r in range(reps):
+        for L in m.layers:
+            eng._gemv(2, L.gu, eng.resid, L.ln2, eng.h)
+            n += 1
+    e1.record(s)
+    torch.cuda.synchronize()
+    L = m.layers[0]
+    H = m.cfg.hidden
+    bytes_per_launch = L.gu.packed.numel() + 4 * L.gu.scale.numel() + 2 * H + 2 * H + 2 * (L.gu.N // 2)
+    return e0.elapsed_time(e1) / n * 1e-3, bytes_per_launch, n
+
+
+def load_traffic():
+    p = os.path.join(REPO, "profiles", "gate_up_gemv_traffic.json")
+    try:
+        with open(p) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return None
+
+
+def cpu_baseline(ctx: int, budget_s: float = 25.0, threads: int | None = None):
+    """The reference's CPU path (oracle restatement of Q/model.py forward with the decode kernel's fp32
+    attention) on the host cores: one layer decode step at `ctx` (median of a few) and the FP8 lm_head,
+    extrapolated to the 36-layer step."""
+    import model as M
+    from oracle import qwen3_ref as O
+    threads = threads or os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    H, I = 4096, 12288
+    w = {}
+    for name, parts in (("qkv", [("q_proj", 4096), ("k_proj", 1024), ("v_proj", 1024)]),
+                        ("gate_up", [("gate_proj", I), ("up_proj", I)])):
+        qs = [M.synth_linear(0, "cpu." + n, r, H, "channel") for n, r in parts]
+        w[name] = (torch.cat([a for a, _ in qs]), torch.cat([b for _, b in qs]).contiguous())
+    w["o_proj"] = M.synth_linear(0, "cpu.o", H, H, "channel")
+    w["down_proj"] = M.synth_linear(0, "cpu.d", H, I, "channel")
+    ones = torch.ones(H, dtype=torch.bfloat16)
+    hd1 = torch.ones(128, dtype=torch.bfloat16)
+    L = O.LayerW(ones, ones, hd1, hd1, *w["qkv"], *w["o_proj"], *w["gate_up"], *w["down_proj"])
+    kc = torch.randn(8, ctx + 1, 128).to(torch.bfloat16)
+    vc = torch.randn(8, ctx + 1, 128).to(torch.bfloat16)
+    cos, sin = M.rope_tables(ctx + 1, 128, 1e6, "cpu")
+    h = torch.randn(H).to(torch.bfloat16)
+    times = []
+    t_start = time.perf_counter()
+    for i in range(8):
+        t0 = time.perf_counter()
+        O.decode_layer(h, L, kc, vc, ctx, cos, sin, 1e-6, attn_impl="f32")
+        times.append(time.perf_counter() - t0)
+        if i >= 2 and time.perf_counter() - t_start > budget_s * 0.6:
+            break
+    layer_s = statistics.median(times[1:]) if len(times) > 1 else times[0]
+    hw, hs = M.quantize_fp8(M.randn((151936, H), 0, "cpu.head", std=0.02), "channel")
+    O.lm_head_logits(h, ones, hw[:1024], hs[:1024], 1e-6)
+    t0 = time.perf_counter()
+    O.lm_head_logits(h, ones, hw, hs, 1e-6)
+    head_s = time.perf_counter() - t0
+    step_s = 36 * layer_s + head_s
+    return {"value": 1.0 / step_s, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{len(times)} one-layer decode steps at ctx {ctx} (median {layer_s * 1e3:.1f} ms) + one FP8 "
+                      f"lm_head ({head_s * 1e3:.0f} ms), extrapolated to 36 layers + head",
+            "layer_ms": layer_s * 1e3, "head_ms": head_s * 1e3}
+
+
+def run_reference(args):
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return
+    ctx = 4096 - args.steps
+    base = cpu_baseline(ctx, budget_s=max(20.0, 0.5 * (args.steps + args.warmup)))
+    out = {"metric": METRIC, "value": base["value"], "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 / base["value"], "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "fp8-e4m3 x fp8 -> fp32 (bf16 activations)",
+           "data": "synthetic (seeded random-init weights, N(0,1) KV)",
+           "config": {"workload": f"reference CPU path: Qwen3-8B-shape decode step at ctx {ctx}", "global_batch": 1,
+                      "seq_len": 4096, "parallelism": "cpu"},
+           "cpu_baseline": base,
+           "e2e": {"value": base["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+
+
+def run_ours(args):
+    import model as M
+    from generate import Engine
+    ws, rank, local = dist_env()
+    if ws > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    dev = f"cuda:{local}" if ws > 1 else "cuda:0"
+    torch.cuda.set_device(dev)
+    K, W = args.steps, args.warmup
+    max_seq = 4096
+    start = max_seq - K
+    assert start > 0, "--steps must be < 4096"
+    cfg = M.Config()
+    m = M.Qwen3FP8Decode.synthetic(cfg, max_seq=max_seq, device=dev, seed=args.seed, scale_mode=args.scale,
+                                   head_dtype=args.head, norm_init="ones")
+    m.fill_cache_random(start, seed=1234 + rank)
+    eng = Engine(m, pdl=not args.no_pdl, attn_chunk=args.chunk)
+    eng.token.fill_(1)
+    eng.state.copy_(torch.tensor([start, 0], dtype=torch.int32))
+    eng.capture()
+
+    def reset():
+        eng.token.fill_(1)
+        eng.state.copy_(torch.tensor([start, 0], dtype=torch.int32, device=dev))
+        eng.best.zero_()
+
+    def barrier():
+        if ws > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    stream = torch.cuda.current_stream()
+    # warm-up
+    reset()
+    eng.step(W)
+    torch.cuda.synchronize()
+    reset()
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local if ws > 1 else 0) as clk:
+        torch.cuda.synchronize()
+        barrier()
+        e0.record(stream)
+        for _ in range(K):
+            eng.graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+    t = e0.elapsed_time(e1) * 1e-3
+    tokens = eng.out_tokens[:K].tolist()
+    err = eng.k.device_error()
+
+    # e2e through the public API: pinned h2d of the step's input token, graph replay, d2h of its output
+    reset()
+    torch.cuda.synchronize()
+    h_in = torch.empty(1, dtype=torch.int32, pin_memory=True)
+    h_out = torch.empty(1, dtype=torch.int32, pin_memory=True)
+    h_in[0] = 1
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(K):
+        eng.token.copy_(h_in, non_blocking=True)
+        eng.graph.replay()
+        h_out.copy_(eng.token, non_blocking=True)
+        stream.synchronize()
+        h_in[0] = h_out[0]
+    t_e2e = time.perf_counter() - t0
+    barrier()
+
+    # dominant kernel alone (roofline)
+    k_s, k_bytes, k_n = gate_up_kernel_timing(eng, reps=2)
+    peak, peak_src = peaks()
+    bytes_tok, wb = step_bytes(m, start, max_seq - 1)
+
+    if ws > 1:
+        import torch.distributed as dist
+        tt = torch.tensor([t, t_e2e], dtype=torch.float64, device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t, t_e2e = float(tt[0]), float(tt[1])
+    value = ws * K / t
+    if rank == 0:
+        achieved = k_bytes / k_s / 1e9
+        traffic = load_traffic()
+        out = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": K, "warmup": W,
+            "ms_per_step": t / K * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "fp8-e4m3 x fp8 -> fp32 (bf16 activations, bf16 KV)", "data": "synthetic (seeded random-init "
+            "weights, N(0,1) KV cache, no checkpoint)",
+            "config": {"workload": f"Qwen3-8B FP8 decode, 36 layers, per-channel FP8 + FP8 lm_head, KV 4096 "
+                                   f"pre-filled to {start}, {K} greedy steps (ctx {start}..{max_seq - 1}), CUDA graph",
+                       "global_batch": ws, "seq_len": max_seq, "parallelism": "replica" if ws > 1 else "tp1",
+                       "scale_mode": args.scale, "head": args.head, "attn_chunk": args.chunk, "pdl": not args.no_pdl,
+                       "l2": "inputs larger than L2 (8.2 GB read per step), no flush"},
+            "e2e": {"value": ws * K / t_e2e, "unit": UNIT, "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
+            "gpu_launches": K * (3 + 5 * len(m.layers)),
+            "roofline": {"bound": "hbm", "kernel": "fp8 gate_up GEMV (SwiGLU epilogue)", "achieved": achieved,
+                         "peak": peak, "peak_source": f"{peak_src} hbm_gbs", "unit": "GB/s", "frac": achieved / peak,
+                         "traffic": traffic.get("bytes_per_launch") if traffic else None,
+                         "bytes_per_launch_algorithmic": k_bytes, "launch_us": k_s * 1e6, "launches_timed": k_n},
+            "step_roofline": {"bytes_per_token": bytes_tok, "achieved_gbs": bytes_tok * K / t / 1e9,
+                              "frac": bytes_tok * K / t / 1e9 / peak, "roofline_tok_s": peak * 1e9 / bytes_tok,
+                              "breakdown": dict(wb, kv=int(bytes_tok - sum(wb.values())))},
+            "clocks": clk.summary(),
+            "device_error": err,
+            "tokens_head": tokens[:8],
+        }
+        if not args.no_cpu_baseline:
+            out["cpu_baseline"] = cpu_baseline(start)
+        print(json.dumps(out), flush=True)
+    if ws > 1:
+        import torch.distributed as dist
+        eng.graph = None
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--scale", default="channel", choices=["channel", "block"])
+    ap.add_argument("--head", default="fp8", choices=["fp8", "bf16"])
+    ap.add_argument("--chunk", type=int, default=64)
+    ap.add_argument("--no-pdl", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

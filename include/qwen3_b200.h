@@ -1,0 +1,121 @@
+/*
+ * qwen3_b200.h - C ABI of the B200 (sm_100a) Qwen3-8B FP8 decode-step kernels.
+ *
+ * Drop-in replacement for the pybind11 ops of the reference engine
+ * (KittenML/inferencekit-engines, qwen3-8b-fp8_rtx-5090/kernels/decode.cu:822-830, loaded by
+ * kernels/__init__.py:11-24 and called from generate.py:102-119). Each reference op maps to one entry point
+ * below; the citations give the reference function each one replaces.
+ *
+ * Conventions
+ *   - All tensor arguments are DEVICE pointers owned by the caller; nothing is allocated by any entry point.
+ *     Scratch (`part`, `counters`, `o_part`, `ml_part`) is caller-provided; counters must be zero before the
+ *     first launch and are left zero by every kernel that uses them.
+ *   - Every launch goes to `stream` (a cudaStream_t) with no host synchronisation, so the calls can be
+ *     captured into a CUDA graph.
+ *   - Return value: QK_OK, or an error code with a message from qk_last_error() (thread-local). Bad
+ *     arguments are rejected before anything is launched.
+ *   - bf16 tensors are passed as void* (__nv_bfloat16 in device code); fp8 weights are e4m3 bytes in the
+ *     packed layout of model.pack_fp8 (1 KiB tiles in mma fragment order).
+ *   - Process-global state, as in the reference: the PDL switch (qk_set_pdl). Not thread-safe to change
+ *     while another thread launches.
+ */
+#ifndef QWEN3_B200_H
+#define QWEN3_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* qk_stream_t; /* == cudaStream_t */
+
+enum {
+  QK_OK = 0,
+  QK_EINVAL = 1,  /* bad argument (message in qk_last_error) */
+  QK_ECUDA = 2    /* CUDA runtime error (message in qk_last_error) */
+};
+
+/* GEMV kinds. 0-3 are the reference's kinds (decode.cu:734-746); 5-8 are the tensor-parallel variants. */
+enum {
+  QK_GEMV_QKV = 0,          /* RMSNorm(x, norm_w) -> quant -> bf16 store                       */
+  QK_GEMV_O = 1,            /* quant(x) -> out[n] = bf16(out[n] + bf16(y[n]))  (residual, in place) */
+  QK_GEMV_GATE_UP = 2,      /* RMSNorm -> quant -> SwiGLU(gate rows, up rows) -> bf16 [N/2]      */
+  QK_GEMV_DOWN = 3,         /* like O with K = 12288 (K is an argument here)                      */
+  QK_GEMV_PARTIAL = 5,      /* quant(x) -> fp32 store (row-parallel shard before the all-reduce)  */
+  QK_GEMV_QKV_RESADD = 6,   /* x = bf16(resid + bf16(resadd)) first (written back), then as QKV   */
+  QK_GEMV_GATE_UP_RESADD = 7 /* the same residual update, then as GATE_UP                         */
+};
+
+enum { QK_SCALE_BLOCK128 = 0, QK_SCALE_CHANNEL = 1 };
+
+/* Library version (major*10000 + minor*100 + patch) and the last error message of this thread. */
+int qk_version(void);
+const char* qk_last_error(void);
+
+/* Programmatic dependent launch on/off for subsequent launches (reference decode.cu:713 set_pdl). */
+int qk_set_pdl(int on);
+
+/* Profiling timestamps (reference decode.cu:716 set_timeline). Only NULL (disabled) is supported. */
+int qk_set_timeline(uint64_t* buf);
+
+/* Read and clear the device-side error word (bit 1: a bounded wait gave up; bit 2: bad step state or
+ * token id). Synchronises `stream`. No counterpart in the reference (its waits are unbounded). */
+int qk_get_device_error(int* err, qk_stream_t stream);
+
+/*
+ * FP8 W8A8 GEMV (reference decode.cu:765-774 fp8_gemv, kernels :128-335).
+ *   w          packed fp8 [N x K] (model.pack_fp8; gate|up units interleaved for kind 2/7)
+ *   w_scale    fp32 scales, [N/128][K/128] (QK_SCALE_BLOCK128) or [N] (QK_SCALE_CHANNEL)
+ *   x          bf16 [K] input (kinds 6/7: the residual stream, updated in place through resid_out)
+ *   norm_w     bf16 [K] RMSNorm weight (kinds 0, 2, 6, 7), else may be NULL
+ *   resadd     fp32 [K] sums added to the residual (kinds 6, 7), else NULL
+ *   resid_out  bf16 [K] destination of the updated residual (kinds 6, 7; may equal x), else NULL
+ *   out        bf16 output: [N] (0, 6), residual [N] in place (1, 3), [N/2] (2, 7); fp32 [N] for kind 5
+ *   part       fp32 scratch of N*K/128 floats; counters: int scratch of N/8 ints, zeroed once
+ *   warps/stages/stage_tiles/pre/ctas_per_sm: launch shape (0 = default). pre = ring stages issued
+ *              before waiting on the previous kernel; stage_tiles = 1 KiB tiles per ring stage.
+ */
+int qk_fp8_gemv(int kind, const void* w, const float* w_scale, int scale_mode, const void* x, const void* norm_w,
+                const float* resadd, void* resid_out, void* out, int N, int K, float eps, float* part, int* counters,
+                int warps, int stages, int stage_tiles, int pre, int ctas_per_sm, qk_stream_t stream);
+
+/*
+ * Fused q/k RMSNorm + RoPE + KV append + GQA split-KV decode attention
+ * (reference decode.cu:776-800 attention, kernel :379-570).
+ *   qkv        bf16 [batch][qkv_stride]: n_q = 4*n_kv query heads, then n_kv k heads, n_kv v heads (128 each)
+ *   state      int32, per sequence b: state[b*state_stride] = position of the new token
+ *   k_cache/v_cache  bf16 [batch][n_kv][max_seq][128] of ONE layer; slot `pos` of each head is written
+ *   o_part     fp32 [batch][n_q][max_splits][128]; ml_part fp32 [batch][n_q][max_splits][2]
+ *   counters   int32 [batch][n_kv], zero before the first launch (left zero)
+ *   out        bf16 [batch][n_q*128]
+ *   chunk      keys per CTA: 32, 64 or 128; requires max_splits*chunk >= max_seq
+ */
+int qk_attention(const void* qkv, const void* q_norm_w, const void* k_norm_w, const void* cos_tab,
+                 const void* sin_tab, const int* state, void* k_cache, void* v_cache, float* o_part,
+                 float* ml_part, int* counters, void* out, int batch, int n_kv, int max_seq, int max_splits,
+                 int qkv_stride, int state_stride, float scale, float eps, int chunk, qk_stream_t stream);
+
+/*
+ * Final RMSNorm + lm_head GEMV + greedy argmax (reference decode.cu:802-810 lm_head_argmax, :584-661).
+ * bf16 head (reference format): w bf16 [V][4096] row-major, w_scale NULL.
+ * fp8 head (per-channel): w packed fp8 [V x 4096], w_scale fp32 [V], part/counters as qk_fp8_gemv.
+ * logits bf16 [V]; best: packed (value, ~index) u64, zero before the launch (qk_finalize clears it).
+ * row_offset: vocabulary index of row 0 (vocab-parallel shards). ctas: CTAs (0 = one per SM).
+ */
+int qk_lm_head_argmax(const void* w, const float* w_scale, int head_fp8, const void* x, const void* norm_w,
+                      void* logits, unsigned long long* best, int V, int row_offset, float eps, float* part,
+                      int* counters, int ctas, qk_stream_t stream);
+
+/* resid[b] = table[token[b]] for b < batch (reference decode.cu:812 embed, :667-673). */
+int qk_embed(const int* token, const void* table, void* resid, int vocab, int batch, qk_stream_t stream);
+
+/* token = argmax key, out_tokens[step] = token, pos++, step++, best = 0; state = [pos, step] per sequence
+ * (reference decode.cu:817 finalize, :676-687). out_len: capacity of out_tokens per sequence. */
+int qk_finalize(unsigned long long* best, int* token, int* out_tokens, int* state, int out_len, int batch,
+                qk_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QWEN3_B200_H */

@@ -1,0 +1,292 @@
+// C ABI of the B200 decode kernels: argument checks, launch shapes, PDL launches. One translation unit so
+// the device symbols (error word) are shared by every kernel without relocatable device code.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/qwen3_b200.h"
+#include "attention.cuh"
+#include "common.cuh"
+#include "gemv.cuh"
+
+using namespace qk;
+
+namespace {
+
+thread_local char g_msg[512] = "";
+bool g_pdl = false;
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_msg, sizeof(g_msg), fmt, ap);
+  va_end(ap);
+  return code;
+}
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(QK_ECUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+int device_sms() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (!cache[dev]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = n > 0 ? n : 148;
+  }
+  return cache[dev];
+}
+
+// Raise a kernel's dynamic shared-memory limit once per (kernel, device); done on the first (eager) call,
+// so nothing but launches happen while a stream is being captured.
+int ensure_smem(const void* fn, int bytes) {
+  static std::mutex mu;
+  static const void* fns[256];
+  static int devs[256], limit[256];
+  static int n = 0;
+  if (bytes <= 48 * 1024) return QK_OK;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lk(mu);
+  for (int i = 0; i < n; ++i)
+    if (fns[i] == fn && devs[i] == dev && limit[i] >= bytes) return QK_OK;
+  int optin = 0;
+  cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  if (bytes > optin) return fail(QK_EINVAL, "needs %d bytes of shared memory per CTA, device allows %d", bytes, optin);
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+  if (n < 256) { fns[n] = fn; devs[n] = dev; limit[n] = optin; ++n; }
+  return QK_OK;
+}
+
+template <typename... KArgs, typename... Args>
+int launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = g_pdl ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, args...);
+  if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
+  return QK_OK;
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+struct GemvShape { int warps, stages, stage_tiles, pre, ctas; };
+
+GemvShape gemv_defaults(int kind) {
+  // 8 warps x 4 stages x 4 KiB ring per warp (128 KiB per CTA), one CTA per SM
+  const bool pairs = (kind == QK_GEMV_GATE_UP || kind == QK_GEMV_GATE_UP_RESADD);
+  return GemvShape{8, 4, pairs ? 2 : 4, 4, 1};
+}
+
+template <int PRO, int EPI, int NG>
+int launch_gemv_scaled(int scale_mode, const GemvParams& p, const GemvShape& sh, cudaStream_t stream) {
+  const int smem = gemv_smem(p.K, sh.warps, sh.stages, sh.stage_tiles * 1024 * NG).total;
+  const dim3 grid(device_sms() * sh.ctas), block(sh.warps * 32);
+  if (scale_mode == QK_SCALE_CHANNEL) {
+    auto k = fp8_gemv_kernel<PRO, EPI, SCALE_CHANNEL, NG>;
+    if (int r = ensure_smem((const void*)k, smem)) return r;
+    return launch(k, grid, block, smem, stream, p);
+  }
+  auto k = fp8_gemv_kernel<PRO, EPI, SCALE_BLOCK, NG>;
+  if (int r = ensure_smem((const void*)k, smem)) return r;
+  return launch(k, grid, block, smem, stream, p);
+}
+
+}  // namespace
+
+extern "C" {
+
+int qk_version(void) { return 100; }
+const char* qk_last_error(void) { return g_msg; }
+
+int qk_set_pdl(int on) {
+  g_pdl = on != 0;
+  return QK_OK;
+}
+
+int qk_set_timeline(uint64_t* buf) {
+  if (buf) return fail(QK_EINVAL, "timeline stamps are not built into these kernels; pass NULL");
+  return QK_OK;
+}
+
+int qk_get_device_error(int* err, qk_stream_t stream) {
+  if (!err) return fail(QK_EINVAL, "err is NULL");
+  int zero = 0;
+  cudaError_t e = cudaMemcpyFromSymbolAsync(err, g_dev_error, sizeof(int), 0, cudaMemcpyDeviceToHost, stream);
+  if (e == cudaSuccess) e = cudaMemcpyToSymbolAsync(g_dev_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) return cuda_fail(e, "reading the device error word");
+  return QK_OK;
+}
+
+int qk_fp8_gemv(int kind, const void* w, const float* w_scale, int scale_mode, const void* x, const void* norm_w,
+                const float* resadd, void* resid_out, void* out, int N, int K, float eps, float* part, int* counters,
+                int warps, int stages, int stage_tiles, int pre, int ctas_per_sm, qk_stream_t stream) {
+  GemvShape sh = gemv_defaults(kind);
+  if (warps) sh.warps = warps;
+  if (stages) sh.stages = stages;
+  if (stage_tiles) sh.stage_tiles = stage_tiles;
+  if (pre >= 0) sh.pre = pre;
+  if (ctas_per_sm) sh.ctas = ctas_per_sm;
+  if (sh.warps < 4 || sh.warps > 16) return fail(QK_EINVAL, "warps must be in [4, 16], got %d", sh.warps);
+  if (sh.stages < 1 || sh.stages > 16 || sh.stage_tiles < 1 || sh.stage_tiles > 64 || sh.ctas < 1 || sh.ctas > 8)
+    return fail(QK_EINVAL, "bad launch shape stages=%d stage_tiles=%d ctas_per_sm=%d", sh.stages, sh.stage_tiles, sh.ctas);
+  if (!w || !w_scale || !x || !out || !part || !counters) return fail(QK_EINVAL, "null pointer argument");
+  if (scale_mode != QK_SCALE_BLOCK128 && scale_mode != QK_SCALE_CHANNEL) return fail(QK_EINVAL, "bad scale_mode %d", scale_mode);
+  if (K <= 0 || K % QB || K > 16384) return fail(QK_EINVAL, "K=%d must be a positive multiple of 128, at most 16384", K);
+  const bool pairs = (kind == QK_GEMV_GATE_UP || kind == QK_GEMV_GATE_UP_RESADD);
+  if (N <= 0 || N % (pairs ? 16 : 8)) return fail(QK_EINVAL, "N=%d must be a positive multiple of %d", N, pairs ? 16 : 8);
+  if (scale_mode == QK_SCALE_BLOCK128 && N % QB) return fail(QK_EINVAL, "block-128 scales need N %% 128 == 0 (N=%d)", N);
+  const bool norm = (kind == QK_GEMV_QKV || kind == QK_GEMV_GATE_UP || kind == QK_GEMV_QKV_RESADD || kind == QK_GEMV_GATE_UP_RESADD);
+  const bool resadd_k = (kind == QK_GEMV_QKV_RESADD || kind == QK_GEMV_GATE_UP_RESADD);
+  if (norm && !norm_w) return fail(QK_EINVAL, "kind %d needs norm_w", kind);
+  if (resadd_k && (!resadd || !resid_out)) return fail(QK_EINVAL, "kind %d needs resadd and resid_out", kind);
+  if (!aligned(w, 16) || !aligned(x, 16) || !aligned(out, 16) || !aligned(w_scale, 8) || !aligned(part, 16) ||
+      (norm_w && !aligned(norm_w, 16)) || (resadd && !aligned(resadd, 16)) || (resid_out && !aligned(resid_out, 16)))
+    return fail(QK_EINVAL, "tensor pointers must be 16-byte aligned");
+  GemvParams p = {};
+  p.w = static_cast<const uint8_t*>(w);
+  p.ws = w_scale;
+  p.x = static_cast<const bf16*>(x);
+  p.norm_w = static_cast<const bf16*>(norm_w);
+  p.resadd = resadd;
+  p.resid_out = static_cast<bf16*>(resid_out);
+  p.out = static_cast<bf16*>(out);
+  p.out_f32 = static_cast<float*>(out);
+  p.part = part;
+  p.counters = counters;
+  p.best = nullptr;
+  p.N = N;
+  p.K = K;
+  p.row_offset = 0;
+  p.eps = eps;
+  p.stages = sh.stages;
+  p.stage_tiles = sh.stage_tiles;
+  p.pre = sh.pre;
+  switch (kind) {
+    case QK_GEMV_QKV: return launch_gemv_scaled<PRO_RMSNORM_QUANT, EPI_STORE, 1>(scale_mode, p, sh, stream);
+    case QK_GEMV_O:
+    case QK_GEMV_DOWN: return launch_gemv_scaled<PRO_QUANT, EPI_RESIDUAL, 1>(scale_mode, p, sh, stream);
+    case QK_GEMV_GATE_UP: return launch_gemv_scaled<PRO_RMSNORM_QUANT, EPI_SWIGLU, 2>(scale_mode, p, sh, stream);
+    case QK_GEMV_PARTIAL: return launch_gemv_scaled<PRO_QUANT, EPI_F32, 1>(scale_mode, p, sh, stream);
+    case QK_GEMV_QKV_RESADD: return launch_gemv_scaled<PRO_RESADD_RMSNORM_QUANT, EPI_STORE, 1>(scale_mode, p, sh, stream);
+    case QK_GEMV_GATE_UP_RESADD: return launch_gemv_scaled<PRO_RESADD_RMSNORM_QUANT, EPI_SWIGLU, 2>(scale_mode, p, sh, stream);
+    default: return fail(QK_EINVAL, "unknown gemv kind %d", kind);
+  }
+}
+
+int qk_attention(const void* qkv, const void* q_norm_w, const void* k_norm_w, const void* cos_tab,
+                 const void* sin_tab, const int* state, void* k_cache, void* v_cache, float* o_part,
+                 float* ml_part, int* counters, void* out, int batch, int n_kv, int max_seq, int max_splits,
+                 int qkv_stride, int state_stride, float scale, float eps, int chunk, qk_stream_t stream) {
+  if (!qkv || !q_norm_w || !k_norm_w || !cos_tab || !sin_tab || !state || !k_cache || !v_cache || !o_part ||
+      !ml_part || !counters || !out)
+    return fail(QK_EINVAL, "null pointer argument");
+  if (batch < 1 || batch > 65535 || n_kv < 1 || n_kv > 64 || max_seq < 1) return fail(QK_EINVAL, "bad batch/n_kv/max_seq");
+  if (chunk != 32 && chunk != 64 && chunk != 128) return fail(QK_EINVAL, "chunk must be 32, 64 or 128, got %d", chunk);
+  if ((long long)max_splits * chunk < max_seq) return fail(QK_EINVAL, "o_part too small: max_splits*chunk < max_seq");
+  if (max_splits > 4096) return fail(QK_EINVAL, "max_splits %d > 4096", max_splits);
+  if (qkv_stride < n_kv * 6 * HEAD_DIM || state_stride < 1) return fail(QK_EINVAL, "bad qkv_stride/state_stride");
+  if (!aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(qkv, 16)) return fail(QK_EINVAL, "caches and qkv must be 16-byte aligned");
+  AttnParams p = {};
+  p.qkv = static_cast<const bf16*>(qkv);
+  p.q_norm_w = static_cast<const bf16*>(q_norm_w);
+  p.k_norm_w = static_cast<const bf16*>(k_norm_w);
+  p.cos_tab = static_cast<const bf16*>(cos_tab);
+  p.sin_tab = static_cast<const bf16*>(sin_tab);
+  p.state = state;
+  p.k_cache = static_cast<bf16*>(k_cache);
+  p.v_cache = static_cast<bf16*>(v_cache);
+  p.o_part = o_part;
+  p.ml_part = ml_part;
+  p.counters = counters;
+  p.out = static_cast<bf16*>(out);
+  p.max_seq = max_seq;
+  p.max_splits = max_splits;
+  p.qkv_stride = qkv_stride;
+  p.state_stride = state_stride;
+  p.scale = scale;
+  p.eps = eps;
+  const dim3 grid(n_kv, (max_seq + chunk - 1) / chunk, batch);
+  auto run = [&](auto kernel, size_t smem) -> int {
+    if (int r = ensure_smem((const void*)kernel, (int)smem)) return r;
+    return launch(kernel, grid, dim3(128), smem, stream, p);
+  };
+  switch (chunk) {
+    case 32: return run(attention_kernel<32>, attention_smem_bytes<32>(max_splits));
+    case 64: return run(attention_kernel<64>, attention_smem_bytes<64>(max_splits));
+    default: return run(attention_kernel<128>, attention_smem_bytes<128>(max_splits));
+  }
+}
+
+int qk_lm_head_argmax(const void* w, const float* w_scale, int head_fp8, const void* x, const void* norm_w,
+                      void* logits, unsigned long long* best, int V, int row_offset, float eps, float* part,
+                      int* counters, int ctas, qk_stream_t stream) {
+  if (!w || !x || !norm_w || !logits || !best) return fail(QK_EINVAL, "null pointer argument");
+  if (V <= 0 || V % 8) return fail(QK_EINVAL, "V=%d must be a positive multiple of 8", V);
+  if (!aligned(w, 16) || !aligned(x, 16) || !aligned(norm_w, 16) || !aligned(logits, 16))
+    return fail(QK_EINVAL, "tensor pointers must be 16-byte aligned");
+  const int sms = device_sms();
+  if (head_fp8) {
+    if (!w_scale || !part || !counters) return fail(QK_EINVAL, "fp8 head needs w_scale, part and counters");
+    GemvShape sh = gemv_defaults(4);
+    if (ctas > 0) sh.ctas = (ctas + sms - 1) / sms;
+    GemvParams p = {};
+    p.w = static_cast<const uint8_t*>(w);
+    p.ws = w_scale;
+    p.x = static_cast<const bf16*>(x);
+    p.norm_w = static_cast<const bf16*>(norm_w);
+    p.out = static_cast<bf16*>(logits);
+    p.part = part;
+    p.counters = counters;
+    p.best = best;
+    p.N = V;
+    p.K = HIDDEN;
+    p.row_offset = row_offset;
+    p.eps = eps;
+    p.stages = sh.stages;
+    p.stage_tiles = sh.stage_tiles;
+    p.pre = sh.pre;
+    return launch_gemv_scaled<PRO_RMSNORM_QUANT, EPI_ARGMAX, 1>(QK_SCALE_CHANNEL, p, sh, stream);
+  }
+  HeadParams p = {};
+  p.w = static_cast<const bf16*>(w);
+  p.x = static_cast<const bf16*>(x);
+  p.norm_w = static_cast<const bf16*>(norm_w);
+  p.logits = static_cast<bf16*>(logits);
+  p.best = best;
+  p.V = V;
+  p.row_offset = row_offset;
+  p.eps = eps;
+  p.stages = 3;
+  p.pre = 3;
+  const int smem = head_smem_total(p.stages);
+  if (int r = ensure_smem((const void*)lm_head_bf16_kernel, smem)) return r;
+  return launch(lm_head_bf16_kernel, dim3(ctas > 0 ? ctas : sms), dim3(HEAD_WARPS * 32), smem, stream, p);
+}
+
+int qk_embed(const int* token, const void* table, void* resid, int vocab, int batch, qk_stream_t stream) {
+  if (!token || !table || !resid || vocab <= 0 || batch < 1) return fail(QK_EINVAL, "bad embed arguments");
+  if (!aligned(table, 16) || !aligned(resid, 16)) return fail(QK_EINVAL, "table/resid must be 16-byte aligned");
+  return launch(embed_kernel, dim3(batch), dim3(HIDDEN / 8), 0, stream, token, static_cast<const bf16*>(table),
+                static_cast<bf16*>(resid), vocab);
+}
+
+int qk_finalize(unsigned long long* best, int* token, int* out_tokens, int* state, int out_len, int batch,
+                qk_stream_t stream) {
+  if (!best || !token || !out_tokens || !state || out_len < 1 || batch < 1) return fail(QK_EINVAL, "bad finalize arguments");
+  return launch(finalize_kernel, dim3(batch), dim3(1), 0, stream, best, token, out_tokens, state, out_len);
+}
+
+}  // extern "C"

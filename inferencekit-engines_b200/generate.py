@@ -1,0 +1,146 @@
+"""Batch-1 greedy decode engine on the B200 kernels: one CUDA graph per decode step.
+
+Mirrors the reference engine (qwen3-8b-fp8_rtx-5090/generate.py:39-197): device-resident step state
+`[pos, step]`, static activation buffers, `decode_step()` (the hot path, 183 launches), `capture()` into one
+CUDA graph, and `generate()`, which replays the graph without a host sync per token.
+
+Prompt processing: the reference runs a Triton prefill (outside this path's scope). Here a prompt is fed
+through the same decode graph one position at a time (teacher forcing), which writes the same KV rows a
+prefill would and leaves the first generated token in `token`; synthetic long-context setups instead fill
+the cache directly (`Qwen3FP8Decode.fill_cache_random`).
+"""
+from __future__ import annotations
+
+import torch
+
+from kernels import ops
+from model import Qwen3FP8Decode, Linear
+
+# Per-kind GEMV launch shape: ring stages per warp, warps per CTA, stages issued before the wait,
+# 1 KiB tiles per stage, CTAs per SM. Kinds: qkv, o_proj, gate_up, down, lm_head (fp8).
+DEFAULT_GEMV_SHAPE = {
+    0: dict(depth=4, warps=8, pre=4, stage_tiles=4, ctas=1),
+    1: dict(depth=4, warps=8, pre=4, stage_tiles=4, ctas=1),
+    2: dict(depth=4, warps=8, pre=4, stage_tiles=2, ctas=1),
+    3: dict(depth=4, warps=8, pre=4, stage_tiles=4, ctas=1),
+}
+
+
+class Engine:
+    def __init__(self, model: Qwen3FP8Decode, pdl: bool = True, attn_chunk: int = 64, lm_head_ctas: int = 0,
+                 gemv_shape: dict | None = None):
+        self.m = m = model
+        self.k = ops()
+        self.pdl = pdl
+        self.k.set_pdl(pdl)
+        cfg = m.cfg
+        dev = m.device
+        bf = dict(dtype=torch.bfloat16, device=dev)
+        self.max_seq = m.max_seq
+        self.token = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.state = torch.zeros(2, dtype=torch.int32, device=dev)        # [pos, step]
+        self.out_tokens = torch.zeros(m.max_seq, dtype=torch.int32, device=dev)
+        self.best = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.resid = torch.zeros(cfg.hidden, **bf)
+        self.qkv = torch.zeros((cfg.n_heads + 2 * cfg.n_kv_heads) * cfg.head_dim, **bf)
+        self.attn = torch.zeros(cfg.n_heads * cfg.head_dim, **bf)
+        self.h = torch.zeros(cfg.inter, **bf)
+        self.logits = torch.zeros(cfg.vocab, **bf)
+        self.max_splits = (m.max_seq + 31) // 32
+        self.o_part = torch.zeros(cfg.n_heads, self.max_splits, cfg.head_dim, dtype=torch.float32, device=dev)
+        self.ml_part = torch.zeros(cfg.n_heads, self.max_splits, 2, dtype=torch.float32, device=dev)
+        self.counters = torch.zeros(cfg.n_kv_heads, dtype=torch.int32, device=dev)
+        self.attn_chunk = attn_chunk
+        self.gemv_shape = {k: dict(v) for k, v in DEFAULT_GEMV_SHAPE.items()}
+        if gemv_shape:
+            for k, v in gemv_shape.items():
+                self.gemv_shape[k].update(v)
+        self.lm_head_ctas = lm_head_ctas
+        self.graph = None
+
+    def settings(self) -> dict:
+        return {"pdl": self.pdl, "decode_graph": True, "attn_chunk": self.attn_chunk, "gemv_shape": self.gemv_shape,
+                "lm_head_ctas": self.lm_head_ctas, "max_seq": self.max_seq, "scale_mode": self.m.scale_mode,
+                "head_dtype": self.m.head_dtype}
+
+    def _gemv(self, kind: int, lin: Linear, x, norm_w, out):
+        s = self.gemv_shape[kind]
+        self.k.fp8_gemv(kind, lin.packed, lin.scale, x, norm_w, out, lin.N, self.m.cfg.eps, s["depth"], s["warps"],
+                        s["pre"], -1, 1, stage_tiles=s["stage_tiles"], ctas_per_sm=s["ctas"])
+
+    # ------------------------------------------------------------------------------------------------------
+    def decode_step(self):
+        """Launch one decode step (eager). Also what gets captured into the graph."""
+        m, k, cfg = self.m, self.k, self.m.cfg
+        k.embed(self.token, m.embed, self.resid)
+        for li, L in enumerate(m.layers):
+            self._gemv(0, L.qkv, self.resid, L.ln1, self.qkv)
+            k.attention(self.qkv, L.q_norm, L.k_norm, m.cos, m.sin, self.state, m.k_cache[li], m.v_cache[li],
+                        self.o_part, self.ml_part, self.counters, self.attn, cfg.head_dim ** -0.5, cfg.eps, 0,
+                        self.attn_chunk)
+            self._gemv(1, L.o, self.attn, None, self.resid)
+            self._gemv(2, L.gu, self.resid, L.ln2, self.h)
+            self._gemv(3, L.down, self.h, None, self.resid)
+        if isinstance(m.lm_head, Linear):
+            k.lm_head_argmax(m.lm_head.packed, self.resid, m.norm, self.logits, self.best, cfg.eps,
+                             self.lm_head_ctas, w_scale=m.lm_head.scale)
+        else:
+            k.lm_head_argmax(m.lm_head, self.resid, m.norm, self.logits, self.best, cfg.eps, self.lm_head_ctas)
+        k.finalize(self.best, self.token, self.out_tokens, self.state)
+
+    def capture(self):
+        """Record one decode step into a CUDA graph (needs a valid state). The warm-up steps rewrite the KV
+        slot at the current position with identical values, so only token and state are restored."""
+        token, state = self.token.clone(), self.state.clone()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                self.token.copy_(token)
+                self.state.copy_(state)
+                self.decode_step()
+        torch.cuda.current_stream().wait_stream(s)
+        self.token.copy_(token)
+        self.state.copy_(state)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.decode_step()
+        torch.cuda.synchronize()
+
+    def step(self, n: int = 1, use_graph: bool = True):
+        for _ in range(n):
+            if use_graph:
+                self.graph.replay()
+            else:
+                self.decode_step()
+
+    # ------------------------------------------------------------------------------------------------------
+    @torch.no_grad()
+    def prefill(self, prompt_ids, use_graph: bool = True) -> torch.Tensor:
+        """Feed the prompt through the decode step at positions 0..P-1. Leaves state = [P, 0] and the first
+        generated token in `token`; returns it as a device tensor (no host sync)."""
+        ids = torch.as_tensor(prompt_ids, dtype=torch.int32, device=self.m.device)
+        P = ids.numel()
+        assert 0 < P < self.max_seq
+        self.state.zero_()
+        self.best.zero_()
+        self.token.copy_(ids[:1])
+        if use_graph and self.graph is None:
+            self.capture()
+        for i in range(P):
+            if i:
+                self.token.copy_(ids[i:i + 1])
+            self.step(1, use_graph)
+        self.state[1].fill_(0)
+        return self.token.clone()
+
+    @torch.no_grad()
+    def generate(self, prompt_ids, gen_len: int, use_graph: bool = True):
+        """Greedy generation of exactly gen_len tokens (no early stop). Returns a list of ids."""
+        assert len(prompt_ids) + gen_len <= self.max_seq
+        first = self.prefill(prompt_ids, use_graph)
+        if gen_len > 1:
+            self.step(gen_len - 1, use_graph)
+        out = [int(first.item())]
+        out += self.out_tokens[: gen_len - 1].tolist()
+        return out

@@ -1,0 +1,171 @@
+"""Loads the B200 decode kernels (C ABI, libqwen3_b200.so) and exposes them under the reference's op names.
+
+Drop-in for the reference's `kernels.ops()` (qwen3-8b-fp8_rtx-5090/kernels/__init__.py:11-24), whose pybind11
+module exports fp8_gemv, attention, lm_head_argmax, embed, finalize, set_pdl and set_timeline
+(kernels/decode.cu:822-830). The methods below take the same positional arguments in the same order and
+launch on torch's current CUDA stream without a host sync, so `Engine.decode_step` can be captured into a
+CUDA graph exactly as before. There is no fallback: if the library is missing or the device is not an
+sm_100 GPU, `ops()` raises.
+
+Differences a caller must know:
+  * FP8 weights must be in `model.pack_fp8` layout (the B200 kernels' tile order). The reference's
+    `kmajor` argument is accepted and ignored; `depth` maps to ring stages per warp, `warps` to warps per
+    CTA, `pre` to ring stages issued before waiting on the previous kernel; `trig` is accepted and ignored
+    (every kernel lets its successor launch right after its own wait).
+  * Scales may be 128x128 blocks [N/128, K/128] or per output channel [N]; the layout is read off the
+    tensor's shape.
+  * `lm_head_argmax` also takes an FP8 head: pass `w_scale=` (fp32 [V]) with packed fp8 weights.
+  * The split-K scratch of the GEMV is owned by this object (allocated on first use per device, before any
+    graph capture when the engine warms up eagerly).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import torch
+
+_here = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_here, "libqwen3_b200.so")
+
+GEMV_QKV, GEMV_O, GEMV_GATE_UP, GEMV_DOWN = 0, 1, 2, 3
+GEMV_PARTIAL, GEMV_QKV_RESADD, GEMV_GATE_UP_RESADD = 5, 6, 7
+SCALE_BLOCK128, SCALE_CHANNEL = 0, 1
+
+_VP, _I, _F = ctypes.c_void_p, ctypes.c_int, ctypes.c_float
+_SIGS = {
+    "qk_version": ([], _I),
+    "qk_last_error": ([], ctypes.c_char_p),
+    "qk_set_pdl": ([_I], _I),
+    "qk_set_timeline": ([_VP], _I),
+    "qk_get_device_error": ([ctypes.POINTER(_I), _VP], _I),
+    "qk_fp8_gemv": ([_I, _VP, _VP, _I, _VP, _VP, _VP, _VP, _VP, _I, _I, _F, _VP, _VP, _I, _I, _I, _I, _I, _VP], _I),
+    "qk_attention": ([_VP] * 12 + [_I, _I, _I, _I, _I, _I, _F, _F, _I, _VP], _I),
+    "qk_lm_head_argmax": ([_VP, _VP, _I, _VP, _VP, _VP, _VP, _I, _I, _F, _VP, _VP, _I, _VP], _I),
+    "qk_embed": ([_VP, _VP, _VP, _I, _I, _VP], _I),
+    "qk_finalize": ([_VP, _VP, _VP, _VP, _I, _I, _VP], _I),
+}
+
+
+def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
+    if not os.path.exists(path):
+        raise RuntimeError(f"{path} is missing: build it with `make -C {os.path.dirname(_here)}` "
+                           "(or __graft_entry__.build())")
+    lib = ctypes.CDLL(path)
+    for name, (args, res) in _SIGS.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = res
+    return lib
+
+
+def _p(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+class DecodeOps:
+    """The reference's op set over the C ABI (see module docstring)."""
+
+    def __init__(self, lib: ctypes.CDLL):
+        self.lib = lib
+        self._scratch = {}
+
+    # ---- helpers ------------------------------------------------------------------------------------------
+    def _check(self, status: int, what: str):
+        if status != 0:
+            raise RuntimeError(f"{what}: {self.lib.qk_last_error().decode()}")
+
+    def scratch(self, device: torch.device, part_floats: int, units: int):
+        """Split-K scratch for the GEMV on `device` (grown, never shrunk; counters start at zero)."""
+        key = device.index if device.index is not None else torch.cuda.current_device()
+        part, counters = self._scratch.get(key, (None, None))
+        if part is None or part.numel() < part_floats or counters.numel() < units:
+            n_part = max(part_floats, 0 if part is None else part.numel())
+            n_cnt = max(units, 0 if counters is None else counters.numel())
+            part = torch.empty(n_part, dtype=torch.float32, device=device)
+            counters = torch.zeros(n_cnt, dtype=torch.int32, device=device)
+            self._scratch[key] = (part, counters)
+        return part, counters
+
+    def device_error(self) -> int:
+        """Read and clear the device error word (bounded waits that gave up, bad state)."""
+        v = ctypes.c_int(0)
+        self._check(self.lib.qk_get_device_error(ctypes.byref(v), _stream()), "qk_get_device_error")
+        return v.value
+
+    # ---- the reference's ops -----------------------------------------------------------------------------
+    def set_pdl(self, on: bool):
+        self._check(self.lib.qk_set_pdl(int(bool(on))), "set_pdl")
+
+    def set_timeline(self, buf=None):
+        self._check(self.lib.qk_set_timeline(_p(buf)), "set_timeline")
+
+    def fp8_gemv(self, kind, w, ws, x, norm_w, out, N, eps, depth=0, warps=0, pre=-1, trig=-1, kmajor=1,
+                 resadd=None, resid_out=None, stage_tiles=0, ctas_per_sm=0):
+        N = int(N)
+        K = w.numel() // N
+        scale_mode = SCALE_CHANNEL if ws.dim() == 1 else SCALE_BLOCK128
+        part, counters = self.scratch(w.device, N * K // 128, N // 8)
+        st = self.lib.qk_fp8_gemv(int(kind), _p(w), _p(ws), scale_mode, _p(x), _p(norm_w), _p(resadd),
+                                  _p(resid_out), _p(out), N, K, float(eps), _p(part), _p(counters),
+                                  int(warps), int(depth), int(stage_tiles), int(pre), int(ctas_per_sm), _stream())
+        self._check(st, "fp8_gemv")
+
+    def attention(self, qkv, q_norm_w, k_norm_w, cos_tab, sin_tab, state, k_cache, v_cache, o_part, ml_part,
+                  counters, out, scale, eps, late_trigger=0, chunk=64, batch=None, state_stride=2):
+        """k_cache/v_cache: one layer, [n_kv, max_seq, 128] (batch 1, as the reference) or
+        [batch, n_kv, max_seq, 128]."""
+        if k_cache.dim() == 3:
+            b, n_kv, max_seq = 1, k_cache.shape[0], k_cache.shape[1]
+        else:
+            b, n_kv, max_seq = k_cache.shape[0], k_cache.shape[1], k_cache.shape[2]
+        if batch is not None:
+            b = batch
+        max_splits = o_part.shape[-2]
+        qkv_stride = qkv.shape[-1] if qkv.dim() > 1 else qkv.numel()
+        st = self.lib.qk_attention(_p(qkv), _p(q_norm_w), _p(k_norm_w), _p(cos_tab), _p(sin_tab), _p(state),
+                                   _p(k_cache), _p(v_cache), _p(o_part), _p(ml_part), _p(counters), _p(out),
+                                   b, n_kv, max_seq, max_splits, qkv_stride, int(state_stride), float(scale),
+                                   float(eps), int(chunk), _stream())
+        self._check(st, "attention")
+
+    def lm_head_argmax(self, w, x, norm_w, logits, best, eps, ctas=0, w_scale=None, row_offset=0):
+        V = logits.numel()
+        fp8 = w_scale is not None
+        part = counters = None
+        if fp8:
+            part, counters = self.scratch(w.device, V * 4096 // 128, V // 8)
+        st = self.lib.qk_lm_head_argmax(_p(w), _p(w_scale), int(fp8), _p(x), _p(norm_w), _p(logits), _p(best), V,
+                                        int(row_offset), float(eps), _p(part), _p(counters), int(ctas), _stream())
+        self._check(st, "lm_head_argmax")
+
+    def embed(self, token, table, resid):
+        b = token.numel()
+        self._check(self.lib.qk_embed(_p(token), _p(table), _p(resid), table.shape[0], b, _stream()), "embed")
+
+    def finalize(self, best, token, out_tokens, state):
+        b = token.numel()
+        out_len = out_tokens.shape[-1]
+        self._check(self.lib.qk_finalize(_p(best), _p(token), _p(out_tokens), _p(state), out_len, b, _stream()),
+                    "finalize")
+
+
+_ops = None
+
+
+def ops() -> DecodeOps:
+    """The decode ops (loads libqwen3_b200.so once). Raises if the library or an sm_100 GPU is missing."""
+    global _ops
+    if _ops is None:
+        lib = load_library()
+        if not torch.cuda.is_available():
+            raise RuntimeError("the B200 decode kernels need a CUDA device")
+        major, minor = torch.cuda.get_device_capability()
+        if (major, minor) != (10, 0):
+            raise RuntimeError(f"libqwen3_b200.so is built for sm_100a; this device is sm_{major}{minor}")
+        _ops = DecodeOps(lib)
+    return _ops

@@ -1,0 +1,69 @@
+"""The C-ABI library (CPU-only checks): it loads, exports every entry point include/qwen3_b200.h declares, and
+rejects bad arguments with QK_EINVAL and a message before touching the GPU."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import REPO
+
+HEADER = os.path.join(REPO, "include", "qwen3_b200.h")
+
+
+def declared():
+    src = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:int|const char\*)\s+(qk_\w+)\s*\(", src, re.M)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from kernels import load_library, LIB_PATH
+    if not os.path.exists(LIB_PATH):
+        pytest.skip("library not built (run __graft_entry__.build())")
+    return load_library()
+
+
+def test_header_declares_the_reference_ops():
+    names = declared()
+    for n in ("qk_fp8_gemv", "qk_attention", "qk_lm_head_argmax", "qk_embed", "qk_finalize", "qk_set_pdl",
+              "qk_set_timeline"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol(lib):
+    missing = [n for n in declared() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_version_and_pdl_switch(lib):
+    assert lib.qk_version() >= 100
+    assert lib.qk_set_pdl(1) == 0 and lib.qk_set_pdl(0) == 0
+
+
+def test_bad_arguments_are_rejected_without_a_gpu(lib):
+    # null weights
+    st = lib.qk_fp8_gemv(0, None, None, 1, None, None, None, None, None, 6144, 4096, 1e-6, None, None,
+                         0, 0, 0, -1, 0, None)
+    assert st == 1 and b"null" in lib.qk_last_error()
+    # bad attention chunk
+    p = ctypes.c_void_p(16)
+    st = lib.qk_attention(p, p, p, p, p, p, p, p, p, p, p, p, 1, 8, 4096, 128, 6144, 2, 0.088, 1e-6, 48, None)
+    assert st == 1 and b"chunk" in lib.qk_last_error()
+    # o_part too small for the context
+    st = lib.qk_attention(p, p, p, p, p, p, p, p, p, p, p, p, 1, 8, 4096, 16, 6144, 2, 0.088, 1e-6, 64, None)
+    assert st == 1 and b"max_splits" in lib.qk_last_error()
+    # K not a multiple of 128
+    st = lib.qk_fp8_gemv(1, p, p, 1, p, None, None, None, p, 4096, 100, 1e-6, p, p, 0, 0, 0, -1, 0, None)
+    assert st == 1 and b"K=100" in lib.qk_last_error()
+    # timeline stamps are not built: a non-null buffer is refused, null accepted
+    assert lib.qk_set_timeline(p) == 1 and lib.qk_set_timeline(None) == 0
+
+
+def test_ops_refuses_to_run_without_cuda():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("has a GPU")
+    import kernels
+    with pytest.raises(RuntimeError):
+        kernels.ops()
