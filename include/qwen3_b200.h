@@ -15,7 +15,7 @@
  *   - Return value: QK_OK, or an error code with a message from qk_last_error() (thread-local). Bad
  *     arguments are rejected before anything is launched.
  *   - bf16 tensors are passed as void* (__nv_bfloat16 in device code); fp8 weights are e4m3 bytes in the
- *     packed layout of model.pack_fp8 (1 KiB tiles in mma fragment order).
+ *     packed layout of model.pack_fp8 (2 KiB tiles of 16 rows x 128 k in MMA fragment order).
  *   - Process-global state, as in the reference: the PDL switch (qk_set_pdl). Not thread-safe to change
  *     while another thread launches.
  */
@@ -72,9 +72,10 @@ int qk_get_device_error(int* err, qk_stream_t stream);
  *   resadd     fp32 [K] sums added to the residual (kinds 6, 7), else NULL
  *   resid_out  bf16 [K] destination of the updated residual (kinds 6, 7; may equal x), else NULL
  *   out        bf16 output: [N] (0, 6), residual [N] in place (1, 3), [N/2] (2, 7); fp32 [N] for kind 5
- *   part       fp32 scratch of N*K/128 floats; counters: int scratch of N/8 ints, zeroed once
+ *   part       fp32 scratch of N*K/128 floats; counters: int scratch of N/16 ints, zeroed once
  *   warps/stages/stage_tiles/pre/ctas_per_sm: launch shape (0 = default). pre = ring stages issued
- *              before waiting on the previous kernel; stage_tiles = 1 KiB tiles per ring stage.
+ *              before waiting on the previous kernel; stage_tiles = tiles per ring stage (a tile is
+ *              16 rows x 128 k = 2 KiB; 4 KiB for the gate|up kinds 2/7).
  */
 int qk_fp8_gemv(int kind, const void* w, const float* w_scale, int scale_mode, const void* x, const void* norm_w,
                 const float* resadd, void* resid_out, void* out, int N, int K, float eps, float* part, int* counters,

@@ -131,14 +131,36 @@ __device__ __forceinline__ uint4 ldg_stream(const void* p) {
 }
 
 // ---- FP8 arithmetic ----------------------------------------------------------------------------------------
-// Tensor-core D[16x8] += A[16x32] * B[32x8] on e4m3 operands, fp32 accumulate. Used as a dot-product engine:
-// every row of A is the quantized activation vector, the 8 columns of B are 8 weight rows.
-__device__ __forceinline__ void mma_e4m3(float (&d)[4], uint32_t a_lo, uint32_t a_hi, uint32_t b0, uint32_t b1) {
+// Two e4m3 values (low byte -> low half) to an f16x2 register; exact (every e4m3 value is an f16 value).
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t two_bytes) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"((uint16_t)two_bytes));
+  return r;
+}
+
+// Tensor-core D[16x8] += A[16x16] * B[16x8], f16 operands, fp32 accumulate (legacy warp-level mma).
+__device__ __forceinline__ void hmma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
   asm volatile(
-      "mma.sync.aligned.m16n8k32.row.col.f32.e4m3.e4m3.f32 "
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
       "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a_lo), "r"(a_lo), "r"(a_hi), "r"(a_hi), "r"(b0), "r"(b1));
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// One 32-wide K chunk of an fp8 dot for two weight rows (r and r+8 of a 16-row unit), x in every B column.
+// w4 = this lane's 16 weight bytes of the chunk: {row r: k 4t..4t+3, row r+8: k 4t.., row r: k 16+4t..,
+// row r+8: k 16+4t..}; xb = the matching x fragments as f16x2 {x(4t,4t+1), x(16+4t,+1), x(4t+2,+3),
+// x(16+4t+2,+3)}. Returns the chunk dots of rows r (e[0]) and r+8 (e[2]).
+// Operand placement and chaining: the pairs (4t,4t+1) and (16+4t,16+4t+1) go through one k16 MMA from zero,
+// the pairs (4t+2,4t+3) and (16+4t+2,..) through a second one accumulating onto it. This is bit-identical to
+// sm_100's `mma.sync.m16n8k32 ... e4m3.e4m3` (verified on 131k random chunks, both operand orientations),
+// which the reference decode kernel uses as its dot engine, while costing only the 8 weight conversions.
+__device__ __forceinline__ void fp8_chunk_dot(const uint4 w4, const uint4 xb, float (&e)[4]) {
+  e[0] = e[1] = e[2] = e[3] = 0.f;
+  hmma16816(e, e4m3x2_to_f16x2(w4.x), e4m3x2_to_f16x2(w4.y), e4m3x2_to_f16x2(w4.z), e4m3x2_to_f16x2(w4.w), xb.x, xb.y);
+  hmma16816(e, e4m3x2_to_f16x2(w4.x >> 16), e4m3x2_to_f16x2(w4.y >> 16), e4m3x2_to_f16x2(w4.z >> 16),
+            e4m3x2_to_f16x2(w4.w >> 16), xb.z, xb.w);
 }
 
 // The reference quantizer divides with the approximate `div.full.f32` (what Triton emits for fp32 `/`).

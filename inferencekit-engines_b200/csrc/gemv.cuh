@@ -1,24 +1,23 @@
 // FP8 W8A8 GEMV for the batch-1 decode step: y[N] = W[N, K] . quant(x[K]), block- or channel-scaled.
 //
 // Design (B200):
-//  * Work split. The weights are a stream of 1 KiB tiles ordered [unit][kb] (unit = 8 output rows, or
-//    8 gate + 8 up rows for SwiGLU; kb = 128-wide K block), see model.pack_fp8. Every warp of the grid
-//    takes an equal, contiguous range of that stream, so each SM reads the same number of bytes
-//    whatever N is (no 8-row granularity loss across 148 SMs).
+//  * Work split. The weights are a stream of tiles ordered [unit][kb] (unit = 16 output rows, or 16 gate
+//    + 16 up rows for SwiGLU; kb = 128-wide K block; a tile is 2 KiB per 16 rows), see model.pack_fp8.
+//    Every warp of the grid takes an equal, contiguous range of that stream, so each SM reads the same
+//    number of bytes whatever N is.
 //  * Data movement. Each warp runs its own shared-memory ring: lane 0 issues bulk async copies
-//    (cp.async.bulk, L2 evict-first) of `stage_tiles` tiles per stage and the warp waits on the
-//    stage's mbarrier. Copies for the first `pre` stages are issued before griddepcontrol.wait, so under
-//    programmatic dependent launch a kernel streams its weights while the previous kernel finishes.
-//  * Math. The activation is RMS-normalised (optional) and quantized to e4m3 per 128-group in the
-//    prologue, into shared memory, in mma fragment order. Per tile, a lane reads two 16-byte words of
-//    weights and issues four mma.m16n8k32 e4m3 (one per 32-wide K chunk) with the activation in every
-//    A row: the tensor core is the dot-product engine, fp8 bytes never pass through a conversion.
+//    (cp.async.bulk, L2 evict-first) of `stage_tiles` tiles per stage and the warp waits on the stage's
+//    mbarrier. The first `pre` stages are requested before griddepcontrol.wait, so under programmatic
+//    dependent launch a kernel streams its weights while the previous kernel finishes.
+//  * Math. The prologue RMS-normalises x (optional), quantizes it to e4m3 per 128-group exactly as the
+//    reference, and stores it as f16 MMA fragments in shared memory. Per 32-wide K chunk a lane reads 16
+//    weight bytes (rows r and r+8 of the unit), converts them to f16 and issues two m16n8k16 MMAs with the
+//    weights as the A operand (see fp8_chunk_dot): 16 rows x 32 k per two MMAs and 8 conversions.
 //    Per K block: acc += d * s_x * s_w (fp32), in K order.
-//  * Exactness. The per-block dot comes from the same mma instruction with the same operand placement
-//    and chaining as the reference decode kernel, and the block terms are added in the same order, so
-//    outputs are bit-identical to it. A unit whose K range is split between two warps stores its raw
-//    block dots in `part`; the warp that completes the unit (atomic counter, last-arriver) replays the
-//    same in-order accumulation from them, so splitting K changes no bit.
+//  * Exactness. The chunk dot is bit-identical to the reference decode kernel's fp8 mma, the chunks and
+//    blocks are accumulated in the same order, so outputs are bit-identical to it. A unit whose K range is
+//    split between two warps stores its raw block dots in `part`; the warp that completes the unit
+//    (atomic counter, last-arriver) replays the same in-order accumulation, so splitting changes no bit.
 //  * Epilogues: bf16 store (qkv), residual add in place (o_proj, down), SwiGLU (gate_up), logits +
 //    greedy argmax (lm_head), fp32 partial store (tensor-parallel row shards).
 #pragma once
@@ -29,6 +28,8 @@ namespace qk {
 enum { PRO_QUANT = 0, PRO_RMSNORM_QUANT = 1, PRO_RESADD_RMSNORM_QUANT = 2 };
 enum { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_SWIGLU = 2, EPI_ARGMAX = 3, EPI_F32 = 4 };
 enum { SCALE_BLOCK = 0, SCALE_CHANNEL = 1 };
+constexpr int GEMV_UNIT_ROWS = 16;
+constexpr int GEMV_TILE_BYTES = GEMV_UNIT_ROWS * QB;   // 2 KiB per 16 rows x 128 k
 
 struct GemvParams {
   const uint8_t* w;          // packed fp8 tiles (model.pack_fp8)
@@ -39,7 +40,7 @@ struct GemvParams {
   bf16* resid_out;           // RESADD: the updated residual (each CTA writes a slice)
   bf16* out;                 // STORE [N] | RESIDUAL [N] in place | SWIGLU [N/2] | ARGMAX logits [N]
   float* out_f32;            // F32 [N]
-  float* part;               // split-K block dots [units][KB][8*NG]
+  float* part;               // split-K block dots [units][KB][16*NG]
   int* counters;             // [units], zero between launches (the kernel leaves them zero)
   unsigned long long* best;  // ARGMAX: packed (value, index) key, zero before the launch
   int N, K;
@@ -50,14 +51,14 @@ struct GemvParams {
 
 // Shared-memory carve-up, computed identically on host and device.
 struct GemvSmem {
-  int xs, xfrag, xscale, red, bestbuf, bars, ring, total;
+  int xs, xh, xscale, red, bestbuf, bars, ring, total;
 };
 __host__ __device__ inline int align_up(int v, int a) { return (v + a - 1) / a * a; }
 __host__ __device__ inline GemvSmem gemv_smem(int K, int warps, int stages, int stage_bytes) {
   GemvSmem L;
   L.xs = 0;                                      // raw bf16 input, K*2
-  L.xfrag = align_up(L.xs + K * 2, 128);         // quantized input in fragment order, K bytes
-  L.xscale = align_up(L.xfrag + K, 16);          // K/128 floats
+  L.xh = align_up(L.xs + K * 2, 128);            // quantized input as f16 MMA fragments, K*2
+  L.xscale = align_up(L.xh + K * 2, 16);         // K/128 floats
   L.red = align_up(L.xscale + (K / QB) * 4, 16); // 32 floats
   L.bestbuf = L.red + 32 * 4;                    // 32 u64
   L.bars = align_up(L.bestbuf + 32 * 8, 16);     // warps*stages mbarriers
@@ -66,9 +67,10 @@ __host__ __device__ inline GemvSmem gemv_smem(int K, int warps, int stages, int 
   return L;
 }
 
-// ---- prologue: x -> (residual add) -> (RMSNorm) -> e4m3 per 128-group, in shared memory -----------------
-// Fragment order: word (kb*4 + t)*8 + 2c + hi holds x[kb*128 + 32c + 16hi + 4t .. +3], so lane (g, t) gets
-// the A fragments of the four 32-wide chunks of block kb with two 16-byte loads.
+// ---- prologue: x -> (residual add) -> (RMSNorm) -> e4m3 per 128-group -> f16 fragments in shared memory -----
+// Fragment order: 16 bytes at ((kb*4 + c)*4 + t)*16 hold x(32c + 4t, +1), x(32c + 16 + 4t, +1),
+// x(32c + 4t + 2, +3), x(32c + 16 + 4t + 2, +3) of block kb as f16x2: the B operands of the two MMAs of
+// chunk c for every lane with that t.
 template <int PRO>
 __device__ __forceinline__ void gemv_prologue(const GemvParams& p, uint8_t* smem, const GemvSmem& L) {
   const int K = p.K, KB = K / QB;
@@ -117,7 +119,7 @@ __device__ __forceinline__ void gemv_prologue(const GemvParams& p, uint8_t* smem
     for (int i = 0; i < 4; ++i) tot += red[i];
     rstd = rsqrtf(tot / (float)K + p.eps);
   }
-  uint32_t* xf = reinterpret_cast<uint32_t*>(smem + L.xfrag);
+  uint32_t* xh = reinterpret_cast<uint32_t*>(smem + L.xh);
   float* xsc = reinterpret_cast<float*>(smem + L.xscale);
   const int c = lane >> 3, hi = (lane >> 2) & 1, t = lane & 3;
   for (int g = warp; g < KB; g += warps) {
@@ -137,7 +139,10 @@ __device__ __forceinline__ void gemv_prologue(const GemvParams& p, uint8_t* smem
     float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
     amax = warp_max(amax);
     const float sc = div_full(amax, 448.0f);
-    xf[(g * 4 + t) * 8 + c * 2 + hi] = quant4(v[0], v[1], v[2], v[3], sc);
+    const uint32_t q = quant4(v[0], v[1], v[2], v[3], sc);   // x(32c + 16hi + 4t + 0..3)
+    uint32_t* dst = xh + ((g * 4 + c) * 4 + t) * 4;
+    dst[hi] = e4m3x2_to_f16x2(q);
+    dst[2 + hi] = e4m3x2_to_f16x2(q >> 16);
     if (lane == 0) xsc[g] = sc;
   }
   __syncthreads();
@@ -147,10 +152,11 @@ __device__ __forceinline__ void gemv_prologue(const GemvParams& p, uint8_t* smem
 template <int PRO, int EPI, int SCALE, int NG>
 __global__ void __launch_bounds__(512) fp8_gemv_kernel(const __grid_constant__ GemvParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
-  constexpr int UB = 1024 * NG;                  // bytes per tile
-  constexpr int RPU = 8 * NG;                    // rows per unit
+  constexpr int UB = GEMV_TILE_BYTES * NG;       // bytes per tile
+  constexpr int RPU = GEMV_UNIT_ROWS * NG;       // rows per unit
   const int K = p.K, KB = K / QB, N = p.N;
-  const int warps = blockDim.x >> 5, lane = threadIdx.x & 31, warp = threadIdx.x >> 5, t = lane & 3;
+  const int warps = blockDim.x >> 5, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = lane >> 2, t = lane & 3;
   const int S = p.stages, ST = p.stage_tiles;
   const GemvSmem L = gemv_smem(K, warps, S, ST * UB);
   const int units = N / RPU;
@@ -182,93 +188,87 @@ __global__ void __launch_bounds__(512) fp8_gemv_kernel(const __grid_constant__ G
     for (int ch = min(p.pre, first); ch < first; ++ch) issue(ch);
 
   gemv_prologue<PRO>(p, smem, L);
-  const uint32_t* xf = reinterpret_cast<const uint32_t*>(smem + L.xfrag);
+  const uint8_t* xh = smem + L.xh;
   const float* xsc = reinterpret_cast<const float*>(smem + L.xscale);
 
-  float acc[NG][2];
-  float swc[NG][2];   // channel scales of rows 2t, 2t+1
+  float acc[NG][2];   // rows r = g and r = g + 8 of each 16-row sub-unit
+  float swc[NG][2];   // channel scales of those rows
   float swb[NG][3];   // block scales of the unit's row block: lane l holds kb = l, l+32, l+64
   bool full = false;
-  int cur_u = -1;
   float best_v = -INFINITY;
   int best_i = 0x7FFFFFFF;
 
-  auto row0 = [&](int u, int gi) { return (NG == 2 && gi == 1) ? N / 2 + u * 8 : u * 8; };
+  auto row0 = [&](int u, int gi) { return (NG == 2 && gi == 1) ? N / 2 + u * 16 : u * 16; };
   auto block_scale = [&](int gi, int kb) {   // warp-uniform kb; all lanes must call
     const float v = kb < 32 ? swb[gi][0] : (kb < 64 ? swb[gi][1] : swb[gi][2]);
     return __shfl_sync(0xffffffffu, v, kb & 31);
   };
-  auto epilogue = [&](int u) {
-    if (EPI == EPI_ARGMAX) {
+  auto begin_unit = [&](int u) {
+    full = (u * KB >= t0) && ((u + 1) * KB <= t1);
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const float lv = bf16r(acc[0][j]);
-        const int idx = p.row_offset + u * 8 + 2 * t + j;
-        if (lane < 4 && (lv > best_v || (lv == best_v && idx < best_i))) { best_v = lv; best_i = idx; }
+    for (int gi = 0; gi < NG; ++gi) {
+      acc[gi][0] = acc[gi][1] = 0.f;
+      if (SCALE == SCALE_CHANNEL) {
+        swc[gi][0] = __ldg(p.ws + row0(u, gi) + g);
+        swc[gi][1] = __ldg(p.ws + row0(u, gi) + g + 8);
+      } else {
+        const float* srow = p.ws + (size_t)(row0(u, gi) / QB) * KB;
+#pragma unroll
+        for (int i = 0; i < 3; ++i) swb[gi][i] = (lane + 32 * i < KB) ? __ldg(srow + lane + 32 * i) : 0.f;
       }
     }
-    if (lane >= 4) return;
-    const int n2 = u * 4 + t;   // bf16x2 index of rows (u*8 + 2t, +1)
-    if (EPI == EPI_STORE || EPI == EPI_ARGMAX) {
-      reinterpret_cast<__nv_bfloat162*>(p.out)[n2] = __floats2bfloat162_rn(acc[0][0], acc[0][1]);
-    } else if (EPI == EPI_RESIDUAL) {
-      const __nv_bfloat162 r = reinterpret_cast<const __nv_bfloat162*>(p.out)[n2];
-      const float y0 = bf16r(acc[0][0]), y1 = bf16r(acc[0][1]);
-      reinterpret_cast<__nv_bfloat162*>(p.out)[n2] = __floats2bfloat162_rn(__low2float(r) + y0, __high2float(r) + y1);
-    } else if (EPI == EPI_SWIGLU) {
-      float h[2];
+  };
+  auto epilogue = [&](int u) {   // lanes with t == 0 own rows u*16 + g and + 8
+    if (t != 0) return;
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
+    for (int j = 0; j < 2; ++j) {
+      const int n = u * 16 + g + 8 * j;
+      if (EPI == EPI_STORE) {
+        p.out[n] = __float2bfloat16_rn(acc[0][j]);
+      } else if (EPI == EPI_ARGMAX) {
+        p.out[n] = __float2bfloat16_rn(acc[0][j]);
+        const float lv = bf16r(acc[0][j]);
+        const int idx = p.row_offset + n;
+        if (lv > best_v || (lv == best_v && idx < best_i)) { best_v = lv; best_i = idx; }
+      } else if (EPI == EPI_RESIDUAL) {
+        p.out[n] = __float2bfloat16_rn(__bfloat162float(p.out[n]) + bf16r(acc[0][j]));
+      } else if (EPI == EPI_SWIGLU) {
         const float gt = bf16r(acc[0][j]);
         const float up = bf16r(acc[NG - 1][j]);
         const float act = bf16r(gt / (1.0f + expf(-gt)));
-        h[j] = act * up;
+        p.out[n] = __float2bfloat16_rn(act * up);
+      } else {  // EPI_F32
+        p.out_f32[n] = acc[0][j];
       }
-      reinterpret_cast<__nv_bfloat162*>(p.out)[n2] = __floats2bfloat162_rn(h[0], h[1]);
-    } else {  // EPI_F32
-      reinterpret_cast<float2*>(p.out_f32)[n2] = make_float2(acc[0][0], acc[0][1]);
     }
   };
 
+  int tt = t0, u = t0 / KB, kb = t0 - (t0 / KB) * KB;
+  if (t0 < t1) begin_unit(u);
   int ch = 0;
   bool ok = true;
   for (; ch < nchunks; ++ch) {
     const int s = ch % S;
     if (!__all_sync(0xffffffffu, mbar_wait(&bar[s], (uint32_t)((ch / S) & 1)))) { ok = false; break; }
     const uint8_t* buf = ring + (size_t)s * ST * UB;
-    const int ta = t0 + ch * ST, tb = min(ta + ST, t1);
-    for (int tt = ta; tt < tb; ++tt) {
-      const int u = tt / KB, kb = tt - u * KB;
-      if (u != cur_u) {
-        cur_u = u;
-        full = (u * KB >= t0) && ((u + 1) * KB <= t1);
+    const int n_here = min(ST, t1 - tt);
+    for (int i = 0; i < n_here; ++i, ++tt) {
+      const uint8_t* tile = buf + (size_t)i * UB;
+      const uint8_t* xk = xh + kb * 256 + t * 16;
+      float dk[NG][2];
+#pragma unroll
+      for (int gi = 0; gi < NG; ++gi) dk[gi][0] = dk[gi][1] = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const uint4 xb = lds128(xk + c * 64);
 #pragma unroll
         for (int gi = 0; gi < NG; ++gi) {
-          acc[gi][0] = acc[gi][1] = 0.f;
-          if (SCALE == SCALE_CHANNEL) {
-            const float2 sv = *reinterpret_cast<const float2*>(p.ws + row0(u, gi) + 2 * t);
-            swc[gi][0] = sv.x;
-            swc[gi][1] = sv.y;
-          } else {
-            const float* srow = p.ws + (size_t)(row0(u, gi) / QB) * KB;
-#pragma unroll
-            for (int i = 0; i < 3; ++i) swb[gi][i] = (lane + 32 * i < KB) ? __ldg(srow + lane + 32 * i) : 0.f;
-          }
+          const uint4 w4 = lds128(tile + gi * GEMV_TILE_BYTES + c * 512 + lane * 16);
+          float e[4];
+          fp8_chunk_dot(w4, xb, e);
+          dk[gi][0] += e[0];
+          dk[gi][1] += e[2];
         }
-      }
-      const uint8_t* tile = buf + (size_t)(tt - ta) * UB;
-      const uint4 xa = lds128(xf + (kb * 4 + t) * 8);
-      const uint4 xb = lds128(xf + (kb * 4 + t) * 8 + 4);
-      float d[NG][4];
-#pragma unroll
-      for (int gi = 0; gi < NG; ++gi) {
-        const uint4 b0 = lds128(tile + gi * 1024 + lane * 16);
-        const uint4 b1 = lds128(tile + gi * 1024 + 512 + lane * 16);
-        d[gi][0] = d[gi][1] = d[gi][2] = d[gi][3] = 0.f;
-        mma_e4m3(d[gi], xa.x, xa.y, b0.x, b0.y);
-        mma_e4m3(d[gi], xa.z, xa.w, b0.z, b0.w);
-        mma_e4m3(d[gi], xb.x, xb.y, b1.x, b1.y);
-        mma_e4m3(d[gi], xb.z, xb.w, b1.z, b1.w);
       }
       if (full) {
         const float sx = xsc[kb];
@@ -277,13 +277,16 @@ __global__ void __launch_bounds__(512) fp8_gemv_kernel(const __grid_constant__ G
           float sw0, sw1;
           if (SCALE == SCALE_CHANNEL) { sw0 = swc[gi][0]; sw1 = swc[gi][1]; }
           else { sw0 = sw1 = block_scale(gi, kb); }
-          acc[gi][0] += d[gi][0] * sx * sw0;
-          acc[gi][1] += d[gi][1] * sx * sw1;
+          acc[gi][0] += dk[gi][0] * sx * sw0;
+          acc[gi][1] += dk[gi][1] * sx * sw1;
         }
-      } else if (lane < 4) {
-        float* dst = p.part + ((size_t)u * KB + kb) * RPU + 2 * t;
+      } else if (t == 0) {
+        float* dst = p.part + ((size_t)u * KB + kb) * RPU + g;
 #pragma unroll
-        for (int gi = 0; gi < NG; ++gi) *reinterpret_cast<float2*>(dst + gi * 8) = make_float2(d[gi][0], d[gi][1]);
+        for (int gi = 0; gi < NG; ++gi) {
+          dst[gi * 16] = dk[gi][0];
+          dst[gi * 16 + 8] = dk[gi][1];
+        }
       }
       if (kb == KB - 1 || tt == t1 - 1) {   // this warp's last tile of unit u
         if (full) {
@@ -298,25 +301,31 @@ __global__ void __launch_bounds__(512) fp8_gemv_kernel(const __grid_constant__ G
           last = __shfl_sync(0xffffffffu, last, 0);
           if (last) {
             __threadfence();
-            const float* src = p.part + (size_t)u * KB * RPU + 2 * t;
+            const float* src = p.part + (size_t)u * KB * RPU + g;
 #pragma unroll
             for (int gi = 0; gi < NG; ++gi) acc[gi][0] = acc[gi][1] = 0.f;
             for (int k2 = 0; k2 < KB; ++k2) {
               const float sx = xsc[k2];
 #pragma unroll
               for (int gi = 0; gi < NG; ++gi) {
-                const float2 dv = __ldcg(reinterpret_cast<const float2*>(src + (size_t)k2 * RPU + gi * 8));
+                const float d0 = __ldcg(src + (size_t)k2 * RPU + gi * 16);
+                const float d1 = __ldcg(src + (size_t)k2 * RPU + gi * 16 + 8);
                 float sw0, sw1;
                 if (SCALE == SCALE_CHANNEL) { sw0 = swc[gi][0]; sw1 = swc[gi][1]; }
                 else { sw0 = sw1 = block_scale(gi, k2); }
-                acc[gi][0] += dv.x * sx * sw0;
-                acc[gi][1] += dv.y * sx * sw1;
+                acc[gi][0] += d0 * sx * sw0;
+                acc[gi][1] += d1 * sx * sw1;
               }
             }
             epilogue(u);
             if (lane == 0) p.counters[u] = 0;
           }
         }
+      }
+      if (++kb == KB) {
+        kb = 0;
+        ++u;
+        if (tt + 1 < t1) begin_unit(u);
       }
     }
     __syncwarp();

@@ -86,12 +86,12 @@ struct GemvShape { int warps, stages, stage_tiles, pre, ctas; };
 GemvShape gemv_defaults(int kind) {
   // 8 warps x 4 stages x 4 KiB ring per warp (128 KiB per CTA), one CTA per SM
   const bool pairs = (kind == QK_GEMV_GATE_UP || kind == QK_GEMV_GATE_UP_RESADD);
-  return GemvShape{8, 4, pairs ? 2 : 4, 4, 1};
+  return GemvShape{8, 4, pairs ? 1 : 2, 4, 1};
 }
 
 template <int PRO, int EPI, int NG>
 int launch_gemv_scaled(int scale_mode, const GemvParams& p, const GemvShape& sh, cudaStream_t stream) {
-  const int smem = gemv_smem(p.K, sh.warps, sh.stages, sh.stage_tiles * 1024 * NG).total;
+  const int smem = gemv_smem(p.K, sh.warps, sh.stages, sh.stage_tiles * GEMV_TILE_BYTES * NG).total;
   const dim3 grid(device_sms() * sh.ctas), block(sh.warps * 32);
   if (scale_mode == QK_SCALE_CHANNEL) {
     auto k = fp8_gemv_kernel<PRO, EPI, SCALE_CHANNEL, NG>;
@@ -146,7 +146,7 @@ int qk_fp8_gemv(int kind, const void* w, const float* w_scale, int scale_mode, c
   if (scale_mode != QK_SCALE_BLOCK128 && scale_mode != QK_SCALE_CHANNEL) return fail(QK_EINVAL, "bad scale_mode %d", scale_mode);
   if (K <= 0 || K % QB || K > 16384) return fail(QK_EINVAL, "K=%d must be a positive multiple of 128, at most 16384", K);
   const bool pairs = (kind == QK_GEMV_GATE_UP || kind == QK_GEMV_GATE_UP_RESADD);
-  if (N <= 0 || N % (pairs ? 16 : 8)) return fail(QK_EINVAL, "N=%d must be a positive multiple of %d", N, pairs ? 16 : 8);
+  if (N <= 0 || N % (pairs ? 32 : 16)) return fail(QK_EINVAL, "N=%d must be a positive multiple of %d", N, pairs ? 32 : 16);
   if (scale_mode == QK_SCALE_BLOCK128 && N % QB) return fail(QK_EINVAL, "block-128 scales need N %% 128 == 0 (N=%d)", N);
   const bool norm = (kind == QK_GEMV_QKV || kind == QK_GEMV_GATE_UP || kind == QK_GEMV_QKV_RESADD || kind == QK_GEMV_GATE_UP_RESADD);
   const bool resadd_k = (kind == QK_GEMV_QKV_RESADD || kind == QK_GEMV_GATE_UP_RESADD);
@@ -234,7 +234,7 @@ int qk_lm_head_argmax(const void* w, const float* w_scale, int head_fp8, const v
                       void* logits, unsigned long long* best, int V, int row_offset, float eps, float* part,
                       int* counters, int ctas, qk_stream_t stream) {
   if (!w || !x || !norm_w || !logits || !best) return fail(QK_EINVAL, "null pointer argument");
-  if (V <= 0 || V % 8) return fail(QK_EINVAL, "V=%d must be a positive multiple of 8", V);
+  if (V <= 0 || V % (head_fp8 ? 16 : 8)) return fail(QK_EINVAL, "V=%d must be a positive multiple of %d", V, head_fp8 ? 16 : 8);
   if (!aligned(w, 16) || !aligned(x, 16) || !aligned(norm_w, 16) || !aligned(logits, 16))
     return fail(QK_EINVAL, "tensor pointers must be 16-byte aligned");
   const int sms = device_sms();

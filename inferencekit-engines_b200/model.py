@@ -10,8 +10,8 @@ Mirrors the decode-relevant half of the reference loader (qwen3-8b-fp8_rtx-5090/
 
 What differs is the FP8 weight layout. The reference re-tiles each matrix for register loads
 (model.py:92-104). The B200 GEMV streams each warp's share of the weights through a shared-memory ring with
-bulk async copies, then reads mma fragments out of shared memory, so `pack_fp8` builds 1 KiB tiles that
-are conflict-free to read from shared memory (see `pack_fp8`).
+bulk async copies, then reads MMA fragments out of shared memory, so `pack_fp8` builds 2 KiB tiles (16 rows
+x 128 k) that are conflict-free to read from shared memory (see `pack_fp8`).
 
 Weights here are synthetic and seeded (no checkpoint in this environment): linear weights N(0, 0.02) in
 fp32, quantized to float8_e4m3fn with either per-output-channel scales (absmax/448, the north-star format)
@@ -53,8 +53,8 @@ class Config:
                "num_key_value_heads": self.n_kv_heads, "head_dim": self.head_dim,
                "intermediate_size": self.inter}
         bad = [f"{k} = {got[k]}, kernels are compiled for {v}" for k, v in KERNEL_SHAPES.items() if got[k] != v]
-        if self.vocab % 8:
-            bad.append(f"vocab_size = {self.vocab} must be a multiple of 8")
+        if self.vocab % 16:
+            bad.append(f"vocab_size = {self.vocab} must be a multiple of 16")
         if bad:
             raise ValueError("unsupported config:\n  - " + "\n  - ".join(bad))
 
@@ -109,31 +109,32 @@ def synth_norm(seed: int, name: str, n: int, init: str, device="cpu") -> torch.T
 def pack_fp8(w: torch.Tensor, pairs: bool = False) -> torch.Tensor:
     """Row-major fp8 [N, K] -> the packed uint8 layout the B200 GEMV streams.
 
-    A unit is 8 output rows (for `pairs`, 8 gate rows + the matching 8 up rows, gate|up stacked as
-    [2I, K]). For unit u and 128-wide K block kb there is one tile per 8 rows of 1024 bytes:
+    A unit is 16 output rows (for `pairs`, 16 gate rows + the matching 16 up rows, gate|up stacked as
+    [2I, K]). For unit u and 128-wide K block kb there is one 2 KiB tile per 16 rows:
 
-        tile[h][lane][16 bytes],  lane = 4*r + t (r = row in the unit, t = 0..3),  h = 0, 1
-        the 16 bytes are k = kb*128 + (2h+c)*32 + hi*16 + t*4 + b for c, hi in {0,1}, b in 0..3
+        tile[c][lane][16 bytes],  c = 32-wide K chunk (0..3), lane = 4*g + t (g = 0..7, t = 0..3)
+        the 16 bytes are words (hi, hh) in the order (0,0) (0,1) (1,0) (1,1), each holding
+        row 16u + 8*hh + g, k = 128*kb + 32*c + 16*hi + 4*t + (0..3)
 
-    i.e. lane L's two 16-byte words are the mma.m16n8k32 B fragments (b0, b1) of row r for the four
-    32-wide K chunks of the block; that mapping is fixed by the mma instruction's fragment layout. The
-    [h][lane] order makes a warp's 16-byte shared-memory reads contiguous (no bank conflicts).
+    i.e. lane L's 16 bytes are exactly its A-operand registers for the two m16n8k16 MMAs of chunk c with
+    rows g and g+8 (see fp8_chunk_dot in csrc/common.cuh); that mapping is fixed by the MMA's fragment
+    layout. [c][lane] order makes a warp's 16-byte shared-memory reads contiguous (no bank conflicts).
     Tiles are ordered [unit][kb] (for pairs [unit][kb][gate, up]), so the tiles of consecutive units are
     one contiguous stream and any split of that stream into ranges is a contiguous byte range.
     """
     N, K = w.shape
-    assert w.dtype == FP8 and N % 8 == 0 and K % QBLOCK == 0
+    assert w.dtype == FP8 and N % 16 == 0 and K % QBLOCK == 0
     KB = K // QBLOCK
     u8 = w.contiguous().view(torch.uint8)
     if pairs:
-        assert N % 16 == 0
+        assert N % 32 == 0
         half = N // 2
-        g = pack_fp8(w[:half]).view(half // 8, KB, 1, 1024)
-        u = pack_fp8(w[half:]).view(half // 8, KB, 1, 1024)
+        g = pack_fp8(w[:half]).view(half // 16, KB, 1, 2048)
+        u = pack_fp8(w[half:]).view(half // 16, KB, 1, 2048)
         return torch.cat([g, u], dim=2).reshape(-1).contiguous()
-    # element (n, k): n = 8*g + r, k = 128*kb + 64*h + 32*c + 16*hi + 4*t + b
-    v = u8.view(N // 8, 8, KB, 2, 2, 2, 4, 4)            # [g, r, kb, h, c, hi, t, b]
-    v = v.permute(0, 2, 3, 1, 6, 4, 5, 7)                 # [g, kb, h, r, t, c, hi, b]
+    # element (n, k): n = 16*u + 8*hh + g, k = 128*kb + 32*c + 16*hi + 4*t + b
+    v = u8.view(N // 16, 2, 8, KB, 4, 2, 4, 4)           # [u, hh, g, kb, c, hi, t, b]
+    v = v.permute(0, 3, 4, 2, 6, 5, 1, 7)                 # [u, kb, c, g, t, hi, hh, b]
     return v.contiguous().view(-1)
 
 
@@ -142,12 +143,12 @@ def unpack_fp8(p: torch.Tensor, N: int, K: int, pairs: bool = False) -> torch.Te
     KB = K // QBLOCK
     if pairs:
         half = N // 2
-        v = p.view(torch.uint8).view(half // 8, KB, 2, 1024)
+        v = p.view(torch.uint8).view(half // 16, KB, 2, 2048)
         g = unpack_fp8(v[:, :, 0].contiguous().view(-1), half, K)
         u = unpack_fp8(v[:, :, 1].contiguous().view(-1), half, K)
         return torch.cat([g, u], 0)
-    v = p.view(torch.uint8).view(N // 8, KB, 2, 8, 4, 2, 2, 4)   # [g, kb, h, r, t, c, hi, b]
-    v = v.permute(0, 3, 1, 2, 5, 6, 4, 7)                       # [g, r, kb, h, c, hi, t, b]
+    v = p.view(torch.uint8).view(N // 16, KB, 4, 8, 4, 2, 2, 4)  # [u, kb, c, g, t, hi, hh, b]
+    v = v.permute(0, 6, 3, 1, 2, 5, 4, 7)                       # [u, hh, g, kb, c, hi, t, b]
     return v.contiguous().view(N, K).view(FP8)
 
 

@@ -61,20 +61,27 @@ def test_config1_layer(name):
     out = eng.resid.cpu()
     kc, vc = inp["kc"].clone(), inp["vc"].clone()
     cos, sin = m.cos.cpu(), m.sin.cpu()
-    ref = O.decode_layer(inp["hidden"], oracle_layer(O, inp), kc, vc, pos, cos, sin, EPS, attn_impl="f32")
-    # K/V rows: V exact; K within one bf16 ulp of the oracle, and equal to the reference forward's fixture
-    # wherever the GPU rsqrt agrees with torch's
-    assert torch.equal(m.v_cache[0, 0, :, pos].cpu(), vc[:, pos])
-    assert np.array_equal(u16(m.v_cache[0, 0, :, pos]), fx["v_row"])
+    tr = {}
+    ref = O.decode_layer(inp["hidden"], oracle_layer(O, inp), kc, vc, pos, cos, sin, EPS, attn_impl="f32", trace=tr)
+    qkv = eng.qkv.cpu()
+    # the qkv projection itself is within the GEMV bar of the oracle's
+    assert rel_l2(qkv, tr["qkv"]) < 1e-2
+    # KV append: the V row is this step's v projection, bit for bit; the K row is the oracle's q/k norm +
+    # RoPE of this step's k projection within one bf16 ulp (rsqrt and reduction order differ from torch)
+    assert torch.equal(m.v_cache[0, 0, :, pos].cpu(), qkv[5120:].view(8, 128))
+    kr = O.norm_rope(qkv[4096:5120].view(8, 128), inp["norms"]["k_norm"], cos[pos], sin[pos], EPS)
     kd = m.k_cache[0, 0, :, pos].cpu()
-    assert (kd.float() - kc[:, pos].float()).abs().max().item() <= 2 * 2 ** -7 * kc[:, pos].float().abs().max().item()
-    # other cache bytes untouched
-    kk = m.k_cache[0, 0].cpu()
+    assert (kd.float() - kr.float()).abs().max().item() <= 2 ** -7 * kr.float().abs().max().item()
+    # no other cache byte changed
+    kk, vv = m.k_cache[0, 0].cpu(), m.v_cache[0, 0].cpu()
     kk[:, pos] = inp["kc"][:, pos]
-    assert torch.equal(kk, inp["kc"])
-    # the layer output: same attention arithmetic as the oracle -> within 1e-2 (W8A8 amplifies 1-ulp flips)
-    assert rel_l2(out, ref) < 1e-2, rel_l2(out, ref)
-    # against the reference forward (bf16-probability SDPA): within the amplified bound of the oracle test
+    vv[:, pos] = inp["vc"][:, pos]
+    assert torch.equal(kk, inp["kc"]) and torch.equal(vv, inp["vc"])
+    # Layer output. Any 1-ulp difference in an activation can move an e4m3 rounding (an e4m3 step is 6%),
+    # and gate_up's act-quant amplifies that to ~1% of the layer output, so a whole layer is compared at
+    # 5e-2 against both the oracle (same attention arithmetic) and the reference forward's golden output;
+    # bit-exactness of the layer is checked against the reference's kernels in test_ref_gpu.py.
+    assert rel_l2(out, ref) < 5e-2, rel_l2(out, ref)
     assert rel_l2(out, bf16(fx["out_resid"])) < 5e-2
 
 
@@ -108,12 +115,16 @@ def test_engine_teacher_forced_tokens_vs_reference_forward():
         eng.graph.replay()
         got.append(int(eng.token.item()))
         logits.append(eng.logits.cpu().clone())
+    checked = 0
     for i, (a, b) in enumerate(zip(got, ref_toks)):
         lg = bf16(fx["logits"][i]).float()
+        assert rel_l2(logits[i], lg) < 5e-2, (i, rel_l2(logits[i], lg))
+        assert a == int(logits[i].float().argmax())      # the fused argmax is the argmax of our logits
         top2 = lg.topk(2).values
-        if (top2[0] - top2[1]).item() > 0.02:
-            assert a == b, (i, a, b)
-        assert rel_l2(logits[i], lg) < 5e-2
+        if (top2[0] - top2[1]).item() > 2 * (logits[i].float() - lg).abs().max().item():
+            assert a == b, (i, a, b)                      # a winner clearer than the logit error must match
+            checked += 1
+    assert checked > 0
 
 
 def test_graph_replay_equals_eager():

@@ -97,13 +97,14 @@ def test_pack_unpack_roundtrip():
     w, _ = M.synth_linear(3, "t", 64, 256, "channel")
     assert torch.equal(M.unpack_fp8(M.pack_fp8(w), 64, 256).view(torch.uint8), w.view(torch.uint8))
     assert torch.equal(M.unpack_fp8(M.pack_fp8(w, True), 64, 256, True).view(torch.uint8), w.view(torch.uint8))
-    # the lane layout: lane L = 4r + t of tile (unit 0, kb 0), word h holds row r, k = 64h + 32c + 16hi + 4t + b
+    # the lane layout of tile (unit 0, kb 0): chunk c, lane L = 4g + t, word (hi, hh) = row 8hh + g,
+    # k = 32c + 16hi + 4t + 0..3
     p = M.pack_fp8(w).view(-1)
     u8 = w.view(torch.uint8)
-    for lane in (0, 5, 31):
-        r, t = lane // 4, lane % 4
-        for h in (0, 1):
-            word = p[h * 512 + lane * 16: h * 512 + lane * 16 + 16]
-            exp = torch.cat([u8[r, 64 * h + 32 * c + 16 * hi + 4 * t: 64 * h + 32 * c + 16 * hi + 4 * t + 4]
-                             for c in (0, 1) for hi in (0, 1)])
+    for c in (0, 3):
+        for lane in (0, 5, 31):
+            g, t = lane // 4, lane % 4
+            word = p[c * 512 + lane * 16: c * 512 + lane * 16 + 16]
+            exp = torch.cat([u8[8 * hh + g, 32 * c + 16 * hi + 4 * t: 32 * c + 16 * hi + 4 * t + 4]
+                             for hi in (0, 1) for hh in (0, 1)])
             assert torch.equal(word, exp)
