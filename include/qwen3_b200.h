@@ -56,8 +56,14 @@ const char* qk_last_error(void);
 /* Programmatic dependent launch on/off for subsequent launches (reference decode.cu:713 set_pdl). */
 int qk_set_pdl(int on);
 
-/* Profiling timestamps (reference decode.cu:716 set_timeline). Only NULL (disabled) is supported. */
-int qk_set_timeline(uint64_t* buf);
+/* Profiling timeline (reference decode.cu:56-62, :716 set_timeline): `buf` is a zeroed device buffer of
+ * n_slots * 2048 u64. Launch number i after this call (any kernel but embed/finalize) writes %globaltimer
+ * stamps of its first 256 CTAs into slot i: CTA c uses words c*8 + j. GEMV and lm_head: j=0 entry, 1 after
+ * the wait on the previous kernel, 2 after the prologue (GEMV), 3 max over warps of the first weight stage
+ * landing (GEMV), 4 max over warps of the end of the weight loop. Attention: 0 entry, 1 after the wait,
+ * 2 partial results written, 3 merge done (merging CTA only). NULL disables. Synchronous; not while
+ * capturing a graph (the slots are fixed into a graph at capture). */
+int qk_set_timeline(uint64_t* buf, int n_slots);
 
 /* Read and clear the device-side error word (bit 1: a bounded wait gave up; bit 2: bad step state or
  * token id). Synchronises `stream`. No counterpart in the reference (its waits are unbounded). */

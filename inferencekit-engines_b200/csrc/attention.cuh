@@ -34,6 +34,7 @@ struct AttnParams {
   bf16* out;                 // [B][n_q * 128]
   int max_seq, max_splits, qkv_stride, state_stride;
   float scale, eps;
+  int tl_slot;               // timeline region of this launch, -1 when off
 };
 
 // Per-head RMSNorm (eps) + RoPE (rotate_half pairs d and d+64 = lane l and l^16), one warp, 4 dims per
@@ -109,6 +110,7 @@ __global__ void __launch_bounds__(128) attention_kernel(const __grid_constant__ 
     for (int i = 0; i < DPT / 8; ++i) kr[i] = ldg_stream(kb + key * HEAD_DIM + slice * DPT + i * 8);
   }
   if (tid == 0) {
+    tl_stamp(p.tl_slot, 0);
     mbar_init(&sm.vbar, 1);
     fence_mbar_init();
     mbar_arrive_expect_tx(&sm.vbar, (uint32_t)(nj * HEAD_DIM * 2));
@@ -116,6 +118,7 @@ __global__ void __launch_bounds__(128) attention_kernel(const __grid_constant__ 
   }
   grid_dep_wait();
   grid_dep_launch();
+  if (tid == 0) tl_stamp(p.tl_slot, 1);
   __syncthreads();                          // barrier init visible to all threads
   const bool v_ok = mbar_wait(&sm.vbar, 0); // the copy must land before the new row is patched in
 
@@ -221,7 +224,10 @@ __global__ void __launch_bounds__(128) attention_kernel(const __grid_constant__ 
   __threadfence();
   __syncthreads();
   int* counter = p.counters + (size_t)b * n_kv + kvh;
-  if (tid == 0) sm.is_last = (atomicAdd(counter, 1) == n_splits - 1);
+  if (tid == 0) {
+    tl_stamp(p.tl_slot, 2);
+    sm.is_last = (atomicAdd(counter, 1) == n_splits - 1);
+  }
   __syncthreads();
   if (!sm.is_last) return;
   __threadfence();
@@ -252,7 +258,10 @@ __global__ void __launch_bounds__(128) attention_kernel(const __grid_constant__ 
 #pragma unroll
   for (int h = 0; h < GQA; ++h)
     p.out[(qbase + kvh * GQA + h) * HEAD_DIM + d] = __float2bfloat16_rn(o[h] / sm.cl[h]);
-  if (tid == 0) *counter = 0;
+  if (tid == 0) {
+    *counter = 0;
+    tl_stamp(p.tl_slot, 3);
+  }
 }
 
 template <int CHUNK>

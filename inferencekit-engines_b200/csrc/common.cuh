@@ -19,6 +19,15 @@ constexpr int QB = 128;         // quantization block (weights and activations)
 enum : int { DEVERR_MBAR_TIMEOUT = 1, DEVERR_BAD_STATE = 2 };
 __device__ int g_dev_error = 0;
 
+// Optional profiling timeline (qk_set_timeline): a caller buffer of `g_timeline_slots` regions of
+// TL_SLOT_WORDS u64; launch number `slot` (assigned by the host in launch order) owns region `slot`, and CTA c
+// (c < TL_MAX_CTAS) writes %globaltimer stamps into words c*TL_CTA_WORDS + i. Null when disabled.
+constexpr int TL_CTA_WORDS = 8;
+constexpr int TL_MAX_CTAS = 256;
+constexpr int TL_SLOT_WORDS = TL_CTA_WORDS * TL_MAX_CTAS;
+__device__ unsigned long long* g_timeline = nullptr;
+__device__ int g_timeline_slots = 0;
+
 // A bounded wait gives up after this many nanoseconds of %globaltimer.
 constexpr unsigned long long WAIT_LIMIT_NS = 2000000000ull;
 
@@ -39,6 +48,21 @@ __device__ __forceinline__ unsigned long long globaltimer() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
+}
+
+__device__ __forceinline__ unsigned long long* tl_cta(int slot) {
+  unsigned long long* tl = g_timeline;
+  const int cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+  if (tl == nullptr || slot < 0 || slot >= g_timeline_slots || cta >= TL_MAX_CTAS) return nullptr;
+  return tl + (size_t)slot * TL_SLOT_WORDS + (size_t)cta * TL_CTA_WORDS;
+}
+__device__ __forceinline__ void tl_stamp(int slot, int i) {
+  unsigned long long* t = tl_cta(slot);
+  if (t) t[i] = globaltimer();
+}
+__device__ __forceinline__ void tl_stamp_max(int slot, int i) {
+  unsigned long long* t = tl_cta(slot);
+  if (t) atomicMax(t + i, globaltimer());
 }
 
 // ---- programmatic dependent launch ------------------------------------------------------------------------

@@ -47,6 +47,7 @@ struct GemvParams {
   int row_offset;            // ARGMAX: vocabulary index of local row 0
   float eps;
   int stages, stage_tiles, pre;
+  int tl_slot;               // timeline region of this launch, -1 when off
 };
 
 // Shared-memory carve-up, computed identically on host and device.
@@ -169,6 +170,7 @@ __global__ void __launch_bounds__(512) fp8_gemv_kernel(const __grid_constant__ G
   uint8_t* ring = smem + L.ring + (size_t)warp * S * ST * UB;
   const uint64_t pol = policy_evict_first();
 
+  if (threadIdx.x == 0) tl_stamp(p.tl_slot, 0);
   if (lane == 0) {
     for (int s = 0; s < S; ++s) mbar_init(&bar[s], 1);
     fence_mbar_init();
@@ -184,10 +186,12 @@ __global__ void __launch_bounds__(512) fp8_gemv_kernel(const __grid_constant__ G
     for (int ch = 0; ch < min(p.pre, first); ++ch) issue(ch);
   grid_dep_wait();
   grid_dep_launch();
+  if (threadIdx.x == 0) tl_stamp(p.tl_slot, 1);
   if (lane == 0)
     for (int ch = min(p.pre, first); ch < first; ++ch) issue(ch);
 
   gemv_prologue<PRO>(p, smem, L);
+  if (threadIdx.x == 0) tl_stamp(p.tl_slot, 2);
   const uint8_t* xh = smem + L.xh;
   const float* xsc = reinterpret_cast<const float*>(smem + L.xscale);
 
@@ -250,6 +254,7 @@ __global__ void __launch_bounds__(512) fp8_gemv_kernel(const __grid_constant__ G
   for (; ch < nchunks; ++ch) {
     const int s = ch % S;
     if (!__all_sync(0xffffffffu, mbar_wait(&bar[s], (uint32_t)((ch / S) & 1)))) { ok = false; break; }
+    if (ch == 0 && lane == 0) tl_stamp_max(p.tl_slot, 3);
     const uint8_t* buf = ring + (size_t)s * ST * UB;
     const int n_here = min(ST, t1 - tt);
     for (int i = 0; i < n_here; ++i, ++tt) {
@@ -334,6 +339,7 @@ __global__ void __launch_bounds__(512) fp8_gemv_kernel(const __grid_constant__ G
       issue(ch + S);
     }
   }
+  if (lane == 0) tl_stamp_max(p.tl_slot, 4);
   if (!ok) {  // a stage never arrived: wait (bounded) for this warp's copies still in flight, then stop
     for (int c2 = ch; c2 < min(ch + S, nchunks); ++c2) mbar_wait(&bar[c2 % S], (uint32_t)((c2 / S) & 1), 100000000ull);
   }
@@ -370,6 +376,7 @@ struct HeadParams {
   int row_offset;
   float eps;
   int stages, pre;
+  int tl_slot;
 };
 constexpr int HEAD_WARPS = 8;
 constexpr int HEAD_ROW_BYTES = HIDDEN * 2;
@@ -402,10 +409,12 @@ __global__ void __launch_bounds__(HEAD_WARPS * 32) lm_head_bf16_kernel(const __g
     bulk_g2s(ring + (size_t)s * HEAD_ROW_BYTES, p.w + (size_t)(r0 + i) * K, HEAD_ROW_BYTES, &bar[s], pol);
   };
   const int first = min(S, nrows);
+  if (threadIdx.x == 0) tl_stamp(p.tl_slot, 0);
   if (lane == 0)
     for (int i = 0; i < min(p.pre, first); ++i) issue(i);
   grid_dep_wait();
   grid_dep_launch();
+  if (threadIdx.x == 0) tl_stamp(p.tl_slot, 1);
   if (lane == 0)
     for (int i = min(p.pre, first); i < first; ++i) issue(i);
 
@@ -462,6 +471,7 @@ __global__ void __launch_bounds__(HEAD_WARPS * 32) lm_head_bf16_kernel(const __g
   if (!ok) {
     for (int c2 = i; c2 < min(i + S, nrows); ++c2) mbar_wait(&bar[c2 % S], (uint32_t)((c2 / S) & 1), 100000000ull);
   }
+  if (lane == 0) tl_stamp_max(p.tl_slot, 4);
   if (lane == 0) bb[warp] = (best_i == 0x7FFFFFFF) ? 0ull : argmax_key(best_v, best_i);
   __syncthreads();
   if (threadIdx.x == 0) {

@@ -16,6 +16,10 @@ namespace {
 
 thread_local char g_msg[512] = "";
 bool g_pdl = false;
+int g_tl_next = -1;        // next timeline slot (launch number since qk_set_timeline), -1 when off
+bool g_tl_ever = false;    // a timeline buffer was set at some point
+
+int next_tl_slot() { return g_tl_next >= 0 ? g_tl_next++ : -1; }
 
 int fail(int code, const char* fmt, ...) {
   va_list ap;
@@ -115,8 +119,21 @@ int qk_set_pdl(int on) {
   return QK_OK;
 }
 
-int qk_set_timeline(uint64_t* buf) {
-  if (buf) return fail(QK_EINVAL, "timeline stamps are not built into these kernels; pass NULL");
+int qk_set_timeline(uint64_t* buf, int n_slots) {
+  if (buf == nullptr) {
+    g_tl_next = -1;
+    if (!g_tl_ever) return QK_OK;   // never enabled: nothing on the device to clear
+    n_slots = 0;
+  } else {
+    if (n_slots <= 0) return fail(QK_EINVAL, "n_slots must be positive");
+    if (reinterpret_cast<uintptr_t>(buf) % 8) return fail(QK_EINVAL, "timeline buffer must be 8-byte aligned");
+    g_tl_ever = true;
+  }
+  unsigned long long* p = reinterpret_cast<unsigned long long*>(buf);
+  cudaError_t e = cudaMemcpyToSymbol(g_timeline, &p, sizeof(p));
+  if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_timeline_slots, &n_slots, sizeof(int));
+  if (e != cudaSuccess) return cuda_fail(e, "setting the timeline buffer");
+  g_tl_next = buf ? 0 : -1;
   return QK_OK;
 }
 
@@ -174,6 +191,7 @@ int qk_fp8_gemv(int kind, const void* w, const float* w_scale, int scale_mode, c
   p.stages = sh.stages;
   p.stage_tiles = sh.stage_tiles;
   p.pre = sh.pre;
+  p.tl_slot = next_tl_slot();
   switch (kind) {
     case QK_GEMV_QKV: return launch_gemv_scaled<PRO_RMSNORM_QUANT, EPI_STORE, 1>(scale_mode, p, sh, stream);
     case QK_GEMV_O:
@@ -218,6 +236,7 @@ int qk_attention(const void* qkv, const void* q_norm_w, const void* k_norm_w, co
   p.state_stride = state_stride;
   p.scale = scale;
   p.eps = eps;
+  p.tl_slot = next_tl_slot();
   const dim3 grid(n_kv, (max_seq + chunk - 1) / chunk, batch);
   auto run = [&](auto kernel, size_t smem) -> int {
     if (int r = ensure_smem((const void*)kernel, (int)smem)) return r;
@@ -258,6 +277,7 @@ int qk_lm_head_argmax(const void* w, const float* w_scale, int head_fp8, const v
     p.stages = sh.stages;
     p.stage_tiles = sh.stage_tiles;
     p.pre = sh.pre;
+    p.tl_slot = next_tl_slot();
     return launch_gemv_scaled<PRO_RMSNORM_QUANT, EPI_ARGMAX, 1>(QK_SCALE_CHANNEL, p, sh, stream);
   }
   HeadParams p = {};
@@ -271,6 +291,7 @@ int qk_lm_head_argmax(const void* w, const float* w_scale, int head_fp8, const v
   p.eps = eps;
   p.stages = 3;
   p.pre = 3;
+  p.tl_slot = next_tl_slot();
   const int smem = head_smem_total(p.stages);
   if (int r = ensure_smem((const void*)lm_head_bf16_kernel, smem)) return r;
   return launch(lm_head_bf16_kernel, dim3(ctas > 0 ? ctas : sms), dim3(HEAD_WARPS * 32), smem, stream, p);

@@ -17,12 +17,12 @@ from kernels import ops
 from model import Qwen3FP8Decode, Linear
 
 # Per-kind GEMV launch shape: ring stages per warp, warps per CTA, stages issued before the wait,
-# 1 KiB tiles per stage, CTAs per SM. Kinds: qkv, o_proj, gate_up, down, lm_head (fp8).
+# tiles per stage (2 KiB = 16 rows x 128 k; 4 KiB for gate|up), CTAs per SM. Kinds: qkv, o_proj, gate_up, down.
 DEFAULT_GEMV_SHAPE = {
-    0: dict(depth=4, warps=8, pre=4, stage_tiles=4, ctas=1),
-    1: dict(depth=4, warps=8, pre=4, stage_tiles=4, ctas=1),
-    2: dict(depth=4, warps=8, pre=4, stage_tiles=2, ctas=1),
-    3: dict(depth=4, warps=8, pre=4, stage_tiles=4, ctas=1),
+    0: dict(depth=4, warps=8, pre=4, stage_tiles=2, ctas=1),
+    1: dict(depth=4, warps=8, pre=4, stage_tiles=2, ctas=1),
+    2: dict(depth=4, warps=8, pre=4, stage_tiles=1, ctas=1),
+    3: dict(depth=4, warps=8, pre=4, stage_tiles=2, ctas=1),
 }
 
 

