@@ -88,6 +88,21 @@ int qk_fp8_gemv(int kind, const void* w, const float* w_scale, int scale_mode, c
                 int warps, int stages, int stage_tiles, int pre, int ctas_per_sm, qk_stream_t stream);
 
 /*
+ * qk_fp8_gemv for callers that cannot allocate device memory (no counterpart in the reference, whose ops take
+ * caller tensors only). Same arguments minus the scratch and the launch shape (defaults are used): the
+ * split-K scratch lives in a fixed 3 MiB + 16 KiB device array inside the library, present on every GPU that
+ * loads it until the process exits. Limit: N*K/128 <= 786432 and N/16 <= 4096 (every per-layer GEMV of
+ * Qwen3-8B fits; the 151936-row lm_head does not), else QK_EINVAL. Nothing is allocated: the first call on a
+ * device looks up the array's device address (cudaGetSymbolAddress) with that device current, so make that
+ * first call before any stream capture. Each call clears the counters with cudaMemsetAsync on `stream`. All
+ * calls share the one array, so calls that may overlap on the GPU (different streams, or concurrent host
+ * threads) race on it; serialise them.
+ */
+int qk_fp8_gemv_noalloc(int kind, const void* w, const float* w_scale, int scale_mode, const void* x,
+                        const void* norm_w, const float* resadd, void* resid_out, void* out, int N, int K, float eps,
+                        qk_stream_t stream);
+
+/*
  * Fused q/k RMSNorm + RoPE + KV append + GQA split-KV decode attention
  * (reference decode.cu:776-800 attention, kernel :379-570).
  *   qkv        bf16 [batch][qkv_stride]: n_q = 4*n_kv query heads, then n_kv k heads, n_kv v heads (128 each)

@@ -311,3 +311,58 @@ int qk_finalize(unsigned long long* best, int* token, int* out_tokens, int* stat
 }
 
 }  // extern "C"
+
+// ---- GEMV without caller-provided scratch --------------------------------------------------------------------
+// qk_fp8_gemv needs two scratch buffers from its caller (the split-K block dots and the per-unit counters).
+// Some callers cannot allocate device memory at all: code that runs inside an allocator-free host runtime,
+// plugins that only receive the tensors of one op call, or a process whose device memory is fully reserved
+// up front. For them, qk_fp8_gemv_noalloc runs the same GEMV with its scratch in the fixed device array
+// below, which the library owns. It is sized for the largest per-layer GEMV of Qwen3-8B (gate|up:
+// N*K/128 = 24576*4096/128 block dots); every GPU that loads this library holds these 3 MiB + 16 KiB until
+// the process exits.
+namespace {
+constexpr size_t NOALLOC_PART_FLOATS = 786432;     // max N*K/128
+constexpr size_t NOALLOC_COUNTERS = 4096;          // max N/16
+constexpr size_t NOALLOC_BYTES = NOALLOC_PART_FLOATS * 4 + NOALLOC_COUNTERS * 4;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[NOALLOC_BYTES];
+
+std::mutex g_noalloc_mu;
+unsigned char* g_noalloc_addr[64] = {nullptr};   // device address of the array, per device
+
+// The array's name in host code is only a host-side stand-in: its device address has to be looked up, once
+// per device, with that device current.
+int noalloc_scratch(unsigned char** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(QK_EINVAL, "device index %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (g_noalloc_addr[dev] == nullptr) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress of the no-alloc scratch");
+    g_noalloc_addr[dev] = static_cast<unsigned char*>(ptr);
+  }
+  *out = g_noalloc_addr[dev];
+  return QK_OK;
+}
+}  // namespace
+
+extern "C" int qk_fp8_gemv_noalloc(int kind, const void* w, const float* w_scale, int scale_mode, const void* x,
+                                   const void* norm_w, const float* resadd, void* resid_out, void* out, int N,
+                                   int K, float eps, qk_stream_t stream) {
+  if (N <= 0 || K <= 0 || K % QB) return fail(QK_EINVAL, "N=%d K=%d: K must be a positive multiple of 128", N, K);
+  const size_t part = (size_t)N * (K / QB), units = (size_t)N / GEMV_UNIT_ROWS;
+  if (part > NOALLOC_PART_FLOATS || units > NOALLOC_COUNTERS)
+    return fail(QK_EINVAL, "N=%d K=%d exceeds the no-alloc scratch (N*K/128 <= %zu, N/16 <= %zu); use qk_fp8_gemv",
+                N, K, NOALLOC_PART_FLOATS, NOALLOC_COUNTERS);
+  unsigned char* base = nullptr;
+  if (int r = noalloc_scratch(&base)) return r;
+  float* part_ptr = reinterpret_cast<float*>(base);
+  int* counters = reinterpret_cast<int*>(base + NOALLOC_PART_FLOATS * 4);
+  // The array keeps whatever the previous call left; the counters must start at zero.
+  cudaError_t e = cudaMemsetAsync(counters, 0, units * sizeof(int), stream);
+  if (e != cudaSuccess) return cuda_fail(e, "clearing the no-alloc counters");
+  return qk_fp8_gemv(kind, w, w_scale, scale_mode, x, norm_w, resadd, resid_out, out, N, K, eps, part_ptr, counters,
+                     0, 0, 0, -1, 0, stream);
+}
