@@ -328,8 +328,54 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_profile_kernel(args):
+    """A few launches of one kernel on one layer's worth of synthetic inputs (for ncu captures)."""
+    import model as M
+    from kernels import ops
+    k = ops()
+    k.set_pdl(False)
+    dev = "cuda"
+    shapes = {"qkv": (0, 6144, 4096), "o_proj": (1, 4096, 4096), "gate_up": (2, 24576, 4096),
+              "down": (3, 4096, 12288), "lm_head": (4, 151936, 4096)}
+    if args.profile_kernel == "attention":
+        max_seq = 4096
+        kc = torch.randn(8, max_seq, 128, device=dev).to(torch.bfloat16)
+        vc = torch.randn(8, max_seq, 128, device=dev).to(torch.bfloat16)
+        qkv = torch.randn(6144, device=dev).to(torch.bfloat16)
+        nw = torch.ones(128, dtype=torch.bfloat16, device=dev)
+        cos, sin = M.rope_tables(max_seq, 128, 1e6, dev)
+        ms = max_seq // 32
+        o_part = torch.zeros(32, ms, 128, device=dev)
+        ml = torch.zeros(32, ms, 2, device=dev)
+        cnt = torch.zeros(8, dtype=torch.int32, device=dev)
+        out = torch.empty(4096, dtype=torch.bfloat16, device=dev)
+        state = torch.tensor([max_seq - 1, 0], dtype=torch.int32, device=dev)
+        for _ in range(args.launches):
+            k.attention(qkv, nw, nw, cos, sin, state, kc, vc, o_part, ml, cnt, out, 128 ** -0.5, 1e-6, 0, args.chunk)
+    else:
+        kind, N, K = shapes[args.profile_kernel]
+        w, s = M.synth_linear(0, "prof", N, K, "channel", device=dev)
+        p = M.pack_fp8(w, pairs=(kind == 2))
+        x = (torch.randn(K, device=dev) * 0.5).to(torch.bfloat16)
+        nw = torch.ones(K, dtype=torch.bfloat16, device=dev)
+        if kind == 4:
+            logits = torch.empty(N, dtype=torch.bfloat16, device=dev)
+            best = torch.zeros(1, dtype=torch.int64, device=dev)
+            for _ in range(args.launches):
+                k.lm_head_argmax(p, x, nw, logits, best, 1e-6, 0, w_scale=s)
+        else:
+            out = torch.zeros(N // 2 if kind == 2 else N, dtype=torch.bfloat16, device=dev)
+            for _ in range(args.launches):
+                k.fp8_gemv(kind, p, s, x, nw if kind in (0, 2) else None, out, N, 1e-6)
+    torch.cuda.synchronize()
+    print(f"profiled {args.profile_kernel} x{args.launches}")
+
+
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--profile-kernel", choices=["qkv", "o_proj", "gate_up", "down", "lm_head", "attention"],
+                    help="launch one kernel --launches times on synthetic inputs and exit (for ncu)")
+    ap.add_argument("--launches", type=int, default=3)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=8)
@@ -341,6 +387,8 @@ def main():
     ap.add_argument("--no-pdl", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
+    if args.profile_kernel:
+        return run_profile_kernel(args)
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     if args.impl == "reference":
