@@ -228,7 +228,8 @@ def run_ours(args):
     m = M.Qwen3FP8Decode.synthetic(cfg, max_seq=max_seq, device=dev, seed=args.seed, scale_mode=args.scale,
                                    head_dtype=args.head, norm_init="ones")
     m.fill_cache_random(start, seed=1234 + rank)
-    eng = Engine(m, pdl=not args.no_pdl, attn_chunk=args.chunk)
+    fused = args.path == "fused"
+    eng = Engine(m, pdl=not args.no_pdl, attn_chunk=args.chunk, fused=fused)
     eng.token.fill_(1)
     eng.state.copy_(torch.tensor([start, 0], dtype=torch.int32))
     eng.capture()
@@ -304,10 +305,10 @@ def run_ours(args):
             "config": {"workload": f"Qwen3-8B FP8 decode, 36 layers, per-channel FP8 + FP8 lm_head, KV 4096 "
                                    f"pre-filled to {start}, {K} greedy steps (ctx {start}..{max_seq - 1}), CUDA graph",
                        "global_batch": ws, "seq_len": max_seq, "parallelism": "replica" if ws > 1 else "tp1",
-                       "scale_mode": args.scale, "head": args.head, "attn_chunk": args.chunk, "pdl": not args.no_pdl,
+                       "scale_mode": args.scale, "head": args.head, "attn_chunk": args.chunk, "pdl": not args.no_pdl, "path": args.path,
                        "l2": "inputs larger than L2 (8.2 GB read per step), no flush"},
             "e2e": {"value": ws * K / t_e2e, "unit": UNIT, "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
-            "gpu_launches": K * (3 + 5 * len(m.layers)),
+            "gpu_launches": K * (1 if fused else 3 + 5 * len(m.layers)),
             "roofline": {"bound": "hbm", "kernel": "fp8 gate_up GEMV (SwiGLU epilogue)", "achieved": achieved,
                          "peak": peak, "peak_source": f"{peak_src} hbm_gbs", "unit": "GB/s", "frac": achieved / peak,
                          "traffic": traffic.get("bytes_per_launch") if traffic else None,
@@ -385,6 +386,8 @@ def main():
     ap.add_argument("--head", default="fp8", choices=["fp8", "bf16"])
     ap.add_argument("--chunk", type=int, default=64)
     ap.add_argument("--no-pdl", action="store_true")
+    ap.add_argument("--path", default="fused", choices=["fused", "ops"],
+                    help="fused: one persistent kernel per token; ops: the reference's 183 per-op launches")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.profile_kernel:

@@ -129,6 +129,39 @@ int qk_lm_head_argmax(const void* w, const float* w_scale, int head_fp8, const v
                       void* logits, unsigned long long* best, int V, int row_offset, float eps, float* part,
                       int* counters, int ctas, qk_stream_t stream);
 
+/* Device pointers of one decoder layer, as laid out in the device array given to qk_decode_step. */
+typedef struct {
+  const void *w_qkv, *w_o, *w_gu, *w_down;       /* packed fp8 (model.pack_fp8; gate|up interleaved) */
+  const float *s_qkv, *s_o, *s_gu, *s_down;      /* scales, layout per scale_mode */
+  const void *ln1, *ln2, *q_norm, *k_norm;       /* bf16 */
+  void *k_cache, *v_cache;                       /* bf16 [8][max_seq][128] of this layer */
+} qk_layer_t;
+
+/*
+ * The whole batch-1 decode step in one launch: embed -> n_layers x (qkv GEMV, attention with KV append,
+ * o_proj, gate_up, down) -> FP8 per-channel lm_head + greedy argmax -> token/state update. Replaces the
+ * reference's 183-launch `Engine.decode_step` (generate.py:102-119) with bit-identical results; the ops it
+ * fuses are the entry points above. Cooperative launch of one CTA per SM (graph-capturable).
+ *   layers      DEVICE array of n_layers qk_layer_t
+ *   state       [pos, step]; token [1]; out_tokens [out_len]; best u64 [1] zero before the first launch
+ *   resid/qkv/attn/h/logits  bf16 activations [4096]/[6144]/[4096]/[12288]/[vocab]
+ *   part        fp32 scratch of part_floats >= qk_decode_step_part_floats(vocab) floats; counters int
+ *               [n_counters >= qk_decode_step_counters(vocab)], zero before the first launch
+ *   o_part/ml_part  fp32 [32][max_splits][128] / [32][max_splits][2]; attn_counters int [8] zero
+ *   sync        unsigned [2] zero before the first launch (left zero)
+ *   max_splits  >= ceil(max_seq/64), <= 1024
+ */
+int qk_decode_step(const qk_layer_t* layers, int n_layers, const void* embed, const void* final_norm,
+                   const void* w_head, const float* s_head, int vocab, const void* cos_tab, const void* sin_tab,
+                   int* token, int* state, int* out_tokens, int out_len, unsigned long long* best, void* resid,
+                   void* qkv, void* attn, void* h, void* logits, float* part, long long part_floats, int* counters,
+                   int n_counters, float* o_part, float* ml_part, int* attn_counters, unsigned* sync, int max_seq,
+                   int max_splits, float eps, int scale_mode, qk_stream_t stream);
+
+/* Minimum scratch sizes of qk_decode_step for a vocabulary size (no GPU needed). */
+long long qk_decode_step_part_floats(int vocab);
+int qk_decode_step_counters(int vocab);
+
 /* resid[b] = table[token[b]] for b < batch (reference decode.cu:812 embed, :667-673). */
 int qk_embed(const int* token, const void* table, void* resid, int vocab, int batch, qk_stream_t stream);
 

@@ -16,8 +16,14 @@ constexpr int QB = 128;         // quantization block (weights and activations)
 
 // Device-side error word: bounded waits that give up set a bit here instead of hanging; the host reads
 // and clears it with qk_get_device_error().
-enum : int { DEVERR_MBAR_TIMEOUT = 1, DEVERR_BAD_STATE = 2 };
+enum : int { DEVERR_MBAR_TIMEOUT = 1, DEVERR_BAD_STATE = 2, DEVERR_GRID_TIMEOUT = 4 };
+// Once a wait has timed out anywhere, every later wait gives up at once instead of waiting its own limit,
+// so a failure ends the launch quickly (the host reads and clears the word with qk_get_device_error).
+constexpr int DEVERR_WAIT_FAILED = DEVERR_MBAR_TIMEOUT | DEVERR_GRID_TIMEOUT;
 __device__ int g_dev_error = 0;
+__device__ __forceinline__ bool wait_failed() {
+  return (*reinterpret_cast<volatile int*>(&g_dev_error) & DEVERR_WAIT_FAILED) != 0;
+}
 
 // Optional profiling timeline (qk_set_timeline): a caller buffer of `g_timeline_slots` regions of
 // TL_SLOT_WORDS u64; launch number `slot` (assigned by the host in launch order) owns region `slot`, and CTA c
@@ -107,6 +113,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer();
   while (!mbar_try_wait(bar, parity)) {
+    if (wait_failed()) return false;
     if (globaltimer() - t0 > limit_ns) {
       atomicOr(&g_dev_error, DEVERR_MBAR_TIMEOUT);
       return false;

@@ -9,6 +9,9 @@
 #include "attention.cuh"
 #include "common.cuh"
 #include "gemv.cuh"
+#include "step.cuh"
+
+static_assert(sizeof(qk_layer_t) == sizeof(qk::StepLayer), "qk_layer_t must mirror StepLayer");
 
 using namespace qk;
 
@@ -295,6 +298,84 @@ int qk_lm_head_argmax(const void* w, const float* w_scale, int head_fp8, const v
   const int smem = head_smem_total(p.stages);
   if (int r = ensure_smem((const void*)lm_head_bf16_kernel, smem)) return r;
   return launch(lm_head_bf16_kernel, dim3(ctas > 0 ? ctas : sms), dim3(HEAD_WARPS * 32), smem, stream, p);
+}
+
+// Scratch of the fused step: block dots of the GEMV units shared by two CTAs, indexed by unit, so sized for
+// the largest N*K/128 (gate|up: 24576*4096/128, or the head: vocab*32) and the most units (gate|up pairs: 768,
+// or the head: vocab/16).
+long long qk_decode_step_part_floats(int vocab) {
+  const long long gu = 24576LL * 4096 / 128, down = 4096LL * 12288 / 128, head = (long long)vocab * 4096 / 128;
+  long long m = gu > down ? gu : down;
+  return m > head ? m : head;
+}
+int qk_decode_step_counters(int vocab) {
+  const int head = vocab / 16;
+  return head > 768 ? head : 768;
+}
+
+int qk_decode_step(const qk_layer_t* layers, int n_layers, const void* embed, const void* final_norm,
+                   const void* w_head, const float* s_head, int vocab, const void* cos_tab, const void* sin_tab,
+                   int* token, int* state, int* out_tokens, int out_len, unsigned long long* best, void* resid,
+                   void* qkv, void* attn, void* h, void* logits, float* part, long long part_floats, int* counters,
+                   int n_counters, float* o_part, float* ml_part, int* attn_counters, unsigned* sync, int max_seq,
+                   int max_splits, float eps, int scale_mode, qk_stream_t stream) {
+  if (!layers || n_layers < 1 || !embed || !final_norm || !w_head || !s_head || !cos_tab || !sin_tab || !token ||
+      !state || !out_tokens || !best || !resid || !qkv || !attn || !h || !logits || !part || !counters || !o_part ||
+      !ml_part || !attn_counters || !sync)
+    return fail(QK_EINVAL, "null pointer argument");
+  if (vocab <= 0 || vocab % 16 || out_len < 1 || max_seq < 1) return fail(QK_EINVAL, "bad vocab/out_len/max_seq");
+  if (part_floats < qk_decode_step_part_floats(vocab) || n_counters < qk_decode_step_counters(vocab))
+    return fail(QK_EINVAL, "scratch too small: part needs %lld floats, counters %d ints",
+                qk_decode_step_part_floats(vocab), qk_decode_step_counters(vocab));
+  if (max_splits < (max_seq + ST_CHUNK - 1) / ST_CHUNK || max_splits > ST_MAX_SPLITS)
+    return fail(QK_EINVAL, "max_splits must cover max_seq/64 and be at most %d", ST_MAX_SPLITS);
+  if (scale_mode != QK_SCALE_BLOCK128 && scale_mode != QK_SCALE_CHANNEL) return fail(QK_EINVAL, "bad scale_mode");
+  StepParams p = {};
+  p.layers = reinterpret_cast<const StepLayer*>(layers);
+  p.n_layers = n_layers;
+  p.embed = static_cast<const bf16*>(embed);
+  p.final_norm = static_cast<const bf16*>(final_norm);
+  p.w_head = static_cast<const uint8_t*>(w_head);
+  p.s_head = s_head;
+  p.vocab = vocab;
+  p.cos_tab = static_cast<const bf16*>(cos_tab);
+  p.sin_tab = static_cast<const bf16*>(sin_tab);
+  p.token = token;
+  p.state = state;
+  p.out_tokens = out_tokens;
+  p.out_len = out_len;
+  p.best = best;
+  p.resid = static_cast<bf16*>(resid);
+  p.qkv = static_cast<bf16*>(qkv);
+  p.attn = static_cast<bf16*>(attn);
+  p.h = static_cast<bf16*>(h);
+  p.logits = static_cast<bf16*>(logits);
+  p.part = part;
+  p.counters = counters;
+  p.o_part = o_part;
+  p.ml_part = ml_part;
+  p.attn_counters = attn_counters;
+  p.sync = sync;
+  p.max_seq = max_seq;
+  p.max_splits = max_splits;
+  p.eps = eps;
+  p.attn_scale = 0.08838834764831845f;   // 128 ** -0.5
+  auto kernel = scale_mode == QK_SCALE_CHANNEL ? decode_step_kernel<SCALE_CHANNEL> : decode_step_kernel<SCALE_BLOCK>;
+  const int smem = (int)sizeof(StepSmem);
+  if (int r = ensure_smem((const void*)kernel, smem)) return r;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(device_sms());
+  cfg.blockDim = dim3(ST_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;   // all CTAs resident: the grid barriers rely on it
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, p);
+  if (e != cudaSuccess) return cuda_fail(e, "decode step launch");
+  return QK_OK;
 }
 
 int qk_embed(const int* token, const void* table, void* resid, int vocab, int batch, qk_stream_t stream) {

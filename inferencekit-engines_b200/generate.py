@@ -27,8 +27,12 @@ DEFAULT_GEMV_SHAPE = {
 
 
 class Engine:
+    """fused=True runs each token as ONE persistent kernel (qk_decode_step, csrc/step.cuh) instead of the
+    reference's 183 launches; results are bit-identical. It needs the FP8 per-channel lm_head and 64-key
+    attention splits; fused=False is the op-by-op path with the reference's drop-in ops."""
+
     def __init__(self, model: Qwen3FP8Decode, pdl: bool = True, attn_chunk: int = 64, lm_head_ctas: int = 0,
-                 gemv_shape: dict | None = None):
+                 gemv_shape: dict | None = None, fused: bool = False):
         self.m = m = model
         self.k = ops()
         self.pdl = pdl
@@ -57,6 +61,23 @@ class Engine:
                 self.gemv_shape[k].update(v)
         self.lm_head_ctas = lm_head_ctas
         self.graph = None
+        self.fused = fused
+        if fused:
+            if not isinstance(m.lm_head, Linear) or attn_chunk != 64 or m.batch != 1:
+                raise ValueError("the fused step needs an FP8 lm_head, 64-key attention splits and batch 1")
+            ptrs = []
+            for li, L in enumerate(m.layers):
+                ptrs.append([L.qkv.packed.data_ptr(), L.o.packed.data_ptr(), L.gu.packed.data_ptr(),
+                             L.down.packed.data_ptr(), L.qkv.scale.data_ptr(), L.o.scale.data_ptr(),
+                             L.gu.scale.data_ptr(), L.down.scale.data_ptr(), L.ln1.data_ptr(), L.ln2.data_ptr(),
+                             L.q_norm.data_ptr(), L.k_norm.data_ptr(), m.k_cache[li, 0].data_ptr(),
+                             m.v_cache[li, 0].data_ptr()])
+            self.layer_table = torch.tensor(ptrs, dtype=torch.int64, device=dev)
+            lib = self.k.lib
+            self.part = torch.empty(lib.qk_decode_step_part_floats(cfg.vocab), dtype=torch.float32, device=dev)
+            self.gemv_counters = torch.zeros(lib.qk_decode_step_counters(cfg.vocab), dtype=torch.int32, device=dev)
+            self.sync = torch.zeros(2, dtype=torch.int32, device=dev)
+            self.scale_mode = 1 if m.scale_mode == "channel" else 0
 
     def settings(self) -> dict:
         return {"pdl": self.pdl, "decode_graph": True, "attn_chunk": self.attn_chunk, "gemv_shape": self.gemv_shape,
@@ -72,6 +93,12 @@ class Engine:
     def decode_step(self):
         """Launch one decode step (eager). Also what gets captured into the graph."""
         m, k, cfg = self.m, self.k, self.m.cfg
+        if self.fused:
+            k.decode_step(self.layer_table, len(m.layers), m.embed, m.norm, m.lm_head.packed, m.lm_head.scale, m.cos,
+                          m.sin, self.token, self.state, self.out_tokens, self.best, self.resid, self.qkv, self.attn,
+                          self.h, self.logits, self.part, self.gemv_counters, self.o_part, self.ml_part,
+                          self.counters, self.sync, m.max_seq, cfg.eps, self.scale_mode)
+            return
         k.embed(self.token, m.embed, self.resid)
         for li, L in enumerate(m.layers):
             self._gemv(0, L.qkv, self.resid, L.ln1, self.qkv)

@@ -67,3 +67,11 @@ def test_ops_refuses_to_run_without_cuda():
     import kernels
     with pytest.raises(RuntimeError):
         kernels.ops()
+
+
+def test_fused_step_scratch_sizes(lib):
+    """The fused step's boundary-unit scratch covers the largest GEMV of a layer even for a small vocabulary."""
+    assert lib.qk_decode_step_part_floats(4096) == 24576 * 4096 // 128
+    assert lib.qk_decode_step_counters(4096) == 768
+    assert lib.qk_decode_step_part_floats(151936) == 151936 * 32
+    assert lib.qk_decode_step_counters(151936) == 151936 // 16
