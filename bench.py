@@ -338,6 +338,19 @@ def run_profile_kernel(args):
     dev = "cuda"
     shapes = {"qkv": (0, 6144, 4096), "o_proj": (1, 4096, 4096), "gate_up": (2, 24576, 4096),
               "down": (3, 4096, 12288), "lm_head": (4, 151936, 4096)}
+    if args.profile_kernel == "decode_step":
+        from generate import Engine
+        cfg = M.Config(layers=args.layers, vocab=16384)
+        m = M.Qwen3FP8Decode.synthetic(cfg, max_seq=4096, device=dev, seed=0, scale_mode="channel", head_dtype="fp8")
+        m.fill_cache_random(3840)
+        eng = Engine(m, fused=True)
+        eng.token.fill_(1)
+        eng.state.copy_(torch.tensor([3840, 0], dtype=torch.int32))
+        for _ in range(args.launches):
+            eng.decode_step()
+        torch.cuda.synchronize()
+        print(f"profiled decode_step ({args.layers} layers) x{args.launches}")
+        return
     if args.profile_kernel == "attention":
         max_seq = 4096
         kc = torch.randn(8, max_seq, 128, device=dev).to(torch.bfloat16)
@@ -374,9 +387,10 @@ def run_profile_kernel(args):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--profile-kernel", choices=["qkv", "o_proj", "gate_up", "down", "lm_head", "attention"],
+    ap.add_argument("--profile-kernel", choices=["qkv", "o_proj", "gate_up", "down", "lm_head", "attention", "decode_step"],
                     help="launch one kernel --launches times on synthetic inputs and exit (for ncu)")
     ap.add_argument("--launches", type=int, default=3)
+    ap.add_argument("--layers", type=int, default=2, help="decoder layers of the --profile-kernel decode_step model")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=8)

@@ -150,13 +150,18 @@ typedef struct {
  *   o_part/ml_part  fp32 [32][max_splits][128] / [32][max_splits][2]; attn_counters int [8] zero
  *   sync        unsigned [2] zero before the first launch (left zero)
  *   max_splits  >= ceil(max_seq/64), <= 1024
+ *   timeline    NULL, or a device buffer of (#SMs) x (5*n_layers + 1) x 8 u64: per CTA and phase (layer l:
+ *               qkv, attn, o, gu, down = 5l+0..4; lm_head = 5*n_layers) the %globaltimer of 0 consumers start,
+ *               1 prologue done (attention: split partials done), 2 work done, 3 producer issues the phase's
+ *               first load; then cumulative clock64 cycles: 4 consumer warp 0 waiting for data, 5 consumer
+ *               warp 0 folding units, 6 producer waiting for free ring stages.
  */
 int qk_decode_step(const qk_layer_t* layers, int n_layers, const void* embed, const void* final_norm,
                    const void* w_head, const float* s_head, int vocab, const void* cos_tab, const void* sin_tab,
                    int* token, int* state, int* out_tokens, int out_len, unsigned long long* best, void* resid,
                    void* qkv, void* attn, void* h, void* logits, float* part, long long part_floats, int* counters,
                    int n_counters, float* o_part, float* ml_part, int* attn_counters, unsigned* sync, int max_seq,
-                   int max_splits, float eps, int scale_mode, qk_stream_t stream);
+                   int max_splits, float eps, int scale_mode, uint64_t* timeline, qk_stream_t stream);
 
 /* Minimum scratch sizes of qk_decode_step for a vocabulary size (no GPU needed). */
 long long qk_decode_step_part_floats(int vocab);

@@ -109,7 +109,27 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 // Wait for phase `parity` of an mbarrier, at most `limit_ns`; on timeout set the device error word.
+// Non-blocking: has the phase with this parity completed? (acquire, like try_wait)
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned long long limit_ns = WAIT_LIMIT_NS) {
+  if (mbar_try_wait(bar, parity)) return true;
+  // Short waits poll only the barrier (clock64 is a local register); after ~0.25 ms the loop also checks
+  // the wall clock and the device error word, both of which cost a global round trip.
+  const long long c0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - c0 > 500000) break;
+  }
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer();
   while (!mbar_try_wait(bar, parity)) {
@@ -172,7 +192,7 @@ __device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t two_bytes) {
 // Tensor-core D[16x8] += A[16x16] * B[16x8], f16 operands, fp32 accumulate (legacy warp-level mma).
 __device__ __forceinline__ void hmma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                           uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(   // a pure register computation: not volatile, so independent MMAs can be interleaved
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
       "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])

@@ -318,7 +318,7 @@ int qk_decode_step(const qk_layer_t* layers, int n_layers, const void* embed, co
                    int* token, int* state, int* out_tokens, int out_len, unsigned long long* best, void* resid,
                    void* qkv, void* attn, void* h, void* logits, float* part, long long part_floats, int* counters,
                    int n_counters, float* o_part, float* ml_part, int* attn_counters, unsigned* sync, int max_seq,
-                   int max_splits, float eps, int scale_mode, qk_stream_t stream) {
+                   int max_splits, float eps, int scale_mode, uint64_t* timeline, qk_stream_t stream) {
   if (!layers || n_layers < 1 || !embed || !final_norm || !w_head || !s_head || !cos_tab || !sin_tab || !token ||
       !state || !out_tokens || !best || !resid || !qkv || !attn || !h || !logits || !part || !counters || !o_part ||
       !ml_part || !attn_counters || !sync)
@@ -360,6 +360,7 @@ int qk_decode_step(const qk_layer_t* layers, int n_layers, const void* embed, co
   p.max_splits = max_splits;
   p.eps = eps;
   p.attn_scale = 0.08838834764831845f;   // 128 ** -0.5
+  p.tl = reinterpret_cast<unsigned long long*>(timeline);
   auto kernel = scale_mode == QK_SCALE_CHANNEL ? decode_step_kernel<SCALE_CHANNEL> : decode_step_kernel<SCALE_BLOCK>;
   const int smem = (int)sizeof(StepSmem);
   if (int r = ensure_smem((const void*)kernel, smem)) return r;

@@ -11,11 +11,12 @@
 //    finally its range of the lm_head. Loads depend only on weights and on KV rows of earlier tokens, so the
 //    producer runs ahead across phase boundaries and keeps DRAM busy while the consumers synchronise.
 //  * warps 0-7 (consumers) execute the phases in order, separated by grid barriers (monotonic counter, bounded
-//    spin): QKV, ATTN, O, GU, DOWN per layer, then HEAD. A GEMV phase gives each CTA a contiguous range of
-//    2 KiB slices (16 rows x 128 k); the 8 warps take one slice each per stage, store the block dots in shared
-//    memory, and one warp folds each finished 16-row unit in K order (units shared with a neighbouring CTA
-//    go through global scratch and a last-arriver fold). The attention phase gives each CTA a range of
-//    (kv head, 64-key split) items; the last CTA of a head merges its splits.
+//    spin): QKV, ATTN, MERGE, O, GU, DOWN per layer, then HEAD. A GEMV phase gives each CTA a contiguous range
+//    of 2 KiB slices (16 rows x 128 k); each warp takes one slice per stage without waiting for the others,
+//    stores its block dots in shared memory, and the warp that completes a 16-row unit folds it in K order
+//    (units shared with a neighbouring CTA go through global scratch and a last-arriver fold). The attention
+//    phase gives each CTA a range of (kv head, 64-key split) items and writes split partials; the merge phase
+//    has 64 CTAs combine them (two per query head).
 //  * The arithmetic is the per-op kernels' (csrc/gemv.cuh, csrc/attention.cuh), operation for operation, so
 //    the step's outputs, logits and KV rows are bit-identical to the per-op path (and so to the reference).
 // All data written by one CTA and read by another in a later phase is read with ld.global.cg (L2), never
@@ -36,6 +37,15 @@ constexpr int ST_NSTAGE = 11;
 constexpr int ST_MAX_K = 12288;
 constexpr int ST_CHUNK = 64;                       // attention keys per item
 constexpr int ST_MAX_SPLITS = 1024;                // contexts up to 64k
+// Block-dot slots: a unit's slices are spread over 8 warps that may drift up to ST_NSTAGE stages apart, so
+// up to ceil((ST_NSTAGE + 1) * ST_SLICES / slices_per_unit) + 2 units can be open at once; a slot holds one
+// unit's KB x 16*NG block dots (2-6 KiB), and 24 KiB always gives enough slots (12, 6 or 4).
+constexpr int ST_BD_FLOATS = 6144;
+constexpr int ST_MAX_SLOTS = 12;
+constexpr int ST_MERGE_SPLITS = 64;                // splits staged per round of the attention merge
+#ifndef ST_SPI
+#define ST_SPI 2                                   // GEMV stages a consumer warp takes per iteration
+#endif
 
 struct StepLayer {
   const uint8_t *w_qkv, *w_o, *w_gu, *w_down;      // model.pack_fp8 layout
@@ -66,21 +76,40 @@ struct StepParams {
   unsigned* sync;                                  // [2]: grid barrier counter, end counter; zero between launches
   int max_seq, max_splits;
   float eps, attn_scale;
+  unsigned long long* tl;                          // optional timeline [CTA][phase][8], null when off
 };
+
+// Phase p of a step: layer l's qkv, attn, o, gu, down are 5l + 0..4; the lm_head is 5 * n_layers.
+// Timeline words per (CTA, phase): 0 consumers start (after the barrier), 1 prologue done, 2 work done
+// (before the next barrier), 3 producer issues the phase's first load.
+// Words 4-6 are cumulative clock64 cycles up to the end of the phase: 4 consumer warp 0 waiting for stages,
+// 5 consumer warp 0 folding units, 6 producer waiting for free stages (cumulative at the phase's first load).
+// Word 7: warp 0 leaves a GEMV phase's stage loop (before its last folds); the attention partials are done.
+constexpr int ST_TL_WORDS = 8;
+__device__ __forceinline__ void step_put(const StepParams& p, int phase, int i, unsigned long long v) {
+  if (p.tl) p.tl[((size_t)blockIdx.x * (5 * p.n_layers + 1) + phase) * ST_TL_WORDS + i] = v;
+}
+__device__ __forceinline__ void step_stamp(const StepParams& p, int phase, int i) {
+  if (p.tl) step_put(p, phase, i, globaltimer());
+}
 
 struct StepSmem {
   uint8_t ring[ST_NSTAGE][ST_STAGE];
   uint32_t xh[ST_MAX_K / 2];                       // x as f16 MMA fragments (see gemv_prologue)
   float xscale[ST_MAX_K / QB];
   union {
-    float bd[2][96 * 16];                          // block dots of the two 16-row units in flight
+    float bd[ST_BD_FLOATS];                        // block dots of the 16-row units in flight (slots)
     bf16 xs[HIDDEN];                               // raw x during an RMSNorm prologue
     struct {
       float qs[GQA][HEAD_DIM + 4];                 // +4: conflict-free reads by 4 heads at once
       float sc[GQA][ST_CHUNK];
-      float m_s[GQA], l_s[GQA], cl[GQA];
-      float cw[GQA][ST_MAX_SPLITS];
+      float m_s[GQA], l_s[GQA];
     } at;
+    struct {
+      float o[ST_MERGE_SPLITS * 64];               // partial outputs of up to 64 splits, 64 dims each
+      float cw[ST_MAX_SPLITS];                     // exp(m_s - M) per split
+      float cl;                                    // sum_s exp(m_s - M) * l_s
+    } mg;
   } u;
   float red[8];
   unsigned long long bestbuf[ST_WARPS];
@@ -108,6 +137,11 @@ __device__ __forceinline__ uint2 ldcg_u2(const void* p) {
   asm volatile("ld.global.cg.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
   return r;
 }
+// 16-byte global -> shared copy through L2 only (data written by another SM), no registers involved
+__device__ __forceinline__ void cp_async16_cg(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 __device__ __forceinline__ uint4 ldcg_u4(const void* p) {
   uint4 r;
   asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
@@ -122,6 +156,9 @@ __device__ __forceinline__ void grid_barrier(unsigned* ctr, unsigned idx) {
     __threadfence();
     atomicAdd(ctr, 1u);
     const unsigned target = (idx + 1) * gridDim.x;
+    const long long c0 = clock64();
+    while (ld_acquire_u32(ctr) < target && clock64() - c0 < 500000) {
+    }
     if (ld_acquire_u32(ctr) < target) {
       const unsigned long long t0 = globaltimer();
       while (ld_acquire_u32(ctr) < target) {
@@ -162,13 +199,16 @@ struct Producer {
   int n;          // stages issued so far
   uint64_t pol;
   bool ok;
+  long long wait_cycles;
   __device__ __forceinline__ void push(const void* src, uint32_t bytes) {
     if (!ok) return;
     const int s = n % ST_NSTAGE;
+    const long long t0 = clock64();
     if (n >= ST_NSTAGE && !mbar_wait(&sm->empty[s], (uint32_t)(((n / ST_NSTAGE) - 1) & 1))) {
       ok = false;
       return;
     }
+    wait_cycles += clock64() - t0;
     mbar_arrive_expect_tx(&sm->full[s], bytes);
     bulk_g2s(sm->ring[s], src, bytes, &sm->full[s], pol);
     ++n;
@@ -197,9 +237,28 @@ struct Consumer {
   int lane, warp, g, t;
   float best_v;
   int best_i;
+  long long wait_cycles, fold_cycles;
+  int tl_phase = 0;   // timeline phase index of the phase being run
 
-  __device__ __forceinline__ bool wait_stage(int s) {
-    return __all_sync(0xffffffffu, mbar_wait(&sm->full[s], (uint32_t)((n / ST_NSTAGE) & 1)));
+  __device__ __forceinline__ bool wait_stage(int s) { return wait_abs(n); }
+  // wait for the load of the consumer's stage number `m` (counted over the whole launch)
+  __device__ __forceinline__ bool wait_abs(int m) {
+    const long long t0 = clock64();
+    const bool ok = __all_sync(0xffffffffu, mbar_wait(&sm->full[m % ST_NSTAGE], (uint32_t)((m / ST_NSTAGE) & 1)));
+    wait_cycles += clock64() - t0;
+    return ok;
+  }
+  // Have all consumer warps released stage number `m`? Its `empty` barrier completes phase m / ST_NSTAGE when
+  // the last warp arrives (release); the test acquires, so every warp's writes before its arrive are visible.
+  // Unambiguous only while this warp has not released stage m + ST_NSTAGE (the slot's next phase).
+  // (warp-uniform results: lane 0's test decides; a lane that saw "not yet" waits, which then returns at once)
+  __device__ __forceinline__ bool released_test(int m) {
+    const bool t = mbar_test_wait(&sm->empty[m % ST_NSTAGE], (uint32_t)((m / ST_NSTAGE) & 1));
+    if (!__shfl_sync(0xffffffffu, (int)t, 0)) return false;
+    return released_wait(m);
+  }
+  __device__ __forceinline__ bool released_wait(int m) {
+    return __all_sync(0xffffffffu, mbar_wait(&sm->empty[m % ST_NSTAGE], (uint32_t)((m / ST_NSTAGE) & 1)));
   }
   __device__ __forceinline__ void release_stage(int s) {
     __syncwarp();
@@ -213,108 +272,215 @@ __device__ __forceinline__ float row_scale(const float* ws, int row, int kb, int
   return SCALE == SCALE_CHANNEL ? __ldg(ws + row) : __ldg(ws + (size_t)(row / QB) * KB + kb);
 }
 
+// Per-row inputs of a unit's epilogue that do not depend on this phase's block dots (the channel scale and,
+// for a residual epilogue, the residual value). The owner loads them for its next unit long before the fold.
+struct FoldPre {
+  float sw, resid;
+};
 template <int EPI, int SCALE, int NG>
+__device__ __forceinline__ FoldPre fold_prefetch(const Consumer& c, const GemvPhase<EPI, SCALE, NG>& ph, int u,
+                                                 bool valid) {
+  const int row = (NG == 2 ? (c.lane >> 4) * (ph.N / 2) : 0) + u * 16 + (c.lane & 15);
+  const bool active = valid && (NG == 2 || c.lane < 16);
+  FoldPre f;
+  f.sw = (SCALE == SCALE_CHANNEL && active) ? __ldg(ph.ws + row) : 0.f;
+  f.resid = (EPI == EPI_RESIDUAL && active) ? __bfloat162float(ldcg_bf16(ph.out + row)) : 0.f;
+  return f;
+}
+
+// Fold of one 16-row unit (32 rows for gate|up) once this CTA's block dots of it are complete: the per-op
+// kernel's in-order sum acc += d * sx * sw over K blocks, then the epilogue. Gate rows fold on lanes 0-15 and
+// up rows on lanes 16-31. A unit shared with a neighbouring CTA is folded by whichever CTA completes it last,
+// from the global scratch. The block dots are read 16 at a time (independent loads), then summed in order.
+template <int KB, int EPI, int SCALE, int NG>
+__device__ __forceinline__ void fold_unit(Consumer& c, const GemvPhase<EPI, SCALE, NG>& ph, const SliceRange& r,
+                                          int u, const FoldPre& pre) {
+  StepSmem& sm = *c.sm;
+  constexpr int RPU = 16 * NG, spu = KB * NG, slot_floats = KB * RPU, nslots = ST_BD_FLOATS / slot_floats;
+  static_assert(KB % 16 == 0, "fold batches");
+  const int lo = max(u * spu, r.s0), hi = min((u + 1) * spu, r.s1);
+  if (u * spu < r.s0) {
+    // The unit started in an earlier CTA, which folds it: publish this CTA's share (already in ph.part). Its
+    // dots were stored by several warps, each of which released them to this warp through the stage's `empty`
+    // barrier; the fence is cumulative over them, so the folding CTA sees all of them after its acquire.
+    if (c.lane == 0) {
+      __threadfence();
+      atomicAdd(&ph.counters[u], hi - lo);
+    }
+    return;
+  }
+  float* slot = &sm.u.bd[(u % nslots) * slot_floats];
+  if (hi < (u + 1) * spu) {
+    // The unit continues in the following CTA(s), which publish their shares early in the phase (their ranges
+    // start with it): wait for them, then copy their block dots behind this CTA's own in the slot. A slice is
+    // 16 consecutive floats of the unit's [KB][NG][16] layout, so the rest is one contiguous run.
+    const int need = (u + 1) * spu - hi;
+    const unsigned* ctr = reinterpret_cast<const unsigned*>(ph.counters + u);
+    bool ok = __all_sync(0xffffffffu, ld_acquire_u32(ctr) >= (unsigned)need);
+    if (!ok) {
+      const unsigned long long t0 = globaltimer();
+      while (!(ok = __all_sync(0xffffffffu, ld_acquire_u32(ctr) >= (unsigned)need))) {
+        if (wait_failed()) break;
+        if (globaltimer() - t0 > WAIT_LIMIT_NS) {
+          if (c.lane == 0) atomicOr(&g_dev_error, DEVERR_GRID_TIMEOUT);
+          break;
+        }
+      }
+    }
+    constexpr int MAXV = spu * 16 / 4 / 32;                   // 16-byte vectors per lane for a whole unit
+    const int off4 = (hi - u * spu) * 4, n4 = spu * 4;        // in 16-byte vectors
+    const uint4* gsrc = reinterpret_cast<const uint4*>(ph.part + (size_t)u * KB * RPU);
+#pragma unroll
+    for (int j = 0; j < MAXV; ++j) {
+      const int i4 = off4 + c.lane + 32 * j;
+      if (ok && i4 < n4) cp_async16_cg(reinterpret_cast<uint4*>(slot) + i4, gsrc + i4);
+    }
+    cp_async_wait_all();
+    __syncwarp();
+    if (c.lane == 0 && ok) ph.counters[u] = 0;
+  }
+  const int rr = c.lane & 15, gi = NG == 2 ? c.lane >> 4 : 0;
+  const int row = gi * (ph.N / 2) + u * 16 + rr;            // gate (or only) row; up row on lanes 16-31
+  const bool active = NG == 2 || c.lane < 16;
+  float a = 0.f;
+  if (active) {
+    const float* s = slot + gi * 16 + rr;
+    for (int k0 = 0; k0 < KB; k0 += 16) {
+      float d[16], sw[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        d[j] = s[(k0 + j) * RPU];
+        sw[j] = SCALE == SCALE_CHANNEL ? pre.sw : row_scale<SCALE>(ph.ws, row, k0 + j, KB);
+      }
+#pragma unroll
+      for (int j = 0; j < 16; ++j) a += d[j] * sm.xscale[k0 + j] * sw[j];
+    }
+  }
+  const float resid_in = pre.resid;
+  if (EPI == EPI_SWIGLU) {
+    const float a_up = __shfl_down_sync(0xffffffffu, a, 16);
+    if (c.lane < 16) {
+      const float gt = bf16r(a);
+      const float up = bf16r(a_up);
+      const float act = bf16r(gt / (1.0f + expf(-gt)));
+      ph.out[row] = __float2bfloat16_rn(act * up);
+    }
+  } else if (c.lane < 16) {
+    if (EPI == EPI_STORE) {
+      ph.out[row] = __float2bfloat16_rn(a);
+    } else if (EPI == EPI_RESIDUAL) {
+      ph.out[row] = __float2bfloat16_rn(resid_in + bf16r(a));
+    } else {  // EPI_ARGMAX
+      ph.out[row] = __float2bfloat16_rn(a);
+      const float lv = bf16r(a);
+      if (lv > c.best_v || (lv == c.best_v && row < c.best_i)) { c.best_v = lv; c.best_i = row; }
+    }
+  }
+}
+
+template <int KB, int EPI, int SCALE, int NG>      // KB = K / 128 (compile time: slice indexing divides by it)
 __device__ void gemv_phase(Consumer& c, const GemvPhase<EPI, SCALE, NG>& ph) {
   StepSmem& sm = *c.sm;
-  const int KB = ph.K / QB;
-  const int RPU = 16 * NG;                          // rows per unit
-  const int spu = KB * NG;                          // slices per unit
+  constexpr int RPU = 16 * NG;                      // rows per unit
+  constexpr int spu = KB * NG;                      // slices per unit
+  constexpr int slot_floats = KB * RPU;
+  constexpr int nslots = ST_BD_FLOATS / slot_floats;
+  // A unit's slot is reused by unit u + nslots, whose first slice lies nslots * spu - spu slices past u's last.
+  // u is folded at the latest when its owner reaches stage (u's last) + ST_NSTAGE, and no warp runs more than
+  // ST_NSTAGE stages ahead of the slowest, so writers stay within (2 * ST_NSTAGE + 2) stages of u's last slice.
+  static_assert((nslots - 1) * spu > (2 * ST_NSTAGE + 2) * ST_SLICES, "too few block-dot slots");
+  static_assert(nslots <= ST_MAX_SLOTS, "slot count");
   const int units = ph.N / RPU;
   const SliceRange r = slice_range(units * spu);
+  const int nst = (r.s1 - r.s0 + ST_SLICES - 1) / ST_SLICES;   // stages of this phase (as the producer issues)
+  const int n0 = c.n;
   const uint8_t* xh = reinterpret_cast<const uint8_t*>(sm.xh);
-  for (int q0 = r.s0; q0 < r.s1; q0 += ST_SLICES) {
-    const int s = c.n % ST_NSTAGE;
-    if (!c.wait_stage(s)) atomicOr(&g_dev_error, DEVERR_MBAR_TIMEOUT);
-    const int q = q0 + c.warp;
-    if (q < r.s1) {
-      const int tile = q / NG, gi = q - tile * NG;
-      const int u = tile / KB, kb = tile - u * KB;
-      const uint8_t* slice = sm.ring[s] + c.warp * ST_SLICE;
-      const uint8_t* xk = xh + kb * 256 + c.t * 16;
-      float d0 = 0.f, d1 = 0.f;
+  // Warps run through the stages without waiting for each other, ST_SPI stages per iteration (one slice of each,
+  // all shared-memory loads issued before the MMAs). A unit is complete for this CTA once every warp has
+  // released the stage holding its last slice, which the ring's `empty` barrier already records; unit u is
+  // folded by warp (u - u_lo) % ST_WARPS as soon as that warp sees its stage released.
+  const int u_lo = r.s0 / spu, u_hi = r.s1 > r.s0 ? (r.s1 - 1) / spu : u_lo - 1;
+  int fu = u_lo + c.warp;                                       // next unit this warp folds
+  auto last_stage = [&](int u) { return (min((u + 1) * spu, r.s1) - 1 - r.s0) / ST_SLICES; };
+  FoldPre pre = fold_prefetch(c, ph, fu, fu <= u_hi);
+  auto fold_next = [&]() {   // fold unit fu, move on to this warp's next unit and prefetch its row inputs
+    const long long t0 = clock64();
+    fold_unit<KB>(c, ph, r, fu, pre);
+    fu += ST_WARPS;
+    pre = fold_prefetch(c, ph, fu, fu <= u_hi);
+    c.fold_cycles += clock64() - t0;
+  };
+  for (int i = 0; i < nst; i += ST_SPI) {
+    const int ns = min(ST_SPI, nst - i);                        // stages in this iteration
+    bool ok = true;
+#pragma unroll
+    for (int j = 0; j < ST_SPI; ++j)
+      if (j < ns) ok = c.wait_abs(n0 + i + j) && ok;
+    if (!ok) atomicOr(&g_dev_error, DEVERR_MBAR_TIMEOUT);
+    // slice coordinates (also computed for slices past the range: kb stays in [0, KB), nothing is stored)
+    int q[ST_SPI], tl[ST_SPI], un[ST_SPI], kb[ST_SPI];
+    uint4 W[ST_SPI][4], X[ST_SPI][4];
+#pragma unroll
+    for (int j = 0; j < ST_SPI; ++j) {
+      q[j] = r.s0 + (i + j) * ST_SLICES + c.warp;
+      tl[j] = q[j] / NG;
+      un[j] = tl[j] / KB;
+      kb[j] = tl[j] - un[j] * KB;
+      const uint8_t* w = sm.ring[(n0 + i + j) % ST_NSTAGE] + c.warp * ST_SLICE + c.lane * 16;
+      const uint8_t* x = xh + kb[j] * 256 + c.t * 16;
 #pragma unroll
       for (int ch = 0; ch < 4; ++ch) {
-        const uint4 xb = lds128(xk + ch * 64);
-        const uint4 w4 = lds128(slice + ch * 512 + c.lane * 16);
+        W[j][ch] = *reinterpret_cast<const uint4*>(w + ch * 512);
+        X[j][ch] = *reinterpret_cast<const uint4*>(x + ch * 64);
+      }
+    }
+    float d0[ST_SPI], d1[ST_SPI];
+#pragma unroll
+    for (int j = 0; j < ST_SPI; ++j) d0[j] = d1[j] = 0.f;
+#pragma unroll
+    for (int ch = 0; ch < 4; ++ch) {
+#pragma unroll
+      for (int j = 0; j < ST_SPI; ++j) {
         float e[4];
-        fp8_chunk_dot(w4, xb, e);
-        d0 += e[0];
-        d1 += e[2];
-      }
-      if (c.t == 0) {
-        const bool interior = (u * spu >= r.s0) && ((u + 1) * spu <= r.s1);
-        float* dst = interior ? &sm.u.bd[u & 1][kb * RPU + gi * 16 + c.g]
-                              : ph.part + ((size_t)u * KB + kb) * RPU + gi * 16 + c.g;
-        dst[0] = d0;
-        dst[8] = d1;
+        fp8_chunk_dot(W[j][ch], X[j][ch], e);
+        d0[j] += e[0];
+        d1[j] += e[2];
       }
     }
-    c.release_stage(s);
-    ++c.n;
-    consumer_sync();
-    // fold the units whose last slice of this CTA's range is in this stage (at most two)
-    const int q_end = min(q0 + ST_SLICES, r.s1) - 1;
-    const int ua = q0 / NG / KB, ub = q_end / NG / KB;
-    for (int u = ua; u <= ub; ++u) {
-      const int last_q = min((u + 1) * spu, r.s1) - 1;
-      if (last_q < q0 || last_q > q_end) continue;
-      if (c.warp != (u & (ST_WARPS - 1))) continue;
-      const bool interior = (u * spu >= r.s0) && ((u + 1) * spu <= r.s1);
-      const float* src;
-      size_t stride;
-      bool do_fold = true;
-      if (interior) {
-        src = sm.u.bd[u & 1];
-        stride = RPU;
-      } else {
-        __threadfence();
-        int last = 0;
-        if (c.lane == 0) {
-          const int mine = last_q - max(u * spu, r.s0) + 1;
-          last = (atomicAdd(&ph.counters[u], mine) + mine == spu);
-        }
-        do_fold = __shfl_sync(0xffffffffu, last, 0) != 0;
-        if (do_fold) __threadfence();
-        src = ph.part + (size_t)u * KB * RPU;
-        stride = RPU;
-      }
-      if (do_fold && c.lane < 16) {
-        const int rr = c.lane;
-        const int row_a = (NG == 2) ? u * 16 + rr : u * 16 + rr;     // gate row (or the row)
-        const int row_b = ph.N / 2 + u * 16 + rr;                     // up row (NG == 2)
-        float a0 = 0.f, a1 = 0.f;
-        const float swa_c = SCALE == SCALE_CHANNEL ? __ldg(ph.ws + row_a) : 0.f;
-        const float swb_c = (SCALE == SCALE_CHANNEL && NG == 2) ? __ldg(ph.ws + row_b) : 0.f;
-        for (int kb = 0; kb < KB; ++kb) {
-          const float sx = sm.xscale[kb];
-          const float da = interior ? src[kb * stride + rr] : __ldcg(src + kb * stride + rr);
-          const float swa = SCALE == SCALE_CHANNEL ? swa_c : row_scale<SCALE>(ph.ws, row_a, kb, KB);
-          a0 += da * sx * swa;
-          if (NG == 2) {
-            const float db = interior ? src[kb * stride + 16 + rr] : __ldcg(src + kb * stride + 16 + rr);
-            const float swb = SCALE == SCALE_CHANNEL ? swb_c : row_scale<SCALE>(ph.ws, row_b, kb, KB);
-            a1 += db * sx * swb;
-          }
-        }
-        // epilogue for this row
-        const int row = u * 16 + rr;
-        if (EPI == EPI_STORE) {
-          ph.out[row] = __float2bfloat16_rn(a0);
-        } else if (EPI == EPI_RESIDUAL) {
-          ph.out[row] = __float2bfloat16_rn(__bfloat162float(ldcg_bf16(ph.out + row)) + bf16r(a0));
-        } else if (EPI == EPI_SWIGLU) {
-          const float gt = bf16r(a0);
-          const float up = bf16r(a1);
-          const float act = bf16r(gt / (1.0f + expf(-gt)));
-          ph.out[row] = __float2bfloat16_rn(act * up);
-        } else {  // EPI_ARGMAX
-          ph.out[row] = __float2bfloat16_rn(a0);
-          const float lv = bf16r(a0);
-          if (lv > c.best_v || (lv == c.best_v && row < c.best_i)) { c.best_v = lv; c.best_i = row; }
+#pragma unroll
+    for (int j = 0; j < ST_SPI; ++j) {
+      if (j < ns && q[j] < r.s1) {
+        const int gi = q[j] - tl[j] * NG;                       // sub-matrix of the slice (0 for NG == 1)
+        const int u = un[j];
+        const bool in = u * spu >= r.s0;                        // this CTA folds u: keep its dots here
+        if (c.t == 0) {
+          float* dst = in ? &sm.u.bd[(u % nslots) * slot_floats + kb[j] * RPU + gi * 16 + c.g]
+                          : ph.part + ((size_t)u * KB + kb[j]) * RPU + gi * 16 + c.g;
+          dst[0] = d0[j];
+          dst[8] = d1[j];
         }
       }
-      if (!interior && do_fold && c.lane == 0) ph.counters[u] = 0;
     }
+    // A unit whose last stage is ST_NSTAGE or more behind the newest stage this warp now holds must be folded
+    // before this warp releases that stage (afterwards the slot's barrier could complete its next phase).
+    const int i_hi = i + ns - 1;
+    while (fu <= u_hi && last_stage(fu) + ST_NSTAGE <= i_hi) {
+      if (!c.released_wait(n0 + last_stage(fu))) atomicOr(&g_dev_error, DEVERR_MBAR_TIMEOUT);
+      fold_next();
+    }
+#pragma unroll
+    for (int j = 0; j < ST_SPI; ++j)
+      if (j < ns) c.release_stage((n0 + i + j) % ST_NSTAGE);
+    c.n = n0 + i_hi + 1;
+    while (fu <= u_hi && last_stage(fu) <= i_hi && c.released_test(n0 + last_stage(fu))) {
+      fold_next();
+    }
+  }
+  if (threadIdx.x == 0) step_stamp(*c.p, c.tl_phase, 7);
+  // the rest of this warp's units: wait for the slowest warp to release their stages
+  while (fu <= u_hi) {
+    if (!c.released_wait(n0 + last_stage(fu))) atomicOr(&g_dev_error, DEVERR_MBAR_TIMEOUT);
+    fold_next();
   }
 }
 
@@ -326,10 +492,26 @@ template <bool NORM>
 __device__ void step_prologue(Consumer& c, const bf16* x, const bf16* norm_w, int K, float eps, bf16* resid_slice_dst) {
   StepSmem& sm = *c.sm;
   const int tid = threadIdx.x;
+  const int KB = K / QB;
+  constexpr int MAXG = ST_MAX_K / QB / ST_WARPS;   // 128-groups per warp at most (12)
+  // Issue every global load of the prologue at once (one L2 round trip instead of one per group).
+  uint2 raw[MAXG], nraw[NORM ? MAXG : 1];
+#pragma unroll
+  for (int i = 0; i < MAXG; ++i) {
+    const int gq = c.warp + i * ST_WARPS;
+    if (gq < KB) {
+      const int k0 = gq * QB + c.lane * 4;
+      if (NORM) nraw[i] = *reinterpret_cast<const uint2*>(norm_w + k0);
+      else raw[i] = ldcg_u2(x + k0);
+    }
+  }
   float rstd = 0.f;
   if (NORM) {   // K == 4096: stage x in shared memory
-    for (int i = tid; i < K / 8; i += ST_WARPS * 32)
-      reinterpret_cast<uint4*>(sm.u.xs)[i] = ldcg_u4(x + i * 8);
+    uint4 xv[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) xv[i] = ldcg_u4(x + (tid + i * ST_WARPS * 32) * 8);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) reinterpret_cast<uint4*>(sm.u.xs)[tid + i * ST_WARPS * 32] = xv[i];
     consumer_sync();
     if (resid_slice_dst) {
       const int per = (K / 8 + gridDim.x - 1) / gridDim.x;
@@ -357,18 +539,17 @@ __device__ void step_prologue(Consumer& c, const bf16* x, const bf16* norm_w, in
     for (int i = 0; i < 4; ++i) tot += sm.red[i];
     rstd = rsqrtf(tot / (float)K + eps);
   }
-  const int KB = K / QB;
   const int ch = c.lane >> 3, hi = (c.lane >> 2) & 1, t = c.lane & 3;
-  for (int gq = c.warp; gq < KB; gq += ST_WARPS) {
+#pragma unroll
+  for (int i = 0; i < MAXG; ++i) {
+    const int gq = c.warp + i * ST_WARPS;
+    if (gq >= KB) break;
     const int k0 = gq * QB + c.lane * 4;
-    uint2 raw;
-    if (NORM) raw = *reinterpret_cast<const uint2*>(sm.u.xs + k0);
-    else raw = ldcg_u2(x + k0);
-    const bf16* e = reinterpret_cast<const bf16*>(&raw);
+    if (NORM) raw[i] = *reinterpret_cast<const uint2*>(sm.u.xs + k0);
+    const bf16* e = reinterpret_cast<const bf16*>(&raw[i]);
     float v[4];
     if (NORM) {
-      const uint2 nraw = *reinterpret_cast<const uint2*>(norm_w + k0);
-      const bf16* we = reinterpret_cast<const bf16*>(&nraw);
+      const bf16* we = reinterpret_cast<const bf16*>(&nraw[i]);
 #pragma unroll
       for (int j = 0; j < 4; ++j) v[j] = bf16r(__bfloat162float(we[j]) * bf16r(__bfloat162float(e[j]) * rstd));
     } else {
@@ -404,6 +585,8 @@ __device__ __forceinline__ void norm_rope_regs(float (&v)[4], const bf16* nw, co
   }
 }
 
+// Attention items (kv head, 64-key split) of this CTA: partial (m, l, o) per query head into o_part/ml_part.
+// The item owning position `pos` appends the new K/V row. Query heads are normalised once per kv head.
 __device__ void attention_phase(Consumer& c, const StepLayer& L, int pos) {
   StepSmem& sm = *c.sm;
   const StepParams& p = *c.p;
@@ -413,6 +596,7 @@ __device__ void attention_phase(Consumer& c, const StepLayer& L, int pos) {
   const int ctx = pos + 1;
   const bf16* cos_row = p.cos_tab + (size_t)pos * HEAD_DIM;
   const bf16* sin_row = p.sin_tab + (size_t)pos * HEAD_DIM;
+  int q_kvh = -1;
   for (int item = it.i0; item < it.i1; ++item) {
     const int kvh = item / it.n_splits, split = item - kvh * it.n_splits;
     const int j0 = split * ST_CHUNK, nj = min(ST_CHUNK, ctx - j0);
@@ -427,10 +611,8 @@ __device__ void attention_phase(Consumer& c, const StepLayer& L, int pos) {
     if (!(okk && okv)) atomicOr(&g_dev_error, DEVERR_MBAR_TIMEOUT);
     const bf16* Ks = reinterpret_cast<const bf16*>(sm.ring[sk]);
     const bf16* Vs = reinterpret_cast<const bf16*>(sm.ring[sv]);
-    // q of the 4 heads (warps 0-3), new k (warp 4) and v (warp 5) of this kv head
-    if (warp < 4) {
-      const bf16* src = p.qkv + (kvh * GQA + warp) * HEAD_DIM + lane * 4;
-      const uint2 raw = ldcg_u2(src);
+    if (warp < 4 && kvh != q_kvh) {   // q of the 4 heads of this kv head (warp = head)
+      const uint2 raw = ldcg_u2(p.qkv + (kvh * GQA + warp) * HEAD_DIM + lane * 4);
       const bf16* e = reinterpret_cast<const bf16*>(&raw);
       float v[4] = {__bfloat162float(e[0]), __bfloat162float(e[1]), __bfloat162float(e[2]), __bfloat162float(e[3])};
       float o[4];
@@ -455,6 +637,7 @@ __device__ void attention_phase(Consumer& c, const StepLayer& L, int pos) {
       *reinterpret_cast<uint2*>(L.v_cache + ((size_t)kvh * p.max_seq + pos) * HEAD_DIM + lane * 4) = raw;
       *reinterpret_cast<uint2*>(const_cast<bf16*>(Vs) + jn * HEAD_DIM + lane * 4) = raw;
     }
+    q_kvh = kvh;
     consumer_sync();
     // scores: thread (key j = tid/4, head h = tid%4): dims 0..63 then 64..127, each summed in order
     {
@@ -516,49 +699,58 @@ __device__ void attention_phase(Consumer& c, const StepLayer& L, int pos) {
     }
     c.release_stage(sk);
     c.release_stage(sv);
-    __threadfence();
     consumer_sync();
-    if (tid == 0) sm.flag = (atomicAdd(p.attn_counters + kvh, 1) == it.n_splits - 1);
+  }
+}
+
+// Merge of the 64-key splits (after a grid barrier): CTA c < 64 produces dims 64*(c%2) .. +63 of query head
+// c/2. The head's partials of up to 64 splits are prefetched into shared memory at once, then every output is
+// the reference's in-order sum over splits: sum_s exp(m_s - M) * o_s[d] / sum_s exp(m_s - M) * l_s.
+__device__ void merge_phase(Consumer& c, int pos) {
+  StepSmem& sm = *c.sm;
+  const StepParams& p = *c.p;
+  if (blockIdx.x >= 64) return;
+  const int tid = threadIdx.x, lane = c.lane, warp = c.warp;
+  const int qh = blockIdx.x >> 1, d0 = (blockIdx.x & 1) * 64;
+  const int n_splits = (pos + 1 + ST_CHUNK - 1) / ST_CHUNK;
+  float* cw = sm.u.mg.cw;
+  if (warp == 0) {
+    const float* ml = p.ml_part + (size_t)qh * p.max_splits * 2;
+    float mloc = -INFINITY;
+    for (int s = lane; s < n_splits; s += 32) mloc = fmaxf(mloc, __ldcg(ml + 2 * s));
+    const float M = warp_max(mloc);
+    float lsum = 0.f;
+    for (int s = lane; s < n_splits; s += 32) {
+      const float wgt = expf(__ldcg(ml + 2 * s) - M);
+      cw[s] = wgt;
+      lsum += wgt * __ldcg(ml + 2 * s + 1);
+    }
+    lsum = warp_sum(lsum);
+    if (lane == 0) sm.u.mg.cl = lsum;
+  }
+  float o = 0.f;
+  const float* op = p.o_part + (size_t)qh * p.max_splits * HEAD_DIM + d0;
+  for (int s0 = 0; s0 < n_splits; s0 += ST_MERGE_SPLITS) {
+    const int ns = min(ST_MERGE_SPLITS, n_splits - s0);
+    // rows s0..s0+ns-1, 64 floats each = 16 float4; 256 threads load ns*16 float4
+    for (int i = tid; i < ns * 16; i += ST_WARPS * 32) {
+      const int s = i >> 4, f = i & 15;
+      reinterpret_cast<uint4*>(sm.u.mg.o)[i] = ldcg_u4(op + (size_t)(s0 + s) * HEAD_DIM + f * 4);
+    }
     consumer_sync();
-    if (sm.flag) {  // the last item of this kv head merges its splits
-      __threadfence();
-      if (warp < 4) {
-        const float* ml = p.ml_part + (size_t)(kvh * GQA + warp) * p.max_splits * 2;
-        float mloc = -INFINITY;
-        for (int s = lane; s < it.n_splits; s += 32) mloc = fmaxf(mloc, __ldcg(ml + 2 * s));
-        const float M = warp_max(mloc);
-        float lsum = 0.f;
-        for (int s = lane; s < it.n_splits; s += 32) {
-          const float wgt = expf(__ldcg(ml + 2 * s) - M);
-          sm.u.at.cw[warp][s] = wgt;
-          lsum += wgt * __ldcg(ml + 2 * s + 1);
-        }
-        lsum = warp_sum(lsum);
-        if (lane == 0) sm.u.at.cl[warp] = lsum;
-      }
-      consumer_sync();
-      const int d = tid & 127, h0 = (tid >> 7) * 2;
-      float o0 = 0.f, o1 = 0.f;
-      const float* op0 = p.o_part + (size_t)(kvh * GQA + h0) * p.max_splits * HEAD_DIM + d;
-      const float* op1 = op0 + (size_t)p.max_splits * HEAD_DIM;
-#pragma unroll 8
-      for (int s = 0; s < it.n_splits; ++s) {
-        o0 += sm.u.at.cw[h0][s] * __ldcg(op0 + (size_t)s * HEAD_DIM);
-        o1 += sm.u.at.cw[h0 + 1][s] * __ldcg(op1 + (size_t)s * HEAD_DIM);
-      }
-      p.attn[(kvh * GQA + h0) * HEAD_DIM + d] = __float2bfloat16_rn(o0 / sm.u.at.cl[h0]);
-      p.attn[(kvh * GQA + h0 + 1) * HEAD_DIM + d] = __float2bfloat16_rn(o1 / sm.u.at.cl[h0 + 1]);
-      if (tid == 0) p.attn_counters[kvh] = 0;
+    if (tid < 64) {
+      for (int s = 0; s < ns; ++s) o += cw[s0 + s] * sm.u.mg.o[s * 64 + tid];
     }
     consumer_sync();
   }
+  if (tid < 64) p.attn[qh * HEAD_DIM + d0 + tid] = __float2bfloat16_rn(o / sm.u.mg.cl);
 }
 
 // ---- the kernel -------------------------------------------------------------------------------------------------
 template <int SCALE>
 __global__ void __launch_bounds__(ST_THREADS, 1) decode_step_kernel(const __grid_constant__ StepParams p) {
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  StepSmem& sm = *reinterpret_cast<StepSmem*>(smem_raw);
+  extern __shared__ __align__(1024) uint8_t smem_step[];
+  StepSmem& sm = *reinterpret_cast<StepSmem*>(smem_step);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int pos = p.state[0];
   if (pos < 0 || pos >= p.max_seq || (pos + ST_CHUNK) / ST_CHUNK > p.max_splits) {
@@ -576,11 +768,15 @@ __global__ void __launch_bounds__(ST_THREADS, 1) decode_step_kernel(const __grid
   constexpr int H = HIDDEN, I = 12288, QKV_N = 6144;
   if (warp == ST_WARPS) {   // ---------------- producer ----------------
     if (lane == 0) {
-      Producer pr{&sm, 0, policy_evict_first(), true};
+      Producer pr{&sm, 0, policy_evict_first(), true, 0};
       const AttnItems it = attn_items(pos, 8);
       for (int l = 0; l < p.n_layers; ++l) {
         const StepLayer& L = p.layers[l];
+        step_stamp(p, 5 * l + 0, 3);
+        step_put(p, 5 * l + 0, 6, pr.wait_cycles);
         pr.gemv(L.w_qkv, (QKV_N / 16) * (H / QB));
+        step_stamp(p, 5 * l + 1, 3);
+        step_put(p, 5 * l + 1, 6, pr.wait_cycles);
         for (int item = it.i0; item < it.i1; ++item) {
           const int kvh = item / it.n_splits, split = item - kvh * it.n_splits;
           const int j0 = split * ST_CHUNK, nj = min(ST_CHUNK, pos + 1 - j0);
@@ -588,46 +784,82 @@ __global__ void __launch_bounds__(ST_THREADS, 1) decode_step_kernel(const __grid
           pr.push(L.k_cache + off, (uint32_t)(nj * HEAD_DIM * 2));
           pr.push(L.v_cache + off, (uint32_t)(nj * HEAD_DIM * 2));
         }
+        step_stamp(p, 5 * l + 2, 3);
+        step_put(p, 5 * l + 2, 6, pr.wait_cycles);
         pr.gemv(L.w_o, (H / 16) * (H / QB));
+        step_stamp(p, 5 * l + 3, 3);
+        step_put(p, 5 * l + 3, 6, pr.wait_cycles);
         pr.gemv(L.w_gu, (2 * I / 16) * (H / QB));
+        step_stamp(p, 5 * l + 4, 3);
+        step_put(p, 5 * l + 4, 6, pr.wait_cycles);
         pr.gemv(L.w_down, (H / 16) * (I / QB));
       }
+      step_stamp(p, 5 * p.n_layers, 3);
+      step_put(p, 5 * p.n_layers, 6, pr.wait_cycles);
       pr.gemv(p.w_head, (p.vocab / 16) * (H / QB));
     }
     return;
   }
   // ---------------- consumers ----------------
-  Consumer c{&sm, &p, 0, lane, warp, lane >> 2, lane & 3, -INFINITY, 0x7FFFFFFF};
+  Consumer c{&sm, &p, 0, lane, warp, lane >> 2, lane & 3, -INFINITY, 0x7FFFFFFF, 0, 0};
   unsigned nbar = 0;
   const int tok = p.token[0];
   const bool tok_ok = tok >= 0 && tok < p.vocab;
   if (!tok_ok && threadIdx.x == 0 && blockIdx.x == 0) atomicOr(&g_dev_error, DEVERR_BAD_STATE);
+  const bool tl = p.tl != nullptr && threadIdx.x == 0;
   for (int l = 0; l < p.n_layers; ++l) {
     const StepLayer& L = p.layers[l];
+    const int ph = 5 * l;
     // QKV
+    if (tl) step_stamp(p, ph, 0);
     if (l == 0) step_prologue<true>(c, p.embed + (size_t)(tok_ok ? tok : 0) * H, L.ln1, H, p.eps, p.resid);
     else step_prologue<true>(c, p.resid, L.ln1, H, p.eps, nullptr);
-    gemv_phase(c, GemvPhase<EPI_STORE, SCALE, 1>{L.s_qkv, QKV_N, H, p.qkv, p.part, p.counters});
+    if (tl) step_stamp(p, ph, 1);
+    c.tl_phase = ph;
+    gemv_phase<32>(c, GemvPhase<EPI_STORE, SCALE, 1>{L.s_qkv, QKV_N, H, p.qkv, p.part, p.counters});
+    if (tl) { step_stamp(p, ph, 2); step_put(p, ph, 4, c.wait_cycles); step_put(p, ph, 5, c.fold_cycles); }
     grid_barrier(p.sync, nbar++);
-    // ATTN (writes K/V rows at pos and the merged attention output)
+    // ATTN: split partials (and the K/V rows at pos), then the merge into the attention output
+    if (tl) step_stamp(p, ph + 1, 0);
     attention_phase(c, L, pos);
+    if (tl) step_stamp(p, ph + 1, 7);
+    grid_barrier(p.sync, nbar++);
+    if (tl) step_stamp(p, ph + 1, 1);
+    merge_phase(c, pos);
+    if (tl) { step_stamp(p, ph + 1, 2); step_put(p, ph + 1, 4, c.wait_cycles); step_put(p, ph + 1, 5, c.fold_cycles); }
     grid_barrier(p.sync, nbar++);
     // O: resid += W_o . quant(attn)
+    if (tl) step_stamp(p, ph + 2, 0);
     step_prologue<false>(c, p.attn, nullptr, H, p.eps, nullptr);
-    gemv_phase(c, GemvPhase<EPI_RESIDUAL, SCALE, 1>{L.s_o, H, H, p.resid, p.part, p.counters});
+    if (tl) step_stamp(p, ph + 2, 1);
+    c.tl_phase = ph + 2;
+    gemv_phase<32>(c, GemvPhase<EPI_RESIDUAL, SCALE, 1>{L.s_o, H, H, p.resid, p.part, p.counters});
+    if (tl) { step_stamp(p, ph + 2, 2); step_put(p, ph + 2, 4, c.wait_cycles); step_put(p, ph + 2, 5, c.fold_cycles); }
     grid_barrier(p.sync, nbar++);
     // GU: h = SwiGLU(W_gu . quant(RMSNorm(resid)))
+    if (tl) step_stamp(p, ph + 3, 0);
     step_prologue<true>(c, p.resid, L.ln2, H, p.eps, nullptr);
-    gemv_phase(c, GemvPhase<EPI_SWIGLU, SCALE, 2>{L.s_gu, 2 * I, H, p.h, p.part, p.counters});
+    if (tl) step_stamp(p, ph + 3, 1);
+    c.tl_phase = ph + 3;
+    gemv_phase<32>(c, GemvPhase<EPI_SWIGLU, SCALE, 2>{L.s_gu, 2 * I, H, p.h, p.part, p.counters});
+    if (tl) { step_stamp(p, ph + 3, 2); step_put(p, ph + 3, 4, c.wait_cycles); step_put(p, ph + 3, 5, c.fold_cycles); }
     grid_barrier(p.sync, nbar++);
     // DOWN: resid += W_down . quant(h)
+    if (tl) step_stamp(p, ph + 4, 0);
     step_prologue<false>(c, p.h, nullptr, I, p.eps, nullptr);
-    gemv_phase(c, GemvPhase<EPI_RESIDUAL, SCALE, 1>{L.s_down, H, I, p.resid, p.part, p.counters});
+    if (tl) step_stamp(p, ph + 4, 1);
+    c.tl_phase = ph + 4;
+    gemv_phase<96>(c, GemvPhase<EPI_RESIDUAL, SCALE, 1>{L.s_down, H, I, p.resid, p.part, p.counters});
+    if (tl) { step_stamp(p, ph + 4, 2); step_put(p, ph + 4, 4, c.wait_cycles); step_put(p, ph + 4, 5, c.fold_cycles); }
     grid_barrier(p.sync, nbar++);
   }
+  if (tl) step_stamp(p, 5 * p.n_layers, 0);
   // HEAD: logits + greedy argmax (FP8 per-channel head)
   step_prologue<true>(c, p.resid, p.final_norm, H, p.eps, nullptr);
-  gemv_phase(c, GemvPhase<EPI_ARGMAX, SCALE_CHANNEL, 1>{p.s_head, p.vocab, H, p.logits, p.part, p.counters});
+  if (tl) step_stamp(p, 5 * p.n_layers, 1);
+  c.tl_phase = 5 * p.n_layers;
+  gemv_phase<32>(c, GemvPhase<EPI_ARGMAX, SCALE_CHANNEL, 1>{p.s_head, p.vocab, H, p.logits, p.part, p.counters});
+  if (tl) { step_stamp(p, 5 * p.n_layers, 2); step_put(p, 5 * p.n_layers, 4, c.wait_cycles); step_put(p, 5 * p.n_layers, 5, c.fold_cycles); }
   {
     unsigned long long key = (c.best_i == 0x7FFFFFFF) ? 0ull : argmax_key(c.best_v, c.best_i);
 #pragma unroll

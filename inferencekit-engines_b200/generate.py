@@ -62,6 +62,7 @@ class Engine:
         self.lm_head_ctas = lm_head_ctas
         self.graph = None
         self.fused = fused
+        self.step_timeline = None     # fused step only: int64 [#SMs, 5*layers+1, 4] %globaltimer stamps
         if fused:
             if not isinstance(m.lm_head, Linear) or attn_chunk != 64 or m.batch != 1:
                 raise ValueError("the fused step needs an FP8 lm_head, 64-key attention splits and batch 1")
@@ -97,7 +98,7 @@ class Engine:
             k.decode_step(self.layer_table, len(m.layers), m.embed, m.norm, m.lm_head.packed, m.lm_head.scale, m.cos,
                           m.sin, self.token, self.state, self.out_tokens, self.best, self.resid, self.qkv, self.attn,
                           self.h, self.logits, self.part, self.gemv_counters, self.o_part, self.ml_part,
-                          self.counters, self.sync, m.max_seq, cfg.eps, self.scale_mode)
+                          self.counters, self.sync, m.max_seq, cfg.eps, self.scale_mode, self.step_timeline)
             return
         k.embed(self.token, m.embed, self.resid)
         for li, L in enumerate(m.layers):

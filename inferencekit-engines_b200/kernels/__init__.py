@@ -44,7 +44,7 @@ _SIGS = {
     "qk_lm_head_argmax": ([_VP, _VP, _I, _VP, _VP, _VP, _VP, _I, _I, _F, _VP, _VP, _I, _VP], _I),
     "qk_embed": ([_VP, _VP, _VP, _I, _I, _VP], _I),
     "qk_decode_step": ([_VP, _I, _VP, _VP, _VP, _VP, _I, _VP, _VP, _VP, _VP, _VP, _I, _VP, _VP, _VP, _VP, _VP, _VP,
-                        _VP, ctypes.c_longlong, _VP, _I, _VP, _VP, _VP, _VP, _I, _I, _F, _I, _VP], _I),
+                        _VP, ctypes.c_longlong, _VP, _I, _VP, _VP, _VP, _VP, _I, _I, _F, _I, _VP, _VP], _I),
     "qk_decode_step_part_floats": ([_I], ctypes.c_longlong),
     "qk_decode_step_counters": ([_I], _I),
     "qk_fp8_gemv_noalloc": ([_I, _VP, _VP, _I, _VP, _VP, _VP, _VP, _VP, _I, _I, _F, _VP], _I),
@@ -164,15 +164,16 @@ class DecodeOps:
 
     def decode_step(self, layer_table, n_layers, embed, final_norm, w_head, s_head, cos_tab, sin_tab, token, state,
                     out_tokens, best, resid, qkv, attn, h, logits, part, counters, o_part, ml_part, attn_counters,
-                    sync, max_seq, eps, scale_mode):
+                    sync, max_seq, eps, scale_mode, timeline=None):
         """The fused decode step (qk_decode_step): one launch per token. layer_table: int64 CUDA tensor
-        [n_layers, 14] of device pointers in qk_layer_t order."""
+        [n_layers, 14] of device pointers in qk_layer_t order; timeline: optional int64 CUDA tensor of
+        #SMs * (5*n_layers + 1) * 4 words (layout in include/qwen3_b200.h)."""
         st = self.lib.qk_decode_step(_p(layer_table), int(n_layers), _p(embed), _p(final_norm), _p(w_head),
                                      _p(s_head), embed.shape[0], _p(cos_tab), _p(sin_tab), _p(token), _p(state),
                                      _p(out_tokens), out_tokens.numel(), _p(best), _p(resid), _p(qkv), _p(attn), _p(h),
                                      _p(logits), _p(part), part.numel(), _p(counters), counters.numel(), _p(o_part),
                                      _p(ml_part), _p(attn_counters), _p(sync), int(max_seq), o_part.shape[-2],
-                                     float(eps), int(scale_mode), _stream())
+                                     float(eps), int(scale_mode), _p(timeline), _stream())
         self._check(st, "decode_step")
 
     def embed(self, token, table, resid):
