@@ -6,15 +6,16 @@
 //
 // Structure (grid = one CTA per SM, cooperative launch so all CTAs are resident):
 //  * warp 8 (producer): lane 0 walks the CTA's static schedule of loads for the entire step and issues them
-//    as bulk async copies into an 11 x 16 KiB shared-memory ring (full/empty mbarriers): for each layer its
-//    slice range of W_qkv, the K and V chunks of its attention items, then its ranges of W_o, W_gu, W_down;
-//    finally its range of the lm_head. Loads depend only on weights and on KV rows of earlier tokens, so the
+//    as bulk async copies into a 5 x 32 KiB shared-memory ring (full/empty mbarriers): for each layer its
+//    slice range of W_qkv, the K and V chunks of its attention items (one stage per item), then its ranges of
+//    W_o, W_gu, W_down; finally its range of the lm_head. Loads depend only on weights and on KV rows of earlier tokens, so the
 //    producer runs ahead across phase boundaries and keeps DRAM busy while the consumers synchronise.
 //  * warps 0-7 (consumers) execute the phases in order, separated by grid barriers (monotonic counter, bounded
 //    spin): QKV, ATTN, MERGE, O, GU, DOWN per layer, then HEAD. A GEMV phase gives each CTA a contiguous range
-//    of 2 KiB slices (16 rows x 128 k); each warp takes one slice per stage without waiting for the others,
-//    stores its block dots in shared memory, and the warp that completes a 16-row unit folds it in K order
-//    (units shared with a neighbouring CTA go through global scratch and a last-arriver fold). The attention
+//    of 2 KiB slices (16 rows x 128 k); each warp takes two slices per stage without waiting for the others and
+//    stores their block dots in shared memory; once every warp has released a 16-row unit's last stage, one
+//    warp folds the unit in K order (a unit split with the next CTA gets that CTA's dots through global
+//    scratch; the CTA holding a unit's first K block always folds it). The attention
 //    phase gives each CTA a range of (kv head, 64-key split) items and writes split partials; the merge phase
 //    has 64 CTAs combine them (two per query head).
 //  * The arithmetic is the per-op kernels' (csrc/gemv.cuh, csrc/attention.cuh), operation for operation, so
@@ -30,21 +31,21 @@ namespace qk {
 
 constexpr int ST_WARPS = 8;                        // consumer warps
 constexpr int ST_THREADS = (ST_WARPS + 1) * 32;    // + one producer warp
-constexpr int ST_STAGE = 16384;
+constexpr int ST_STAGE = 32768;
 constexpr int ST_SLICE = 2048;                     // 16 rows x 128 k of fp8
-constexpr int ST_SLICES = ST_STAGE / ST_SLICE;     // 8 slices per stage, one per consumer warp
-constexpr int ST_NSTAGE = 11;
+constexpr int ST_SLICES = ST_STAGE / ST_SLICE;     // 16 slices per stage
+constexpr int ST_SPW = ST_SLICES / ST_WARPS;       // 2 slices per consumer warp per stage
+constexpr int ST_NSTAGE = 5;
 constexpr int ST_MAX_K = 12288;
 constexpr int ST_CHUNK = 64;                       // attention keys per item
 constexpr int ST_MAX_SPLITS = 1024;                // contexts up to 64k
-// Block-dot slots: a unit's slices are spread over 8 warps that may drift up to ST_NSTAGE stages apart, so
-// up to ceil((ST_NSTAGE + 1) * ST_SLICES / slices_per_unit) + 2 units can be open at once; a slot holds one
-// unit's KB x 16*NG block dots (2-6 KiB), and 24 KiB always gives enough slots (12, 6 or 4).
+// Block-dot slots: a slot holds one open unit's KB x 16*NG block dots (2-6 KiB); 24 KiB gives 12, 6 or 4 slots,
+// enough for the units that can be open at once (see the bound in gemv_phase).
 constexpr int ST_BD_FLOATS = 6144;
 constexpr int ST_MAX_SLOTS = 12;
 constexpr int ST_MERGE_SPLITS = 64;                // splits staged per round of the attention merge
 #ifndef ST_SPI
-#define ST_SPI 2                                   // GEMV stages a consumer warp takes per iteration
+#define ST_SPI 1                                   // GEMV stages a consumer warp takes per iteration
 #endif
 
 struct StepLayer {
@@ -211,6 +212,21 @@ struct Producer {
     wait_cycles += clock64() - t0;
     mbar_arrive_expect_tx(&sm->full[s], bytes);
     bulk_g2s(sm->ring[s], src, bytes, &sm->full[s], pol);
+    ++n;
+  }
+  // K and V chunks of one attention item into one stage (K in the first half, V in the second)
+  __device__ __forceinline__ void push_kv(const void* k, const void* v, uint32_t bytes) {
+    if (!ok) return;
+    const int s = n % ST_NSTAGE;
+    const long long t0 = clock64();
+    if (n >= ST_NSTAGE && !mbar_wait(&sm->empty[s], (uint32_t)(((n / ST_NSTAGE) - 1) & 1))) {
+      ok = false;
+      return;
+    }
+    wait_cycles += clock64() - t0;
+    mbar_arrive_expect_tx(&sm->full[s], 2 * bytes);
+    bulk_g2s(sm->ring[s], k, bytes, &sm->full[s], pol);
+    bulk_g2s(sm->ring[s] + ST_STAGE / 2, v, bytes, &sm->full[s], pol);
     ++n;
   }
   __device__ __forceinline__ void gemv(const uint8_t* w, int n_slices) {
@@ -395,7 +411,7 @@ __device__ void gemv_phase(Consumer& c, const GemvPhase<EPI, SCALE, NG>& ph) {
   const int nst = (r.s1 - r.s0 + ST_SLICES - 1) / ST_SLICES;   // stages of this phase (as the producer issues)
   const int n0 = c.n;
   const uint8_t* xh = reinterpret_cast<const uint8_t*>(sm.xh);
-  // Warps run through the stages without waiting for each other, ST_SPI stages per iteration (one slice of each,
+  // Warps run through the stages without waiting for each other, ST_SPI stages per iteration (ST_SPW slices of each,
   // all shared-memory loads issued before the MMAs). A unit is complete for this CTA once every warp has
   // released the stage holding its last slice, which the ring's `empty` barrier already records; unit u is
   // folded by warp (u - u_lo) % ST_WARPS as soon as that warp sees its stage released.
@@ -417,16 +433,19 @@ __device__ void gemv_phase(Consumer& c, const GemvPhase<EPI, SCALE, NG>& ph) {
     for (int j = 0; j < ST_SPI; ++j)
       if (j < ns) ok = c.wait_abs(n0 + i + j) && ok;
     if (!ok) atomicOr(&g_dev_error, DEVERR_MBAR_TIMEOUT);
-    // slice coordinates (also computed for slices past the range: kb stays in [0, KB), nothing is stored)
-    int q[ST_SPI], tl[ST_SPI], un[ST_SPI], kb[ST_SPI];
-    uint4 W[ST_SPI][4], X[ST_SPI][4];
+    // slice coordinates (also computed for slices past the range: kb stays in [0, KB), nothing is stored);
+    // slice j of the iteration is slice (j % ST_SPW) * ST_WARPS + warp of stage i + j / ST_SPW
+    constexpr int NSL = ST_SPI * ST_SPW;
+    int q[NSL], tl[NSL], un[NSL], kb[NSL];
+    uint4 W[NSL][4], X[NSL][4];
 #pragma unroll
-    for (int j = 0; j < ST_SPI; ++j) {
-      q[j] = r.s0 + (i + j) * ST_SLICES + c.warp;
+    for (int j = 0; j < NSL; ++j) {
+      const int st = j / ST_SPW, k = j % ST_SPW;
+      q[j] = r.s0 + (i + st) * ST_SLICES + k * ST_WARPS + c.warp;
       tl[j] = q[j] / NG;
       un[j] = tl[j] / KB;
       kb[j] = tl[j] - un[j] * KB;
-      const uint8_t* w = sm.ring[(n0 + i + j) % ST_NSTAGE] + c.warp * ST_SLICE + c.lane * 16;
+      const uint8_t* w = sm.ring[(n0 + i + st) % ST_NSTAGE] + (k * ST_WARPS + c.warp) * ST_SLICE + c.lane * 16;
       const uint8_t* x = xh + kb[j] * 256 + c.t * 16;
 #pragma unroll
       for (int ch = 0; ch < 4; ++ch) {
@@ -434,13 +453,13 @@ __device__ void gemv_phase(Consumer& c, const GemvPhase<EPI, SCALE, NG>& ph) {
         X[j][ch] = *reinterpret_cast<const uint4*>(x + ch * 64);
       }
     }
-    float d0[ST_SPI], d1[ST_SPI];
+    float d0[NSL], d1[NSL];
 #pragma unroll
-    for (int j = 0; j < ST_SPI; ++j) d0[j] = d1[j] = 0.f;
+    for (int j = 0; j < NSL; ++j) d0[j] = d1[j] = 0.f;
 #pragma unroll
     for (int ch = 0; ch < 4; ++ch) {
 #pragma unroll
-      for (int j = 0; j < ST_SPI; ++j) {
+      for (int j = 0; j < NSL; ++j) {
         float e[4];
         fp8_chunk_dot(W[j][ch], X[j][ch], e);
         d0[j] += e[0];
@@ -448,8 +467,8 @@ __device__ void gemv_phase(Consumer& c, const GemvPhase<EPI, SCALE, NG>& ph) {
       }
     }
 #pragma unroll
-    for (int j = 0; j < ST_SPI; ++j) {
-      if (j < ns && q[j] < r.s1) {
+    for (int j = 0; j < NSL; ++j) {
+      if (j / ST_SPW < ns && q[j] < r.s1) {
         const int gi = q[j] - tl[j] * NG;                       // sub-matrix of the slice (0 for NG == 1)
         const int u = un[j];
         const bool in = u * spu >= r.s0;                        // this CTA folds u: keep its dots here
@@ -603,14 +622,10 @@ __device__ void attention_phase(Consumer& c, const StepLayer& L, int pos) {
     const bool owns_new = (split == it.n_splits - 1);
     const int jn = pos - j0;
     const int sk = c.n % ST_NSTAGE;
-    const bool okk = c.wait_stage(sk);
+    if (!c.wait_stage(sk)) atomicOr(&g_dev_error, DEVERR_MBAR_TIMEOUT);
     ++c.n;
-    const int sv = c.n % ST_NSTAGE;
-    const bool okv = c.wait_stage(sv);
-    ++c.n;
-    if (!(okk && okv)) atomicOr(&g_dev_error, DEVERR_MBAR_TIMEOUT);
     const bf16* Ks = reinterpret_cast<const bf16*>(sm.ring[sk]);
-    const bf16* Vs = reinterpret_cast<const bf16*>(sm.ring[sv]);
+    const bf16* Vs = reinterpret_cast<const bf16*>(sm.ring[sk] + ST_STAGE / 2);
     if (warp < 4 && kvh != q_kvh) {   // q of the 4 heads of this kv head (warp = head)
       const uint2 raw = ldcg_u2(p.qkv + (kvh * GQA + warp) * HEAD_DIM + lane * 4);
       const bf16* e = reinterpret_cast<const bf16*>(&raw);
@@ -698,7 +713,6 @@ __device__ void attention_phase(Consumer& c, const StepLayer& L, int pos) {
       }
     }
     c.release_stage(sk);
-    c.release_stage(sv);
     consumer_sync();
   }
 }
@@ -781,8 +795,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) decode_step_kernel(const __grid
           const int kvh = item / it.n_splits, split = item - kvh * it.n_splits;
           const int j0 = split * ST_CHUNK, nj = min(ST_CHUNK, pos + 1 - j0);
           const size_t off = ((size_t)kvh * p.max_seq + j0) * HEAD_DIM;
-          pr.push(L.k_cache + off, (uint32_t)(nj * HEAD_DIM * 2));
-          pr.push(L.v_cache + off, (uint32_t)(nj * HEAD_DIM * 2));
+          pr.push_kv(L.k_cache + off, L.v_cache + off, (uint32_t)(nj * HEAD_DIM * 2));
         }
         step_stamp(p, 5 * l + 2, 3);
         step_put(p, 5 * l + 2, 6, pr.wait_cycles);
