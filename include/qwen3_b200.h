@@ -134,7 +134,6 @@ typedef struct {
   const void *w_qkv, *w_o, *w_gu, *w_down;       /* packed fp8 (model.pack_fp8; gate|up interleaved) */
   const float *s_qkv, *s_o, *s_gu, *s_down;      /* scales, layout per scale_mode */
   const void *ln1, *ln2, *q_norm, *k_norm;       /* bf16 */
-  void *k_cache, *v_cache;                       /* bf16 [8][max_seq][128] of this layer */
 } qk_layer_t;
 
 /*
@@ -143,6 +142,8 @@ typedef struct {
  * reference's 183-launch `Engine.decode_step` (generate.py:102-119) with bit-identical results; the ops it
  * fuses are the entry points above. Cooperative launch of one CTA per SM (graph-capturable).
  *   layers      DEVICE array of n_layers qk_layer_t
+ *   k_cache/v_cache  bf16 KV caches of all layers: layer l at byte offset l * kv_layer_stride, each
+ *               [8][max_seq][128] (16-byte aligned, stride a multiple of 16); read through TMA tensor maps
  *   state       [pos, step]; token [1]; out_tokens [out_len]; best u64 [1] zero before the first launch
  *   resid/qkv/attn/h/logits  bf16 activations [4096]/[6144]/[4096]/[12288]/[vocab]
  *   part        fp32 scratch of part_floats >= qk_decode_step_part_floats(vocab) floats; counters int
@@ -156,12 +157,13 @@ typedef struct {
  *               first load; then cumulative clock64 cycles: 4 consumer warp 0 waiting for data, 5 consumer
  *               warp 0 folding units, 6 producer waiting for free ring stages.
  */
-int qk_decode_step(const qk_layer_t* layers, int n_layers, const void* embed, const void* final_norm,
-                   const void* w_head, const float* s_head, int vocab, const void* cos_tab, const void* sin_tab,
-                   int* token, int* state, int* out_tokens, int out_len, unsigned long long* best, void* resid,
-                   void* qkv, void* attn, void* h, void* logits, float* part, long long part_floats, int* counters,
-                   int n_counters, float* o_part, float* ml_part, int* attn_counters, unsigned* sync, int max_seq,
-                   int max_splits, float eps, int scale_mode, uint64_t* timeline, qk_stream_t stream);
+int qk_decode_step(const qk_layer_t* layers, int n_layers, void* k_cache, void* v_cache, long long kv_layer_stride,
+                   const void* embed, const void* final_norm, const void* w_head, const float* s_head, int vocab,
+                   const void* cos_tab, const void* sin_tab, int* token, int* state, int* out_tokens, int out_len,
+                   unsigned long long* best, void* resid, void* qkv, void* attn, void* h, void* logits, float* part,
+                   long long part_floats, int* counters, int n_counters, float* o_part, float* ml_part,
+                   int* attn_counters, unsigned* sync, int max_seq, int max_splits, float eps, int scale_mode,
+                   uint64_t* timeline, qk_stream_t stream);
 
 /* Minimum scratch sizes of qk_decode_step for a vocabulary size (no GPU needed). */
 long long qk_decode_step_part_floats(int vocab);

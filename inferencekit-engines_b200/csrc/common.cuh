@@ -38,6 +38,9 @@ __device__ int g_timeline_slots = 0;
 constexpr unsigned long long WAIT_LIMIT_NS = 2000000000ull;
 
 __device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+// The low / high bf16 of a 32-bit word as f32 (exact: a bf16 is the high half of an f32).
+__device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
@@ -108,7 +111,6 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Wait for phase `parity` of an mbarrier, at most `limit_ns`; on timeout set the device error word.
 // Non-blocking: has the phase with this parity completed? (acquire, like try_wait)
 __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
@@ -122,6 +124,7 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Wait for phase `parity` of an mbarrier, at most `limit_ns`; on timeout set the device error word.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned long long limit_ns = WAIT_LIMIT_NS) {
   if (mbar_try_wait(bar, parity)) return true;
   // Short waits poll only the barrier (clock64 is a local register); after ~0.25 ms the loop also checks
@@ -166,6 +169,21 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
                : "memory");
 }
 
+// Tiled TMA load of one box of a 4-D tensor map into shared memory (no multicast), completion counted on an
+// mbarrier in transaction bytes. x (innermost) * element size must be a multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_4d(void* dst, const void* tmap, int x, int y, int z, int w, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+      "[%6];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ uint4 lds128_at(uint32_t a) {   // a: shared-memory address
+  uint4 r;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(a));
+  return r;
+}
 __device__ __forceinline__ uint4 lds128(const void* p) {
   uint4 r;
   asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(smem_u32(p)));

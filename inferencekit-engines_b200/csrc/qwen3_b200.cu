@@ -1,5 +1,7 @@
 // C ABI of the B200 decode kernels: argument checks, launch shapes, PDL launches. One translation unit so
 // the device symbols (error word) are shared by every kernel without relocatable device code.
+#include <cudaTypedefs.h>   // PFN_cuTensorMapEncodeTiled
+
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -33,6 +35,36 @@ int fail(int code, const char* fmt, ...) {
 }
 int cuda_fail(cudaError_t e, const char* what) {
   return fail(QK_ECUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+// cuTensorMapEncodeTiled from the driver, looked up once through the runtime (no link against libcuda).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  return fn;
+}
+
+// TMA map of a whole-model K or V cache: bf16 {128 dims, max_seq keys, 8 kv heads, n_layers}, box {64, 64, 1, 1}
+// (8 KiB), 128-byte swizzle, out-of-range rows zero-filled.
+int encode_kv_map(CUtensorMap* map, void* base, int max_seq, int n_layers, long long layer_stride_bytes) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return fail(QK_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  const cuuint64_t dims[4] = {HEAD_DIM, (cuuint64_t)max_seq, 8, (cuuint64_t)n_layers};
+  const cuuint64_t strides[3] = {HEAD_DIM * 2, (cuuint64_t)max_seq * HEAD_DIM * 2, (cuuint64_t)layer_stride_bytes};
+  const cuuint32_t box[4] = {64, 64, 1, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, base, dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(QK_EINVAL, "cuTensorMapEncodeTiled failed for the KV cache (CUresult %d)", (int)r);
+  return QK_OK;
 }
 
 int device_sms() {
@@ -313,16 +345,22 @@ int qk_decode_step_counters(int vocab) {
   return head > 768 ? head : 768;
 }
 
-int qk_decode_step(const qk_layer_t* layers, int n_layers, const void* embed, const void* final_norm,
-                   const void* w_head, const float* s_head, int vocab, const void* cos_tab, const void* sin_tab,
-                   int* token, int* state, int* out_tokens, int out_len, unsigned long long* best, void* resid,
-                   void* qkv, void* attn, void* h, void* logits, float* part, long long part_floats, int* counters,
-                   int n_counters, float* o_part, float* ml_part, int* attn_counters, unsigned* sync, int max_seq,
-                   int max_splits, float eps, int scale_mode, uint64_t* timeline, qk_stream_t stream) {
-  if (!layers || n_layers < 1 || !embed || !final_norm || !w_head || !s_head || !cos_tab || !sin_tab || !token ||
-      !state || !out_tokens || !best || !resid || !qkv || !attn || !h || !logits || !part || !counters || !o_part ||
-      !ml_part || !attn_counters || !sync)
+int qk_decode_step(const qk_layer_t* layers, int n_layers, void* k_cache, void* v_cache, long long kv_layer_stride,
+                   const void* embed, const void* final_norm, const void* w_head, const float* s_head, int vocab,
+                   const void* cos_tab, const void* sin_tab, int* token, int* state, int* out_tokens, int out_len,
+                   unsigned long long* best, void* resid, void* qkv, void* attn, void* h, void* logits, float* part,
+                   long long part_floats, int* counters, int n_counters, float* o_part, float* ml_part,
+                   int* attn_counters, unsigned* sync, int max_seq, int max_splits, float eps, int scale_mode,
+                   uint64_t* timeline, qk_stream_t stream) {
+  if (!layers || n_layers < 1 || !k_cache || !v_cache || !embed || !final_norm || !w_head || !s_head || !cos_tab ||
+      !sin_tab || !token || !state || !out_tokens || !best || !resid || !qkv || !attn || !h || !logits || !part ||
+      !counters || !o_part || !ml_part || !attn_counters || !sync)
     return fail(QK_EINVAL, "null pointer argument");
+  if (max_seq < 1) return fail(QK_EINVAL, "bad max_seq");
+  if (!aligned(k_cache, 16) || !aligned(v_cache, 16) || kv_layer_stride % 16 ||
+      kv_layer_stride < 8LL * max_seq * HEAD_DIM * 2)
+    return fail(QK_EINVAL, "KV caches must be 16-byte aligned with a layer stride (bytes) that is a multiple of 16 "
+                           "and at least 8 * max_seq * 256");
   if (vocab <= 0 || vocab % 16 || out_len < 1 || max_seq < 1) return fail(QK_EINVAL, "bad vocab/out_len/max_seq");
   if (part_floats < qk_decode_step_part_floats(vocab) || n_counters < qk_decode_step_counters(vocab))
     return fail(QK_EINVAL, "scratch too small: part needs %lld floats, counters %d ints",
@@ -331,6 +369,11 @@ int qk_decode_step(const qk_layer_t* layers, int n_layers, const void* embed, co
     return fail(QK_EINVAL, "max_splits must cover max_seq/64 and be at most %d", ST_MAX_SPLITS);
   if (scale_mode != QK_SCALE_BLOCK128 && scale_mode != QK_SCALE_CHANNEL) return fail(QK_EINVAL, "bad scale_mode");
   StepParams p = {};
+  if (int r = encode_kv_map(&p.tm_k, k_cache, max_seq, n_layers, kv_layer_stride)) return r;
+  if (int r = encode_kv_map(&p.tm_v, v_cache, max_seq, n_layers, kv_layer_stride)) return r;
+  p.k_cache = static_cast<bf16*>(k_cache);
+  p.v_cache = static_cast<bf16*>(v_cache);
+  p.kv_layer_elems = kv_layer_stride / 2;
   p.layers = reinterpret_cast<const StepLayer*>(layers);
   p.n_layers = n_layers;
   p.embed = static_cast<const bf16*>(embed);

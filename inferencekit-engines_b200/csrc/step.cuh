@@ -23,6 +23,7 @@
 // All data written by one CTA and read by another in a later phase is read with ld.global.cg (L2), never
 // through L1, because L1 is not coherent across SMs.
 #pragma once
+#include <cuda.h>   // CUtensorMap
 #include "attention.cuh"
 #include "common.cuh"
 #include "gemv.cuh"
@@ -44,6 +45,7 @@ constexpr int ST_MAX_SPLITS = 1024;                // contexts up to 64k
 constexpr int ST_BD_FLOATS = 6144;
 constexpr int ST_MAX_SLOTS = 12;
 constexpr int ST_MERGE_SPLITS = 64;                // splits staged per round of the attention merge
+constexpr int ST_ABATCH = 4;                       // attention items processed together (<= ST_NSTAGE)
 #ifndef ST_SPI
 #define ST_SPI 1                                   // GEMV stages a consumer warp takes per iteration
 #endif
@@ -52,10 +54,20 @@ struct StepLayer {
   const uint8_t *w_qkv, *w_o, *w_gu, *w_down;      // model.pack_fp8 layout
   const float *s_qkv, *s_o, *s_gu, *s_down;        // scales (layout per the kernel's SCALE)
   const bf16 *ln1, *ln2, *q_norm, *k_norm;
-  bf16 *k_cache, *v_cache;                         // [n_kv][max_seq][128] of this layer
 };
 
+// K/V cache chunks reach shared memory through these TMA maps ({128 dims, max_seq, 8 kv heads, layers}, box
+// {64, 64, 1, 1}, 128-byte swizzle): a 64-key chunk is two 8 KiB boxes (dims 0-63, 64-127) of 64 rows x 128 B,
+// 16-byte chunk c of row r stored at chunk c ^ (r & 7), so eight keys read at the same dims hit eight
+// different bank groups.
+__device__ __forceinline__ uint32_t kv_swz(int r, int d) {   // byte offset of (row r, dim d) in a chunk
+  return (uint32_t)((d >> 6) * 8192 + r * 128 + ((((d & 63) >> 3) ^ (r & 7)) << 4) + (d & 7) * 2);
+}
+
 struct StepParams {
+  CUtensorMap tm_k, tm_v;                          // see kv_swz
+  bf16 *k_cache, *v_cache;                         // layer l: + l * kv_layer_elems, [8][max_seq][128]
+  long long kv_layer_elems;
   const StepLayer* layers;                         // device array [n_layers]
   int n_layers;
   const bf16* embed;                               // [vocab][4096]
@@ -102,9 +114,9 @@ struct StepSmem {
     float bd[ST_BD_FLOATS];                        // block dots of the 16-row units in flight (slots)
     bf16 xs[HIDDEN];                               // raw x during an RMSNorm prologue
     struct {
-      float qs[GQA][HEAD_DIM + 4];                 // +4: conflict-free reads by 4 heads at once
-      float sc[GQA][ST_CHUNK];
-      float m_s[GQA], l_s[GQA];
+      float qs[ST_ABATCH][GQA][HEAD_DIM + 4];      // q per kv head of the batch; +4: 4 heads read conflict-free
+      float sc[ST_ABATCH][GQA][ST_CHUNK];          // scores, then probabilities, per item and query head
+      float m_s[ST_ABATCH][GQA], l_s[ST_ABATCH][GQA];
     } at;
     struct {
       float o[ST_MERGE_SPLITS * 64];               // partial outputs of up to 64 splits, 64 dims each
@@ -214,8 +226,9 @@ struct Producer {
     bulk_g2s(sm->ring[s], src, bytes, &sm->full[s], pol);
     ++n;
   }
-  // K and V chunks of one attention item into one stage (K in the first half, V in the second)
-  __device__ __forceinline__ void push_kv(const void* k, const void* v, uint32_t bytes) {
+  // K and V chunk (keys j0..j0+63 of kv head kvh, layer l) of one attention item into one stage: K in the first
+  // half, V in the second, each as two swizzled 8 KiB boxes (rows past the cache end are zero-filled)
+  __device__ __forceinline__ void push_kv(const StepParams& p, int l, int kvh, int j0) {
     if (!ok) return;
     const int s = n % ST_NSTAGE;
     const long long t0 = clock64();
@@ -224,9 +237,11 @@ struct Producer {
       return;
     }
     wait_cycles += clock64() - t0;
-    mbar_arrive_expect_tx(&sm->full[s], 2 * bytes);
-    bulk_g2s(sm->ring[s], k, bytes, &sm->full[s], pol);
-    bulk_g2s(sm->ring[s] + ST_STAGE / 2, v, bytes, &sm->full[s], pol);
+    mbar_arrive_expect_tx(&sm->full[s], ST_STAGE);
+    tma_load_4d(sm->ring[s], &p.tm_k, 0, j0, kvh, l, &sm->full[s]);
+    tma_load_4d(sm->ring[s] + 8192, &p.tm_k, 64, j0, kvh, l, &sm->full[s]);
+    tma_load_4d(sm->ring[s] + 16384, &p.tm_v, 0, j0, kvh, l, &sm->full[s]);
+    tma_load_4d(sm->ring[s] + 24576, &p.tm_v, 64, j0, kvh, l, &sm->full[s]);
     ++n;
   }
   __device__ __forceinline__ void gemv(const uint8_t* w, int n_slices) {
@@ -605,114 +620,186 @@ __device__ __forceinline__ void norm_rope_regs(float (&v)[4], const bf16* nw, co
 }
 
 // Attention items (kv head, 64-key split) of this CTA: partial (m, l, o) per query head into o_part/ml_part.
-// The item owning position `pos` appends the new K/V row. Query heads are normalised once per kv head.
-__device__ void attention_phase(Consumer& c, const StepLayer& L, int pos) {
+// The item owning position `pos` appends the new K/V row. Items go in batches of up to ST_ABATCH (one ring
+// stage each) so that every thread carries independent dot chains of several items: scores with thread =
+// (key, query head) over all items of the batch, softmax with one warp per (item, head) row, P @ V with two
+// warps per item and thread = (2 dims, 4 heads). Every sum keeps the reference's order.
+__device__ void attention_phase(Consumer& c, const StepLayer& L, int l, int pos) {
   StepSmem& sm = *c.sm;
   const StepParams& p = *c.p;
   const int tid = threadIdx.x, lane = c.lane, warp = c.warp;
   constexpr int NKV = 8, NQ = 32;
   const AttnItems it = attn_items(pos, NKV);
   const int ctx = pos + 1;
+  const int last_split = it.n_splits - 1;
   const bf16* cos_row = p.cos_tab + (size_t)pos * HEAD_DIM;
   const bf16* sin_row = p.sin_tab + (size_t)pos * HEAD_DIM;
-  int q_kvh = -1;
-  for (int item = it.i0; item < it.i1; ++item) {
-    const int kvh = item / it.n_splits, split = item - kvh * it.n_splits;
-    const int j0 = split * ST_CHUNK, nj = min(ST_CHUNK, ctx - j0);
-    const bool owns_new = (split == it.n_splits - 1);
-    const int jn = pos - j0;
-    const int sk = c.n % ST_NSTAGE;
-    if (!c.wait_stage(sk)) atomicOr(&g_dev_error, DEVERR_MBAR_TIMEOUT);
-    ++c.n;
-    const bf16* Ks = reinterpret_cast<const bf16*>(sm.ring[sk]);
-    const bf16* Vs = reinterpret_cast<const bf16*>(sm.ring[sk] + ST_STAGE / 2);
-    if (warp < 4 && kvh != q_kvh) {   // q of the 4 heads of this kv head (warp = head)
-      const uint2 raw = ldcg_u2(p.qkv + (kvh * GQA + warp) * HEAD_DIM + lane * 4);
-      const bf16* e = reinterpret_cast<const bf16*>(&raw);
-      float v[4] = {__bfloat162float(e[0]), __bfloat162float(e[1]), __bfloat162float(e[2]), __bfloat162float(e[3])};
-      float o[4];
-      norm_rope_regs(v, L.q_norm, cos_row, sin_row, lane, p.eps, o);
+  bf16* k_cache = p.k_cache + (size_t)l * p.kv_layer_elems;
+  bf16* v_cache = p.v_cache + (size_t)l * p.kv_layer_elems;
+  for (int b0 = it.i0; b0 < it.i1; b0 += ST_ABATCH) {
+    const int nb = min(ST_ABATCH, it.i1 - b0);
+    const int kv0 = b0 / it.n_splits, nkv = (b0 + nb - 1) / it.n_splits - kv0 + 1;   // kv heads in the batch
+    bool ok = true;
+    for (int k = 0; k < nb; ++k) ok = c.wait_abs(c.n + k) && ok;
+    if (!ok) atomicOr(&g_dev_error, DEVERR_MBAR_TIMEOUT);
+    auto stage = [&](int k) { return sm.ring[(c.n + k) % ST_NSTAGE]; };
+    // setup tasks, one warp each: q of every query head of the batch's kv heads (RMSNorm + RoPE), and the new
+    // K row (RMSNorm + RoPE) and V row of every kv head whose last split is in the batch
+    const int n_tasks = 4 * nkv + 2 * nkv;
+    for (int t = warp; t < n_tasks; t += ST_WARPS) {
+      if (t < 4 * nkv) {
+        const int slot = t >> 2, qh = t & 3;
+        const uint2 raw = ldcg_u2(p.qkv + ((kv0 + slot) * GQA + qh) * HEAD_DIM + lane * 4);
+        const bf16* e = reinterpret_cast<const bf16*>(&raw);
+        float v[4] = {__bfloat162float(e[0]), __bfloat162float(e[1]), __bfloat162float(e[2]), __bfloat162float(e[3])};
+        float o[4];
+        norm_rope_regs(v, L.q_norm, cos_row, sin_row, lane, p.eps, o);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) sm.u.at.qs[warp][lane * 4 + j] = bf16r(o[j]);
-    } else if (owns_new && warp == 4) {
-      const uint2 raw = ldcg_u2(p.qkv + (NQ + kvh) * HEAD_DIM + lane * 4);
-      const bf16* e = reinterpret_cast<const bf16*>(&raw);
-      float v[4] = {__bfloat162float(e[0]), __bfloat162float(e[1]), __bfloat162float(e[2]), __bfloat162float(e[3])};
-      float o[4];
-      norm_rope_regs(v, L.k_norm, cos_row, sin_row, lane, p.eps, o);
-      bf16* dst = L.k_cache + ((size_t)kvh * p.max_seq + pos) * HEAD_DIM + lane * 4;
-      bf16* sdst = const_cast<bf16*>(Ks) + jn * HEAD_DIM + lane * 4;
+        for (int j = 0; j < 4; ++j) sm.u.at.qs[slot][qh][lane * 4 + j] = bf16r(o[j]);
+      } else {
+        const int kvh = kv0 + ((t - 4 * nkv) >> 1), is_v = (t - 4 * nkv) & 1;
+        const int k = kvh * it.n_splits + last_split - b0;     // batch index of the item owning pos
+        if (k < 0 || k >= nb) continue;
+        const int jn = pos - last_split * ST_CHUNK;
+        uint8_t* st = stage(k) + (is_v ? ST_STAGE / 2 : 0);
+        if (!is_v) {
+          const uint2 raw = ldcg_u2(p.qkv + (NQ + kvh) * HEAD_DIM + lane * 4);
+          const bf16* e = reinterpret_cast<const bf16*>(&raw);
+          float v[4] = {__bfloat162float(e[0]), __bfloat162float(e[1]), __bfloat162float(e[2]), __bfloat162float(e[3])};
+          float o[4];
+          norm_rope_regs(v, L.k_norm, cos_row, sin_row, lane, p.eps, o);
+          bf16* dst = k_cache + ((size_t)kvh * p.max_seq + pos) * HEAD_DIM + lane * 4;
+          bf16* sdst = reinterpret_cast<bf16*>(st + kv_swz(jn, lane * 4));
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        dst[j] = __float2bfloat16_rn(o[j]);
-        sdst[j] = __float2bfloat16_rn(o[j]);
+          for (int j = 0; j < 4; ++j) {
+            dst[j] = __float2bfloat16_rn(o[j]);
+            sdst[j] = __float2bfloat16_rn(o[j]);
+          }
+        } else {
+          const uint2 raw = ldcg_u2(p.qkv + (NQ + NKV + kvh) * HEAD_DIM + lane * 4);
+          *reinterpret_cast<uint2*>(v_cache + ((size_t)kvh * p.max_seq + pos) * HEAD_DIM + lane * 4) = raw;
+          *reinterpret_cast<uint2*>(st + kv_swz(jn, lane * 4)) = raw;
+        }
+        fence_proxy_async_smem();   // this stage is refilled by TMA (async proxy) after its release
       }
-    } else if (owns_new && warp == 5) {
-      const uint2 raw = ldcg_u2(p.qkv + (NQ + NKV + kvh) * HEAD_DIM + lane * 4);
-      *reinterpret_cast<uint2*>(L.v_cache + ((size_t)kvh * p.max_seq + pos) * HEAD_DIM + lane * 4) = raw;
-      *reinterpret_cast<uint2*>(const_cast<bf16*>(Vs) + jn * HEAD_DIM + lane * 4) = raw;
     }
-    q_kvh = kvh;
     consumer_sync();
-    // scores: thread (key j = tid/4, head h = tid%4): dims 0..63 then 64..127, each summed in order
+    // scores: thread (key j = tid / 4, head hh = tid % 4), every item of the batch: dims 0..63 and 64..127 each
+    // summed in order, then added. Items past the batch recompute the last one and store nothing.
     {
       const int j = tid >> 2, hh = tid & 3;
-      float sfin = -INFINITY;
-      if (j < nj) {
-        float part[2];
+      float dot[ST_ABATCH][2];
+      uint32_t ks[ST_ABATCH], qrow[ST_ABATCH];        // shared-memory addresses
 #pragma unroll
-        for (int sl = 0; sl < 2; ++sl) {
-          float dot = 0.f;
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const uint4 kv = lds128(Ks + j * HEAD_DIM + sl * 64 + i * 8);
-            const bf16* e = reinterpret_cast<const bf16*>(&kv);
-#pragma unroll
-            for (int jj = 0; jj < 8; ++jj) dot += sm.u.at.qs[hh][sl * 64 + i * 8 + jj] * __bfloat162float(e[jj]);
-          }
-          part[sl] = dot;
-        }
-        float s = part[0];
-        s += part[1];
-        sfin = s * p.attn_scale;
+      for (int k = 0; k < ST_ABATCH; ++k) {
+        const int kk = min(k, nb - 1);
+        ks[k] = smem_u32(stage(kk));
+        qrow[k] = smem_u32(sm.u.at.qs[(b0 + kk) / it.n_splits - kv0][hh]);
+        dot[k][0] = dot[k][1] = 0.f;
       }
-      sm.u.at.sc[hh][j] = sfin;
+#pragma unroll
+      for (int sl = 0; sl < 2; ++sl) {
+#pragma unroll 1
+        for (int i = 0; i < 8; ++i) {
+          const uint32_t ko = kv_swz(j, sl * 64 + i * 8), qo = (sl * 64 + i * 8) * 4;
+#pragma unroll
+          for (int k = 0; k < ST_ABATCH; ++k) {
+            const uint4 kv = lds128_at(ks[k] + ko);
+            const uint4 qa = lds128_at(qrow[k] + qo);
+            const uint4 qb = lds128_at(qrow[k] + qo + 16);
+            // dims in order: the low then the high bf16 of each 32-bit word (exact bf16 -> f32)
+            float& dt = dot[k][sl];
+            dt += __uint_as_float(qa.x) * bf16lo(kv.x);
+            dt += __uint_as_float(qa.y) * bf16hi(kv.x);
+            dt += __uint_as_float(qa.z) * bf16lo(kv.y);
+            dt += __uint_as_float(qa.w) * bf16hi(kv.y);
+            dt += __uint_as_float(qb.x) * bf16lo(kv.z);
+            dt += __uint_as_float(qb.y) * bf16hi(kv.z);
+            dt += __uint_as_float(qb.z) * bf16lo(kv.w);
+            dt += __uint_as_float(qb.w) * bf16hi(kv.w);
+          }
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < ST_ABATCH; ++k) {
+        if (k < nb) {
+          const int split = (b0 + k) % it.n_splits;
+          const int nj = min(ST_CHUNK, ctx - split * ST_CHUNK);
+          float sc = dot[k][0];
+          sc += dot[k][1];
+          sm.u.at.sc[k][hh][j] = j < nj ? sc * p.attn_scale : -INFINITY;
+        }
+      }
     }
     consumer_sync();
-    if (warp < 4) {  // softmax over the chunk, one warp per query head
+    // softmax over each (item, head) row, one warp per row
+    for (int r = warp; r < nb * GQA; r += ST_WARPS) {
+      float* row = sm.u.at.sc[r >> 2][r & 3];
       float pr[2];
       float m = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < 2; ++i) { pr[i] = sm.u.at.sc[warp][lane + 32 * i]; m = fmaxf(m, pr[i]); }
+      for (int i = 0; i < 2; ++i) { pr[i] = row[lane + 32 * i]; m = fmaxf(m, pr[i]); }
       m = warp_max(m);
-      float l = 0.f;
+      float lsum = 0.f;
 #pragma unroll
-      for (int i = 0; i < 2; ++i) { pr[i] = expf(pr[i] - m); l += pr[i]; sm.u.at.sc[warp][lane + 32 * i] = pr[i]; }
-      l = warp_sum(l);
-      if (lane == 0) { sm.u.at.m_s[warp] = m; sm.u.at.l_s[warp] = l; }
+      for (int i = 0; i < 2; ++i) { pr[i] = expf(pr[i] - m); lsum += pr[i]; row[lane + 32 * i] = pr[i]; }
+      lsum = warp_sum(lsum);
+      if (lane == 0) { sm.u.at.m_s[r >> 2][r & 3] = m; sm.u.at.l_s[r >> 2][r & 3] = lsum; }
     }
     consumer_sync();
-    // P @ V: thread (d = tid % 128, heads 2*(tid/128) + {0,1})
-    {
-      const int d = tid & 127, h0 = (tid >> 7) * 2;
-      float acc0 = 0.f, acc1 = 0.f;
-      for (int j = 0; j < nj; ++j) {
-        const float vf = __bfloat162float(Vs[j * HEAD_DIM + d]);
-        acc0 += sm.u.at.sc[h0][j] * vf;
-        acc1 += sm.u.at.sc[h0 + 1][j] * vf;
+    // P @ V: warps 2k, 2k+1 take item k; thread = dims d, d + 1 of all 4 heads; each output sums over the keys
+    // in order (the reference's sequential loop). Keys go in groups of 8, for which the swizzled offsets of
+    // this thread's dims are fixed (they depend on key & 7 only).
+    if ((warp >> 1) < nb) {
+      const int k = warp >> 1, item = b0 + k;
+      const int kvh = item / it.n_splits, split = item - kvh * it.n_splits;
+      const int nj = min(ST_CHUNK, ctx - split * ST_CHUNK);
+      const int d = ((warp & 1) * 32 + lane) * 2;
+      const uint8_t* Vs = stage(k) + ST_STAGE / 2;
+      uint32_t off[8];
+#pragma unroll
+      for (int r = 0; r < 8; ++r) off[r] = kv_swz(r, d);
+      float acc[GQA][2];
+#pragma unroll
+      for (int h = 0; h < GQA; ++h) acc[h][0] = acc[h][1] = 0.f;
+      const int n8 = nj >> 3;
+      for (int t = 0; t < n8; ++t) {
+        uint32_t v2[8];
+#pragma unroll
+        for (int r = 0; r < 8; ++r) v2[r] = *reinterpret_cast<const uint32_t*>(Vs + t * 1024 + off[r]);
+#pragma unroll
+        for (int h = 0; h < GQA; ++h) {
+          const float4 pa = *reinterpret_cast<const float4*>(&sm.u.at.sc[k][h][t * 8]);
+          const float4 pb = *reinterpret_cast<const float4*>(&sm.u.at.sc[k][h][t * 8 + 4]);
+          const float pj[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
+#pragma unroll
+          for (int r = 0; r < 8; ++r) {
+            acc[h][0] += pj[r] * bf16lo(v2[r]);
+            acc[h][1] += pj[r] * bf16hi(v2[r]);
+          }
+        }
       }
-      const size_t row0 = (size_t)(kvh * GQA + h0) * p.max_splits + split;
-      const size_t row1 = row0 + p.max_splits;
-      p.o_part[row0 * HEAD_DIM + d] = acc0;
-      p.o_part[row1 * HEAD_DIM + d] = acc1;
-      if (d == 0) {
-        p.ml_part[row0 * 2 + 0] = sm.u.at.m_s[h0];
-        p.ml_part[row0 * 2 + 1] = sm.u.at.l_s[h0];
-        p.ml_part[row1 * 2 + 0] = sm.u.at.m_s[h0 + 1];
-        p.ml_part[row1 * 2 + 1] = sm.u.at.l_s[h0 + 1];
+      for (int j = n8 * 8; j < nj; ++j) {
+        const uint32_t v2 = *reinterpret_cast<const uint32_t*>(Vs + kv_swz(j, d));
+#pragma unroll
+        for (int h = 0; h < GQA; ++h) {
+          const float pj = sm.u.at.sc[k][h][j];
+          acc[h][0] += pj * bf16lo(v2);
+          acc[h][1] += pj * bf16hi(v2);
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < GQA; ++h) {
+        const size_t row = (size_t)(kvh * GQA + h) * p.max_splits + split;
+        *reinterpret_cast<float2*>(p.o_part + row * HEAD_DIM + d) = make_float2(acc[h][0], acc[h][1]);
+        if (d == 0) {
+          p.ml_part[row * 2 + 0] = sm.u.at.m_s[k][h];
+          p.ml_part[row * 2 + 1] = sm.u.at.l_s[k][h];
+        }
       }
     }
-    c.release_stage(sk);
+    for (int k = 0; k < nb; ++k) c.release_stage((c.n + k) % ST_NSTAGE);
+    c.n += nb;
     consumer_sync();
   }
 }
@@ -793,9 +880,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) decode_step_kernel(const __grid
         step_put(p, 5 * l + 1, 6, pr.wait_cycles);
         for (int item = it.i0; item < it.i1; ++item) {
           const int kvh = item / it.n_splits, split = item - kvh * it.n_splits;
-          const int j0 = split * ST_CHUNK, nj = min(ST_CHUNK, pos + 1 - j0);
-          const size_t off = ((size_t)kvh * p.max_seq + j0) * HEAD_DIM;
-          pr.push_kv(L.k_cache + off, L.v_cache + off, (uint32_t)(nj * HEAD_DIM * 2));
+          pr.push_kv(p, l, kvh, split * ST_CHUNK);
         }
         step_stamp(p, 5 * l + 2, 3);
         step_put(p, 5 * l + 2, 6, pr.wait_cycles);
@@ -834,7 +919,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) decode_step_kernel(const __grid
     grid_barrier(p.sync, nbar++);
     // ATTN: split partials (and the K/V rows at pos), then the merge into the attention output
     if (tl) step_stamp(p, ph + 1, 0);
-    attention_phase(c, L, pos);
+    attention_phase(c, L, l, pos);
     if (tl) step_stamp(p, ph + 1, 7);
     grid_barrier(p.sync, nbar++);
     if (tl) step_stamp(p, ph + 1, 1);

@@ -71,8 +71,7 @@ class Engine:
                 ptrs.append([L.qkv.packed.data_ptr(), L.o.packed.data_ptr(), L.gu.packed.data_ptr(),
                              L.down.packed.data_ptr(), L.qkv.scale.data_ptr(), L.o.scale.data_ptr(),
                              L.gu.scale.data_ptr(), L.down.scale.data_ptr(), L.ln1.data_ptr(), L.ln2.data_ptr(),
-                             L.q_norm.data_ptr(), L.k_norm.data_ptr(), m.k_cache[li, 0].data_ptr(),
-                             m.v_cache[li, 0].data_ptr()])
+                             L.q_norm.data_ptr(), L.k_norm.data_ptr()])
             self.layer_table = torch.tensor(ptrs, dtype=torch.int64, device=dev)
             lib = self.k.lib
             self.part = torch.empty(lib.qk_decode_step_part_floats(cfg.vocab), dtype=torch.float32, device=dev)
@@ -95,10 +94,11 @@ class Engine:
         """Launch one decode step (eager). Also what gets captured into the graph."""
         m, k, cfg = self.m, self.k, self.m.cfg
         if self.fused:
-            k.decode_step(self.layer_table, len(m.layers), m.embed, m.norm, m.lm_head.packed, m.lm_head.scale, m.cos,
-                          m.sin, self.token, self.state, self.out_tokens, self.best, self.resid, self.qkv, self.attn,
-                          self.h, self.logits, self.part, self.gemv_counters, self.o_part, self.ml_part,
-                          self.counters, self.sync, m.max_seq, cfg.eps, self.scale_mode, self.step_timeline)
+            k.decode_step(self.layer_table, len(m.layers), m.k_cache, m.v_cache, m.embed, m.norm, m.lm_head.packed,
+                          m.lm_head.scale, m.cos, m.sin, self.token, self.state, self.out_tokens, self.best,
+                          self.resid, self.qkv, self.attn, self.h, self.logits, self.part, self.gemv_counters,
+                          self.o_part, self.ml_part, self.counters, self.sync, m.max_seq, cfg.eps, self.scale_mode,
+                          self.step_timeline)
             return
         k.embed(self.token, m.embed, self.resid)
         for li, L in enumerate(m.layers):

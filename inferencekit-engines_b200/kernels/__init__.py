@@ -43,8 +43,9 @@ _SIGS = {
     "qk_attention": ([_VP] * 12 + [_I, _I, _I, _I, _I, _I, _F, _F, _I, _VP], _I),
     "qk_lm_head_argmax": ([_VP, _VP, _I, _VP, _VP, _VP, _VP, _I, _I, _F, _VP, _VP, _I, _VP], _I),
     "qk_embed": ([_VP, _VP, _VP, _I, _I, _VP], _I),
-    "qk_decode_step": ([_VP, _I, _VP, _VP, _VP, _VP, _I, _VP, _VP, _VP, _VP, _VP, _I, _VP, _VP, _VP, _VP, _VP, _VP,
-                        _VP, ctypes.c_longlong, _VP, _I, _VP, _VP, _VP, _VP, _I, _I, _F, _I, _VP, _VP], _I),
+    "qk_decode_step": ([_VP, _I, _VP, _VP, ctypes.c_longlong, _VP, _VP, _VP, _VP, _I, _VP, _VP, _VP, _VP, _VP, _I,
+                        _VP, _VP, _VP, _VP, _VP, _VP, _VP, ctypes.c_longlong, _VP, _I, _VP, _VP, _VP, _VP, _I, _I,
+                        _F, _I, _VP, _VP], _I),
     "qk_decode_step_part_floats": ([_I], ctypes.c_longlong),
     "qk_decode_step_counters": ([_I], _I),
     "qk_fp8_gemv_noalloc": ([_I, _VP, _VP, _I, _VP, _VP, _VP, _VP, _VP, _I, _I, _F, _VP], _I),
@@ -162,13 +163,18 @@ class DecodeOps:
         self._check(st, "lm_head_argmax")
         self._tl("lm_head")
 
-    def decode_step(self, layer_table, n_layers, embed, final_norm, w_head, s_head, cos_tab, sin_tab, token, state,
-                    out_tokens, best, resid, qkv, attn, h, logits, part, counters, o_part, ml_part, attn_counters,
-                    sync, max_seq, eps, scale_mode, timeline=None):
+    def decode_step(self, layer_table, n_layers, k_cache, v_cache, embed, final_norm, w_head, s_head, cos_tab,
+                    sin_tab, token, state, out_tokens, best, resid, qkv, attn, h, logits, part, counters, o_part,
+                    ml_part, attn_counters, sync, max_seq, eps, scale_mode, timeline=None):
         """The fused decode step (qk_decode_step): one launch per token. layer_table: int64 CUDA tensor
-        [n_layers, 14] of device pointers in qk_layer_t order; timeline: optional int64 CUDA tensor of
-        #SMs * (5*n_layers + 1) * 4 words (layout in include/qwen3_b200.h)."""
-        st = self.lib.qk_decode_step(_p(layer_table), int(n_layers), _p(embed), _p(final_norm), _p(w_head),
+        [n_layers, 12] of device pointers in qk_layer_t order; k_cache/v_cache: bf16 [n_layers, 1, 8, max_seq, 128]
+        (a layer stride of any multiple of 16 bytes); timeline: optional int64 CUDA tensor of
+        #SMs * (5*n_layers + 1) * 8 words (layout in include/qwen3_b200.h)."""
+        if k_cache.stride() != v_cache.stride() or k_cache.shape[-2] != max_seq or k_cache.shape[-1] != 128:
+            raise ValueError("k_cache/v_cache must be [layers, 1, 8, max_seq, 128] with equal strides")
+        stride = k_cache.stride(0) * k_cache.element_size()
+        st = self.lib.qk_decode_step(_p(layer_table), int(n_layers), _p(k_cache), _p(v_cache), stride, _p(embed),
+                                     _p(final_norm), _p(w_head),
                                      _p(s_head), embed.shape[0], _p(cos_tab), _p(sin_tab), _p(token), _p(state),
                                      _p(out_tokens), out_tokens.numel(), _p(best), _p(resid), _p(qkv), _p(attn), _p(h),
                                      _p(logits), _p(part), part.numel(), _p(counters), counters.numel(), _p(o_part),
