@@ -13,8 +13,10 @@ replay stream, with a synchronize (and for N>1 a barrier) on both sides; max ove
 K steps through the public engine API with, every step, the input token copied from pinned host memory
 and the output token read back to pinned host memory (host-synchronous streaming decode).
 
-N > 1: tensor parallelism is not wired into this arm yet, so each rank decodes its own full replica
-(scaling "weak", no collective); rank 0 prints the aggregate.
+N > 1: tensor parallelism over the N GPUs (tp.py: Megatron-style shards, NCCL all-reduces of the fp32
+partials after o_proj and down, vocab-parallel lm_head), one process per GPU, the same 4k-context workload
+(scaling "strong": the job decodes one token stream; value = tokens/s of that stream). The step time is the
+max over ranks.
 
 --impl reference: the reference engine's CPU path (its `model.forward` math restated in oracle/, run on the
 host cores with all threads), one decoder layer per step at the same context plus the lm_head, reported as
@@ -235,11 +237,19 @@ def run_ours(args):
     start = max_seq - K
     assert start > 0, "--steps must be < 4096"
     cfg = M.Config()
-    m = M.Qwen3FP8Decode.synthetic(cfg, max_seq=max_seq, device=dev, seed=args.seed, scale_mode=args.scale,
-                                   head_dtype=args.head, norm_init="ones")
-    m.fill_cache_random(start, seed=1234 + rank)
-    fused = args.path == "fused"
-    eng = Engine(m, pdl=not args.no_pdl, attn_chunk=args.chunk, fused=fused)
+    if ws > 1:
+        import tp as TP
+        m = TP.synthetic_shard(cfg, ws, rank, max_seq=max_seq, device=dev, seed=args.seed, scale_mode=args.scale,
+                               head_dtype=args.head, norm_init="ones")
+        m.fill_cache_random(start, seed=1234 + rank)
+        fused = False
+        eng = TP.TPEngine(m, attn_chunk=args.chunk)
+    else:
+        m = M.Qwen3FP8Decode.synthetic(cfg, max_seq=max_seq, device=dev, seed=args.seed, scale_mode=args.scale,
+                                       head_dtype=args.head, norm_init="ones")
+        m.fill_cache_random(start, seed=1234 + rank)
+        fused = args.path == "fused"
+        eng = Engine(m, pdl=not args.no_pdl, attn_chunk=args.chunk, fused=fused)
     eng.token.fill_(1)
     eng.state.copy_(torch.tensor([start, 0], dtype=torch.int32))
     eng.capture()
@@ -295,8 +305,8 @@ def run_ours(args):
 
     peak, peak_src = peaks()
     bytes_tok, wb = step_bytes(m, start, max_seq - 1)
-    if fused:
-        # the step kernel is the whole step: its launch time is the timed region / K
+    if fused or ws > 1:
+        # fused: the step kernel is the whole step; TP: the rank's whole step (its shard's bytes)
         k_s, k_bytes, k_n = t / K, bytes_tok, K
     else:
         k_s, k_bytes, k_n = gate_up_kernel_timing(eng, reps=2)   # dominant kernel alone
@@ -306,10 +316,14 @@ def run_ours(args):
         tt = torch.tensor([t, t_e2e], dtype=torch.float64, device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         t, t_e2e = float(tt[0]), float(tt[1])
-    value = ws * K / t
+    value = K / t
     if rank == 0:
         achieved = k_bytes / k_s / 1e9
-        if fused:
+        if ws > 1:
+            kname = (f"one TP rank's step ({3 + 5 * len(m.layers)} kernels on 1/{ws} of the weights, KV and "
+                     f"lm_head, {2 * len(m.layers) + 1} NCCL all-reduces)")
+            traffic = None
+        elif fused:
             kname = "decode_step_kernel (the whole token: 36 layers + lm_head, one persistent launch)"
             traffic = step_traffic(bytes_tok)
         else:
@@ -318,16 +332,18 @@ def run_ours(args):
             traffic = tr.get("bytes_per_launch") if tr else None
         out = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": K, "warmup": W,
-            "ms_per_step": t / K * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "ms_per_step": t / K * 1e3, "higher_is_better": True, "scaling": "strong" if ws > 1 else "weak",
+            "vs_baseline": None,
             "dtype": "fp8-e4m3 x fp8 -> fp32 (bf16 activations, bf16 KV)", "data": "synthetic (seeded random-init "
             "weights, N(0,1) KV cache, no checkpoint)",
             "config": {"workload": f"Qwen3-8B FP8 decode, 36 layers, per-channel FP8 + FP8 lm_head, KV 4096 "
                                    f"pre-filled to {start}, {K} greedy steps (ctx {start}..{max_seq - 1}), CUDA graph",
-                       "global_batch": ws, "seq_len": max_seq, "parallelism": "replica" if ws > 1 else "tp1",
-                       "scale_mode": args.scale, "head": args.head, "attn_chunk": args.chunk, "pdl": not args.no_pdl, "path": args.path,
+                       "global_batch": 1, "seq_len": max_seq, "parallelism": f"tp{ws}",
+                       "scale_mode": args.scale, "head": args.head, "attn_chunk": args.chunk, "pdl": not args.no_pdl,
+                       "path": "ops+nccl" if ws > 1 else args.path,
                        "l2": "inputs larger than L2 (8.2 GB read per step), no flush"},
-            "e2e": {"value": ws * K / t_e2e, "unit": UNIT, "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
-            "gpu_launches": K * (1 if fused else 3 + 5 * len(m.layers)),
+            "e2e": {"value": K / t_e2e, "unit": UNIT, "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
+            "gpu_launches": K * (1 if fused else (3 + 5 * len(m.layers) + (3 if ws > 1 else 0))),
             "roofline": {"bound": "hbm", "kernel": kname, "achieved": achieved, "peak": peak,
                          "peak_source": f"{peak_src} hbm_gbs (burst copy)", "unit": "GB/s", "frac": achieved / peak,
                          "traffic": traffic, "bytes_per_launch_algorithmic": k_bytes, "launch_us": k_s * 1e6,
@@ -339,12 +355,13 @@ def run_ours(args):
             "device_error": err,
             "tokens_head": tokens[:8],
         }
-        if not args.no_cpu_baseline:
+        if not args.no_cpu_baseline and ws == 1:
             out["cpu_baseline"] = cpu_baseline(start)
         print(json.dumps(out), flush=True)
     if ws > 1:
         import torch.distributed as dist
-        eng.graph = None
+        eng.release()
+        dist.barrier()
         dist.destroy_process_group()
 
 

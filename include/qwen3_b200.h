@@ -177,6 +177,13 @@ int qk_embed(const int* token, const void* table, void* resid, int vocab, int ba
 int qk_finalize(unsigned long long* best, int* token, int* out_tokens, int* state, int out_len, int batch,
                 qk_stream_t stream);
 
+/* Tensor-parallel helpers (no counterpart in the single-GPU reference; the TP plan of its decode step):
+ * resid[i] = bf16(resid[i] + bf16(sum[i])) for the fp32 all-reduced partial of a row-parallel GEMV (the
+ * rounding of the reference's residual epilogue, decode.cu:320-323); and the top-bit flip of packed argmax
+ * keys, which maps their unsigned order onto signed int64 order for an NCCL int64 MAX all-reduce. */
+int qk_residual_add(void* resid, const float* sum, int n, qk_stream_t stream);
+int qk_argmax_key_flip(unsigned long long* keys, int n, qk_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -285,6 +285,20 @@ __global__ void __launch_bounds__(512) embed_kernel(const int* __restrict__ toke
 }
 
 // Decode the argmax key into the next token, record it, advance the step state [pos, step], clear the key.
+// resid[i] = bf16(resid[i] + bf16(sum[i])): the residual update of a row-parallel layer after its all-reduce
+// (the same rounding as the in-place residual epilogue, decode.cu:320-323).
+__global__ void residual_add_kernel(bf16* __restrict__ resid, const float* __restrict__ sum, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) resid[i] = __float2bfloat16_rn(__bfloat162float(resid[i]) + bf16r(sum[i]));
+}
+
+// Flip the top bit of packed argmax keys: unsigned key order <-> signed 64-bit order, so a signed MAX
+// reduction (NCCL int64) picks the same key as the unsigned atomicMax.
+__global__ void key_flip_kernel(unsigned long long* __restrict__ keys, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) keys[i] ^= 0x8000000000000000ull;
+}
+
 __global__ void finalize_kernel(unsigned long long* __restrict__ best, int* __restrict__ token,
                                 int* __restrict__ out_tokens, int* __restrict__ state, int out_len) {
   grid_dep_wait();

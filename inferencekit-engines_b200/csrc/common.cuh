@@ -154,7 +154,7 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
 }
 
 // Bulk (non-tensor) async copy global -> shared, completion counted on an mbarrier in transaction bytes.
-// dst, src 16-byte aligned, bytes a multiple of 16. No multicast.
+// dst, src 16-byte aligned, bytes a multiple of 16. Destination: this CTA only.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t pol) {
   asm volatile(
       "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
@@ -169,7 +169,7 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
                : "memory");
 }
 
-// Tiled TMA load of one box of a 4-D tensor map into shared memory (no multicast), completion counted on an
+// Tiled TMA load of one box of a 4-D tensor map into this CTA's shared memory, completion counted on an
 // mbarrier in transaction bytes. x (innermost) * element size must be a multiple of 16 bytes.
 __device__ __forceinline__ void tma_load_4d(void* dst, const void* tmap, int x, int y, int z, int w, uint64_t* bar) {
   asm volatile(

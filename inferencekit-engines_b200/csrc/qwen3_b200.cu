@@ -435,6 +435,21 @@ int qk_finalize(unsigned long long* best, int* token, int* out_tokens, int* stat
   return launch(finalize_kernel, dim3(batch), dim3(1), 0, stream, best, token, out_tokens, state, out_len);
 }
 
+int qk_residual_add(void* resid, const float* sum, int n, qk_stream_t stream) {
+  if (!resid || !sum || n < 1) return fail(QK_EINVAL, "bad residual_add arguments");
+  const int threads = 256;
+  residual_add_kernel<<<(n + threads - 1) / threads, threads, 0, stream>>>(static_cast<bf16*>(resid), sum, n);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? QK_OK : cuda_fail(e, "residual_add launch");
+}
+
+int qk_argmax_key_flip(unsigned long long* keys, int n, qk_stream_t stream) {
+  if (!keys || n < 1) return fail(QK_EINVAL, "bad argmax_key_flip arguments");
+  key_flip_kernel<<<(n + 255) / 256, 256, 0, stream>>>(keys, n);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? QK_OK : cuda_fail(e, "argmax_key_flip launch");
+}
+
 }  // extern "C"
 
 // ---- GEMV without caller-provided scratch --------------------------------------------------------------------

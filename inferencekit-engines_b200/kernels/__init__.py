@@ -46,6 +46,8 @@ _SIGS = {
     "qk_decode_step": ([_VP, _I, _VP, _VP, ctypes.c_longlong, _VP, _VP, _VP, _VP, _I, _VP, _VP, _VP, _VP, _VP, _I,
                         _VP, _VP, _VP, _VP, _VP, _VP, _VP, ctypes.c_longlong, _VP, _I, _VP, _VP, _VP, _VP, _I, _I,
                         _F, _I, _VP, _VP], _I),
+    "qk_residual_add": ([_VP, _VP, _I, _VP], _I),
+    "qk_argmax_key_flip": ([_VP, _I, _VP], _I),
     "qk_decode_step_part_floats": ([_I], ctypes.c_longlong),
     "qk_decode_step_counters": ([_I], _I),
     "qk_fp8_gemv_noalloc": ([_I, _VP, _VP, _I, _VP, _VP, _VP, _VP, _VP, _I, _I, _F, _VP], _I),
@@ -181,6 +183,14 @@ class DecodeOps:
                                      _p(ml_part), _p(attn_counters), _p(sync), int(max_seq), o_part.shape[-2],
                                      float(eps), int(scale_mode), _p(timeline), _stream())
         self._check(st, "decode_step")
+
+    def residual_add(self, resid, sum_f32):
+        """resid = bf16(resid + bf16(sum)) (after the all-reduce of a row-parallel partial)."""
+        self._check(self.lib.qk_residual_add(_p(resid), _p(sum_f32), resid.numel(), _stream()), "residual_add")
+
+    def argmax_key_flip(self, keys):
+        """Unsigned <-> signed order of packed argmax keys (int64 tensor), in place."""
+        self._check(self.lib.qk_argmax_key_flip(_p(keys), keys.numel(), _stream()), "argmax_key_flip")
 
     def embed(self, token, table, resid):
         b = token.numel()

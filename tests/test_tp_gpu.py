@@ -1,0 +1,98 @@
+"""Tensor-parallel decode on 2 GPUs (NCCL) against the single-GPU engine on the same seeded weights.
+
+Each rank runs `tp.TPEngine` on its shard under a CUDA graph. Both engines are teacher-forced with the
+single-GPU engine's greedy tokens, so they see the same inputs at every step. The checks:
+* the layer-0 K/V rows the ranks append equal the TP=1 rows of their heads, bit for bit (layer 0 has no
+  reduction before its qkv);
+* the logits (each rank's vocabulary shard) are within 2e-2 rel-L2 of TP=1 at the first step and 5e-2 at
+  every step (they differ only by the order of the fp32 partial sums after o_proj and down, amplified by the
+  W8A8 re-quantisation of the next layer's input);
+* the greedy tokens agree on at least 90% of the steps.
+"""
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+STEPS = 24
+POS0 = 100
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank(rank, world, port, out_dir):
+    import datetime
+    import torch.distributed as dist
+    import model as M
+    import tp as TP
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", rank))
+    eng = None
+    try:
+        cfg = M.Config(layers=2, vocab=16384)
+        dev = f"cuda:{rank}"
+        m = TP.synthetic_shard(cfg, world, rank, max_seq=512, device=dev, seed=0)
+        tokens = torch.load(os.path.join(out_dir, "tokens.pt"))
+        eng = TP.TPEngine(m)
+        eng.state.copy_(torch.tensor([POS0, 0], dtype=torch.int32))
+        eng.token.fill_(int(tokens[0]))
+        eng.capture()
+        logits, got = [], []
+        for i in range(STEPS):
+            eng.token.fill_(int(tokens[i]))
+            eng.graph.replay()
+            logits.append(eng.logits.float().cpu())
+            got.append(int(eng.token.item()))
+        kv = (m.k_cache[0, 0, :, POS0].cpu(), m.v_cache[0, 0, :, POS0].cpu())
+        torch.save({"logits": torch.stack(logits), "tokens": got, "kv": kv, "vocab_offset": m.vocab_offset},
+                   os.path.join(out_dir, f"rank{rank}.pt"))
+    finally:
+        if eng is not None:
+            eng.release()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tp2_matches_single_gpu(tmp_path):
+    import torch.multiprocessing as mp
+    import model as M
+    from generate import Engine
+    cfg = M.Config(layers=2, vocab=16384)
+    m = M.Qwen3FP8Decode.synthetic(cfg, max_seq=512, device="cuda:0", seed=0)
+    eng = Engine(m)
+    eng.state.copy_(torch.tensor([POS0, 0], dtype=torch.int32))
+    eng.token.fill_(1)
+    eng.capture()
+    tokens, logits = [1], []
+    for i in range(STEPS):
+        eng.token.fill_(tokens[i])
+        eng.graph.replay()
+        logits.append(eng.logits.float().cpu())
+        tokens.append(int(eng.token.item()))
+    kv = (m.k_cache[0, 0, :, POS0].cpu(), m.v_cache[0, 0, :, POS0].cpu())
+    torch.save(torch.tensor(tokens), str(tmp_path / "tokens.pt"))
+    del eng, m
+    torch.cuda.empty_cache()
+    mp.start_processes(_rank, args=(2, _free_port(), str(tmp_path)), nprocs=2, start_method="spawn", join=True)
+    ref = torch.stack(logits)
+    agree = 0
+    for r in range(2):
+        d = torch.load(str(tmp_path / f"rank{r}.pt"))
+        a, b = d["vocab_offset"], d["vocab_offset"] + d["logits"].shape[1]
+        per_step = [((d["logits"][i] - ref[i, a:b]).norm() / ref[i, a:b].norm()).item() for i in range(STEPS)]
+        # the first step differs only through the fp32 partial-sum order of 2 layers; later steps also see
+        # KV rows written with those differences, amplified by W8A8 re-quantisation
+        assert per_step[0] < 2e-2 and max(per_step) < 5e-2, (r, per_step)
+        heads = slice(4 * r, 4 * r + 4)
+        assert torch.equal(d["kv"][0], kv[0][heads]) and torch.equal(d["kv"][1], kv[1][heads]), r
+        agree = sum(int(x == y) for x, y in zip(d["tokens"], tokens[1:]))
+        print(f"rank {r}: logits rel-L2 first {per_step[0]:.4f} max {max(per_step):.4f}; tokens agree {agree}/{STEPS}")
+    assert agree >= 0.9 * STEPS, (agree, STEPS)
