@@ -684,51 +684,48 @@ __device__ void attention_phase(Consumer& c, const StepLayer& L, int l, int pos)
       }
     }
     consumer_sync();
-    // scores: thread (key j = tid / 4, head hh = tid % 4), every item of the batch: dims 0..63 and 64..127 each
-    // summed in order, then added. Items past the batch recompute the last one and store nothing.
-    {
-      const int j = tid >> 2, hh = tid & 3;
-      float dot[ST_ABATCH][2];
-      uint32_t ks[ST_ABATCH], qrow[ST_ABATCH];        // shared-memory addresses
+    // scores: thread (item k = tid / 64, key j = tid % 64), all 4 query heads: dims 0..63 and 64..127 each
+    // summed in order, then added. Each K chunk is loaded and converted once for the 4 heads; the q values
+    // are the same for the whole warp (broadcast reads).
+    if ((tid >> 6) < nb) {
+      const int k = tid >> 6, j = tid & 63;
+      const int item = b0 + k, split = item % it.n_splits;
+      const int nj = min(ST_CHUNK, ctx - split * ST_CHUNK);
+      const uint32_t ks = smem_u32(stage(k));
+      const uint32_t qb0 = smem_u32(sm.u.at.qs[item / it.n_splits - kv0][0]);
+      constexpr uint32_t QROW = (HEAD_DIM + 4) * 4;            // bytes between the heads' q rows
+      float dot[GQA][2];
 #pragma unroll
-      for (int k = 0; k < ST_ABATCH; ++k) {
-        const int kk = min(k, nb - 1);
-        ks[k] = smem_u32(stage(kk));
-        qrow[k] = smem_u32(sm.u.at.qs[(b0 + kk) / it.n_splits - kv0][hh]);
-        dot[k][0] = dot[k][1] = 0.f;
-      }
+      for (int h = 0; h < GQA; ++h) dot[h][0] = dot[h][1] = 0.f;
 #pragma unroll
       for (int sl = 0; sl < 2; ++sl) {
-#pragma unroll 1
+#pragma unroll 2
         for (int i = 0; i < 8; ++i) {
-          const uint32_t ko = kv_swz(j, sl * 64 + i * 8), qo = (sl * 64 + i * 8) * 4;
+          const uint4 kv = lds128_at(ks + kv_swz(j, sl * 64 + i * 8));
+          const float k0 = bf16lo(kv.x), k1 = bf16hi(kv.x), k2 = bf16lo(kv.y), k3 = bf16hi(kv.y);
+          const float k4 = bf16lo(kv.z), k5 = bf16hi(kv.z), k6 = bf16lo(kv.w), k7 = bf16hi(kv.w);
+          const uint32_t qo = (sl * 64 + i * 8) * 4;
 #pragma unroll
-          for (int k = 0; k < ST_ABATCH; ++k) {
-            const uint4 kv = lds128_at(ks[k] + ko);
-            const uint4 qa = lds128_at(qrow[k] + qo);
-            const uint4 qb = lds128_at(qrow[k] + qo + 16);
-            // dims in order: the low then the high bf16 of each 32-bit word (exact bf16 -> f32)
-            float& dt = dot[k][sl];
-            dt += __uint_as_float(qa.x) * bf16lo(kv.x);
-            dt += __uint_as_float(qa.y) * bf16hi(kv.x);
-            dt += __uint_as_float(qa.z) * bf16lo(kv.y);
-            dt += __uint_as_float(qa.w) * bf16hi(kv.y);
-            dt += __uint_as_float(qb.x) * bf16lo(kv.z);
-            dt += __uint_as_float(qb.y) * bf16hi(kv.z);
-            dt += __uint_as_float(qb.z) * bf16lo(kv.w);
-            dt += __uint_as_float(qb.w) * bf16hi(kv.w);
+          for (int h = 0; h < GQA; ++h) {
+            const uint4 qa = lds128_at(qb0 + h * QROW + qo);
+            const uint4 qb = lds128_at(qb0 + h * QROW + qo + 16);
+            float& dt = dot[h][sl];
+            dt += __uint_as_float(qa.x) * k0;
+            dt += __uint_as_float(qa.y) * k1;
+            dt += __uint_as_float(qa.z) * k2;
+            dt += __uint_as_float(qa.w) * k3;
+            dt += __uint_as_float(qb.x) * k4;
+            dt += __uint_as_float(qb.y) * k5;
+            dt += __uint_as_float(qb.z) * k6;
+            dt += __uint_as_float(qb.w) * k7;
           }
         }
       }
 #pragma unroll
-      for (int k = 0; k < ST_ABATCH; ++k) {
-        if (k < nb) {
-          const int split = (b0 + k) % it.n_splits;
-          const int nj = min(ST_CHUNK, ctx - split * ST_CHUNK);
-          float sc = dot[k][0];
-          sc += dot[k][1];
-          sm.u.at.sc[k][hh][j] = j < nj ? sc * p.attn_scale : -INFINITY;
-        }
+      for (int h = 0; h < GQA; ++h) {
+        float sc = dot[h][0];
+        sc += dot[h][1];
+        sm.u.at.sc[k][h][j] = j < nj ? sc * p.attn_scale : -INFINITY;
       }
     }
     consumer_sync();
@@ -763,6 +760,7 @@ __device__ void attention_phase(Consumer& c, const StepLayer& L, int l, int pos)
 #pragma unroll
       for (int h = 0; h < GQA; ++h) acc[h][0] = acc[h][1] = 0.f;
       const int n8 = nj >> 3;
+#pragma unroll 2
       for (int t = 0; t < n8; ++t) {
         uint32_t v2[8];
 #pragma unroll
