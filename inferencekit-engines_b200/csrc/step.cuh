@@ -132,6 +132,10 @@ struct StepSmem {
 
 // ---- small helpers -------------------------------------------------------------------------------------------
 __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(ST_WARPS * 32) : "memory"); }
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+__device__ __forceinline__ void red_add_relaxed(int* p, int v) {
+  asm volatile("red.relaxed.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
   unsigned v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -319,6 +323,21 @@ __device__ __forceinline__ FoldPre fold_prefetch(const Consumer& c, const GemvPh
   return f;
 }
 
+// Copy the block dots of unit u's slices [hi, end of unit), published by the following CTA(s) in `part`, into
+// the unit's slot behind this CTA's own (cp.async through L2; the caller waits).
+template <int KB, int NG>
+__device__ __forceinline__ void fetch_unit_tail(const Consumer& c, const float* part, float* slot, int u, int hi) {
+  constexpr int RPU = 16 * NG, spu = KB * NG;
+  constexpr int MAXV = spu * 16 / 4 / 32;                     // 16-byte vectors per lane for a whole unit
+  const int off4 = (hi - u * spu) * 4, n4 = spu * 4;          // in 16-byte vectors
+  const uint4* gsrc = reinterpret_cast<const uint4*>(part + (size_t)u * KB * RPU);
+#pragma unroll
+  for (int j = 0; j < MAXV; ++j) {
+    const int i4 = off4 + c.lane + 32 * j;
+    if (i4 < n4) cp_async16_cg(reinterpret_cast<uint4*>(slot) + i4, gsrc + i4);
+  }
+}
+
 // Fold of one 16-row unit (32 rows for gate|up) once this CTA's block dots of it are complete: the per-op
 // kernel's in-order sum acc += d * sx * sw over K blocks, then the epilogue. Gate rows fold on lanes 0-15 and
 // up rows on lanes 16-31. A unit shared with a neighbouring CTA is folded by whichever CTA completes it last,
@@ -335,8 +354,8 @@ __device__ __forceinline__ void fold_unit(Consumer& c, const GemvPhase<EPI, SCAL
     // dots were stored by several warps, each of which released them to this warp through the stage's `empty`
     // barrier; the fence is cumulative over them, so the folding CTA sees all of them after its acquire.
     if (c.lane == 0) {
-      __threadfence();
-      atomicAdd(&ph.counters[u], hi - lo);
+      fence_acq_rel_gpu();
+      red_add_relaxed(&ph.counters[u], hi - lo);
     }
     return;
   }
@@ -358,14 +377,7 @@ __device__ __forceinline__ void fold_unit(Consumer& c, const GemvPhase<EPI, SCAL
         }
       }
     }
-    constexpr int MAXV = spu * 16 / 4 / 32;                   // 16-byte vectors per lane for a whole unit
-    const int off4 = (hi - u * spu) * 4, n4 = spu * 4;        // in 16-byte vectors
-    const uint4* gsrc = reinterpret_cast<const uint4*>(ph.part + (size_t)u * KB * RPU);
-#pragma unroll
-    for (int j = 0; j < MAXV; ++j) {
-      const int i4 = off4 + c.lane + 32 * j;
-      if (ok && i4 < n4) cp_async16_cg(reinterpret_cast<uint4*>(slot) + i4, gsrc + i4);
-    }
+    if (ok) fetch_unit_tail<KB, NG>(c, ph.part, slot, u, hi);
     cp_async_wait_all();
     __syncwarp();
     if (c.lane == 0 && ok) ph.counters[u] = 0;
