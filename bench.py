@@ -13,8 +13,10 @@ replay stream, with a synchronize (and for N>1 a barrier) on both sides; max ove
 K steps through the public engine API with, every step, the input token copied from pinned host memory
 and the output token read back to pinned host memory (host-synchronous streaming decode).
 
-N > 1: tensor parallelism over the N GPUs (tp.py: Megatron-style shards, NCCL all-reduces of the fp32
-partials after o_proj and down, vocab-parallel lm_head), one process per GPU, the same 4k-context workload
+N > 1: tensor parallelism over the N GPUs (tp.py: Megatron-style shards, vocab-parallel lm_head), one process
+per GPU. Default: the fused TP step (one persistent launch per token and rank, the fp32 partials of o_proj
+and down exchanged inside the kernel over NVLink); --path ops: the op-by-op engine with NCCL all-reduces.
+The same 4k-context workload
 (scaling "strong": the job decodes one token stream; value = tokens/s of that stream). The step time is the
 max over ranks.
 
@@ -242,8 +244,8 @@ def run_ours(args):
         m = TP.synthetic_shard(cfg, ws, rank, max_seq=max_seq, device=dev, seed=args.seed, scale_mode=args.scale,
                                head_dtype=args.head, norm_init="ones")
         m.fill_cache_random(start, seed=1234 + rank)
-        fused = False
-        eng = TP.TPEngine(m, attn_chunk=args.chunk)
+        fused = args.path == "fused"
+        eng = TP.FusedTPEngine(m) if fused else TP.TPEngine(m, attn_chunk=args.chunk)
     else:
         m = M.Qwen3FP8Decode.synthetic(cfg, max_seq=max_seq, device=dev, seed=args.seed, scale_mode=args.scale,
                                        head_dtype=args.head, norm_init="ones")
@@ -306,7 +308,7 @@ def run_ours(args):
     peak, peak_src = peaks()
     bytes_tok, wb = step_bytes(m, start, max_seq - 1)
     if fused or ws > 1:
-        # fused: the step kernel is the whole step; TP: the rank's whole step (its shard's bytes)
+        # fused: the step kernel is the whole step (TP: the rank's, on its shard's bytes)
         k_s, k_bytes, k_n = t / K, bytes_tok, K
     else:
         k_s, k_bytes, k_n = gate_up_kernel_timing(eng, reps=2)   # dominant kernel alone
@@ -319,7 +321,11 @@ def run_ours(args):
     value = K / t
     if rank == 0:
         achieved = k_bytes / k_s / 1e9
-        if ws > 1:
+        if ws > 1 and fused:
+            kname = (f"decode_step_kernel<TP={ws}>: one rank's whole token on 1/{ws} of the weights, KV and "
+                     f"lm_head, partials exchanged in-kernel over NVLink")
+            traffic = None
+        elif ws > 1:
             kname = (f"one TP rank's step ({3 + 5 * len(m.layers)} kernels on 1/{ws} of the weights, KV and "
                      f"lm_head, {2 * len(m.layers) + 1} NCCL all-reduces)")
             traffic = None
@@ -340,7 +346,7 @@ def run_ours(args):
                                    f"pre-filled to {start}, {K} greedy steps (ctx {start}..{max_seq - 1}), CUDA graph",
                        "global_batch": 1, "seq_len": max_seq, "parallelism": f"tp{ws}",
                        "scale_mode": args.scale, "head": args.head, "attn_chunk": args.chunk, "pdl": not args.no_pdl,
-                       "path": "ops+nccl" if ws > 1 else args.path,
+                       "path": ("fused-tp" if fused else "ops+nccl") if ws > 1 else args.path,
                        "l2": "inputs larger than L2 (8.2 GB read per step), no flush"},
             "e2e": {"value": K / t_e2e, "unit": UNIT, "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
             "gpu_launches": K * (1 if fused else (3 + 5 * len(m.layers) + (3 if ws > 1 else 0))),

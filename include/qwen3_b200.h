@@ -165,6 +165,43 @@ int qk_decode_step(const qk_layer_t* layers, int n_layers, void* k_cache, void* 
                    int* attn_counters, unsigned* sync, int max_seq, int max_splits, float eps, int scale_mode,
                    uint64_t* timeline, qk_stream_t stream);
 
+/*
+ * Tensor-parallel fused step (no counterpart in the reference, whose engine is single-GPU; this is the TP
+ * `comm` handle entry point its scope allows). Every rank runs qk_decode_step_tp on its shard, one process per
+ * GPU: query heads 32/tp, KV heads 8/tp (KV caches [n_layers][8/tp][max_seq][128]), gate|up rows 2*12288/tp,
+ * o_proj and down columns 4096/tp and 12288/tp, lm_head rows `vocab` (this rank's) from global id
+ * `vocab_offset`. o_proj and down produce fp32 partials that the kernel exchanges itself: it stores them into
+ * every rank's TP area over NVLink (plain stores to peer memory mapped with CUDA IPC) and waits on a
+ * system-scope counter; each rank adds the partials to its residual in rank order, so all ranks hold the same
+ * residual. The argmax keys are exchanged the same way and every rank writes the same token. Results equal
+ * the single-GPU step up to the order of the fp32 partial sums. Per-channel scales only.
+ *   areas      DEVICE array [tp] of every rank's TP area as mapped in this process ([rank] = its own):
+ *              qk_tp_area_alloc on each rank, the 64-byte IPC handles exchanged by the caller, then
+ *              qk_tp_area_open on each peer's handle. Areas start zeroed and must not be reset between launches.
+ *   resid_alt  a second bf16 [4096] residual buffer
+ * All ranks must launch the same number of steps; a rank that stops makes the others' bounded waits time out
+ * and set the device error word (qk_get_device_error).
+ */
+typedef struct {
+  int tp;                   /* ranks: 2, 4 or 8 */
+  int rank;                 /* this rank */
+  void* const* areas;       /* DEVICE array [tp] of TP area pointers */
+} qk_tp_comm_t;
+
+long long qk_tp_area_bytes(void);
+int qk_tp_area_alloc(void** area, void* ipc_handle /* 64 bytes out */);
+int qk_tp_area_open(const void* ipc_handle, void** peer_area);
+int qk_tp_area_close(void* peer_area);
+int qk_tp_area_free(void* area);
+int qk_decode_step_tp(const qk_layer_t* layers, int n_layers, void* k_cache, void* v_cache, long long kv_layer_stride,
+                      const void* embed, const void* final_norm, const void* w_head, const float* s_head, int vocab,
+                      const void* cos_tab, const void* sin_tab, int* token, int* state, int* out_tokens,
+                      int out_len, unsigned long long* best, void* resid, void* qkv, void* attn, void* h,
+                      void* logits, float* part, long long part_floats, int* counters, int n_counters,
+                      float* o_part, float* ml_part, int* attn_counters, unsigned* sync, int max_seq,
+                      int max_splits, float eps, uint64_t* timeline, void* resid_alt, int vocab_offset,
+                      const qk_tp_comm_t* comm, qk_stream_t stream);
+
 /* Minimum scratch sizes of qk_decode_step for a vocabulary size (no GPU needed). */
 long long qk_decode_step_part_floats(int vocab);
 int qk_decode_step_counters(int vocab);

@@ -51,12 +51,12 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
-// TMA map of a whole-model K or V cache: bf16 {128 dims, max_seq keys, 8 kv heads, n_layers}, box {64, 64, 1, 1}
+// TMA map of a whole-model K or V cache: bf16 {128 dims, max_seq keys, n_kv heads, n_layers}, box {64, 64, 1, 1}
 // (8 KiB), 128-byte swizzle, out-of-range rows zero-filled.
-int encode_kv_map(CUtensorMap* map, void* base, int max_seq, int n_layers, long long layer_stride_bytes) {
+int encode_kv_map(CUtensorMap* map, void* base, int max_seq, int n_kv, int n_layers, long long layer_stride_bytes) {
   auto enc = tensor_map_encoder();
   if (!enc) return fail(QK_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
-  const cuuint64_t dims[4] = {HEAD_DIM, (cuuint64_t)max_seq, 8, (cuuint64_t)n_layers};
+  const cuuint64_t dims[4] = {HEAD_DIM, (cuuint64_t)max_seq, (cuuint64_t)n_kv, (cuuint64_t)n_layers};
   const cuuint64_t strides[3] = {HEAD_DIM * 2, (cuuint64_t)max_seq * HEAD_DIM * 2, (cuuint64_t)layer_stride_bytes};
   const cuuint32_t box[4] = {64, 64, 1, 1};
   const cuuint32_t estr[4] = {1, 1, 1, 1};
@@ -345,23 +345,29 @@ int qk_decode_step_counters(int vocab) {
   return head > 768 ? head : 768;
 }
 
-int qk_decode_step(const qk_layer_t* layers, int n_layers, void* k_cache, void* v_cache, long long kv_layer_stride,
-                   const void* embed, const void* final_norm, const void* w_head, const float* s_head, int vocab,
-                   const void* cos_tab, const void* sin_tab, int* token, int* state, int* out_tokens, int out_len,
-                   unsigned long long* best, void* resid, void* qkv, void* attn, void* h, void* logits, float* part,
-                   long long part_floats, int* counters, int n_counters, float* o_part, float* ml_part,
-                   int* attn_counters, unsigned* sync, int max_seq, int max_splits, float eps, int scale_mode,
-                   uint64_t* timeline, qk_stream_t stream) {
+}  // extern "C"
+
+namespace {
+// Shared by qk_decode_step (tp = 1) and qk_decode_step_tp (tp > 1: this rank's shard, see StepParams).
+int launch_decode_step(const qk_layer_t* layers, int n_layers, void* k_cache, void* v_cache, long long kv_layer_stride,
+                       const void* embed, const void* final_norm, const void* w_head, const float* s_head, int vocab,
+                       const void* cos_tab, const void* sin_tab, int* token, int* state, int* out_tokens, int out_len,
+                       unsigned long long* best, void* resid, void* qkv, void* attn, void* h, void* logits,
+                       float* part, long long part_floats, int* counters, int n_counters, float* o_part,
+                       float* ml_part, int* attn_counters, unsigned* sync, int max_seq, int max_splits, float eps,
+                       int scale_mode, uint64_t* timeline, int tp, int rank, void* resid_alt, int vocab_offset,
+                       void* const* areas, cudaStream_t stream) {
   if (!layers || n_layers < 1 || !k_cache || !v_cache || !embed || !final_norm || !w_head || !s_head || !cos_tab ||
       !sin_tab || !token || !state || !out_tokens || !best || !resid || !qkv || !attn || !h || !logits || !part ||
       !counters || !o_part || !ml_part || !attn_counters || !sync)
     return fail(QK_EINVAL, "null pointer argument");
   if (max_seq < 1) return fail(QK_EINVAL, "bad max_seq");
+  const int n_kv = 8 / tp;
   if (!aligned(k_cache, 16) || !aligned(v_cache, 16) || kv_layer_stride % 16 ||
-      kv_layer_stride < 8LL * max_seq * HEAD_DIM * 2)
+      kv_layer_stride < (long long)n_kv * max_seq * HEAD_DIM * 2)
     return fail(QK_EINVAL, "KV caches must be 16-byte aligned with a layer stride (bytes) that is a multiple of 16 "
-                           "and at least 8 * max_seq * 256");
-  if (vocab <= 0 || vocab % 16 || out_len < 1 || max_seq < 1) return fail(QK_EINVAL, "bad vocab/out_len/max_seq");
+                           "and at least n_kv * max_seq * 256");
+  if (vocab <= 0 || vocab % 16 || out_len < 1) return fail(QK_EINVAL, "bad vocab/out_len");
   if (part_floats < qk_decode_step_part_floats(vocab) || n_counters < qk_decode_step_counters(vocab))
     return fail(QK_EINVAL, "scratch too small: part needs %lld floats, counters %d ints",
                 qk_decode_step_part_floats(vocab), qk_decode_step_counters(vocab));
@@ -369,8 +375,8 @@ int qk_decode_step(const qk_layer_t* layers, int n_layers, void* k_cache, void* 
     return fail(QK_EINVAL, "max_splits must cover max_seq/64 and be at most %d", ST_MAX_SPLITS);
   if (scale_mode != QK_SCALE_BLOCK128 && scale_mode != QK_SCALE_CHANNEL) return fail(QK_EINVAL, "bad scale_mode");
   StepParams p = {};
-  if (int r = encode_kv_map(&p.tm_k, k_cache, max_seq, n_layers, kv_layer_stride)) return r;
-  if (int r = encode_kv_map(&p.tm_v, v_cache, max_seq, n_layers, kv_layer_stride)) return r;
+  if (int r = encode_kv_map(&p.tm_k, k_cache, max_seq, n_kv, n_layers, kv_layer_stride)) return r;
+  if (int r = encode_kv_map(&p.tm_v, v_cache, max_seq, n_kv, n_layers, kv_layer_stride)) return r;
   p.k_cache = static_cast<bf16*>(k_cache);
   p.v_cache = static_cast<bf16*>(v_cache);
   p.kv_layer_elems = kv_layer_stride / 2;
@@ -404,7 +410,16 @@ int qk_decode_step(const qk_layer_t* layers, int n_layers, void* k_cache, void* 
   p.eps = eps;
   p.attn_scale = 0.08838834764831845f;   // 128 ** -0.5
   p.tl = reinterpret_cast<unsigned long long*>(timeline);
-  auto kernel = scale_mode == QK_SCALE_CHANNEL ? decode_step_kernel<SCALE_CHANNEL> : decode_step_kernel<SCALE_BLOCK>;
+  p.tp = tp;
+  p.tp_rank = rank;
+  p.vocab_offset = vocab_offset;
+  p.resid_alt = static_cast<bf16*>(resid_alt);
+  p.areas = reinterpret_cast<TpArea* const*>(areas);
+  void (*kernel)(const StepParams) = nullptr;
+  if (tp == 1) kernel = scale_mode == QK_SCALE_CHANNEL ? decode_step_kernel<SCALE_CHANNEL, 1> : decode_step_kernel<SCALE_BLOCK, 1>;
+  else if (tp == 2) kernel = decode_step_kernel<SCALE_CHANNEL, 2>;
+  else if (tp == 4) kernel = decode_step_kernel<SCALE_CHANNEL, 4>;
+  else if (tp == 8) kernel = decode_step_kernel<SCALE_CHANNEL, 8>;
   const int smem = (int)sizeof(StepSmem);
   if (int r = ensure_smem((const void*)kernel, smem)) return r;
   cudaLaunchConfig_t cfg = {};
@@ -420,6 +435,79 @@ int qk_decode_step(const qk_layer_t* layers, int n_layers, void* k_cache, void* 
   cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, p);
   if (e != cudaSuccess) return cuda_fail(e, "decode step launch");
   return QK_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int qk_decode_step(const qk_layer_t* layers, int n_layers, void* k_cache, void* v_cache, long long kv_layer_stride,
+                   const void* embed, const void* final_norm, const void* w_head, const float* s_head, int vocab,
+                   const void* cos_tab, const void* sin_tab, int* token, int* state, int* out_tokens, int out_len,
+                   unsigned long long* best, void* resid, void* qkv, void* attn, void* h, void* logits, float* part,
+                   long long part_floats, int* counters, int n_counters, float* o_part, float* ml_part,
+                   int* attn_counters, unsigned* sync, int max_seq, int max_splits, float eps, int scale_mode,
+                   uint64_t* timeline, qk_stream_t stream) {
+  return launch_decode_step(layers, n_layers, k_cache, v_cache, kv_layer_stride, embed, final_norm, w_head, s_head,
+                            vocab, cos_tab, sin_tab, token, state, out_tokens, out_len, best, resid, qkv, attn, h,
+                            logits, part, part_floats, counters, n_counters, o_part, ml_part, attn_counters, sync,
+                            max_seq, max_splits, eps, scale_mode, timeline, 1, 0, nullptr, 0, nullptr, stream);
+}
+
+long long qk_tp_area_bytes(void) { return (long long)sizeof(TpArea); }
+
+int qk_tp_area_alloc(void** area, void* ipc_handle) {
+  if (!area || !ipc_handle) return fail(QK_EINVAL, "null pointer argument");
+  void* a = nullptr;
+  cudaError_t e = cudaMalloc(&a, sizeof(TpArea));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc (TP area)");
+  e = cudaMemset(a, 0, sizeof(TpArea));
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(ipc_handle), a);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    cudaFree(a);
+    return cuda_fail(e, "TP area setup");
+  }
+  *area = a;
+  return QK_OK;
+}
+
+int qk_tp_area_open(const void* ipc_handle, void** peer_area) {
+  if (!ipc_handle || !peer_area) return fail(QK_EINVAL, "null pointer argument");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(peer_area, h, cudaIpcMemLazyEnablePeerAccess);
+  return e == cudaSuccess ? QK_OK : cuda_fail(e, "cudaIpcOpenMemHandle (peer TP area)");
+}
+
+int qk_tp_area_close(void* peer_area) {
+  if (!peer_area) return fail(QK_EINVAL, "null pointer argument");
+  const cudaError_t e = cudaIpcCloseMemHandle(peer_area);
+  return e == cudaSuccess ? QK_OK : cuda_fail(e, "cudaIpcCloseMemHandle");
+}
+
+int qk_tp_area_free(void* area) {
+  if (!area) return fail(QK_EINVAL, "null pointer argument");
+  const cudaError_t e = cudaFree(area);
+  return e == cudaSuccess ? QK_OK : cuda_fail(e, "cudaFree (TP area)");
+}
+
+int qk_decode_step_tp(const qk_layer_t* layers, int n_layers, void* k_cache, void* v_cache, long long kv_layer_stride,
+                      const void* embed, const void* final_norm, const void* w_head, const float* s_head, int vocab,
+                      const void* cos_tab, const void* sin_tab, int* token, int* state, int* out_tokens,
+                      int out_len, unsigned long long* best, void* resid, void* qkv, void* attn, void* h,
+                      void* logits, float* part, long long part_floats, int* counters, int n_counters,
+                      float* o_part, float* ml_part, int* attn_counters, unsigned* sync, int max_seq,
+                      int max_splits, float eps, uint64_t* timeline, void* resid_alt, int vocab_offset,
+                      const qk_tp_comm_t* comm, qk_stream_t stream) {
+  if (!comm || !comm->areas || !resid_alt) return fail(QK_EINVAL, "null pointer argument");
+  if (comm->tp != 2 && comm->tp != 4 && comm->tp != 8) return fail(QK_EINVAL, "tp must be 2, 4 or 8");
+  if (comm->rank < 0 || comm->rank >= comm->tp) return fail(QK_EINVAL, "bad rank");
+  if (vocab_offset < 0 || vocab_offset % 16) return fail(QK_EINVAL, "bad vocab_offset");
+  return launch_decode_step(layers, n_layers, k_cache, v_cache, kv_layer_stride, embed, final_norm, w_head, s_head,
+                            vocab, cos_tab, sin_tab, token, state, out_tokens, out_len, best, resid, qkv, attn, h,
+                            logits, part, part_floats, counters, n_counters, o_part, ml_part, attn_counters, sync,
+                            max_seq, max_splits, eps, QK_SCALE_CHANNEL, timeline, comm->tp, comm->rank, resid_alt,
+                            vocab_offset, comm->areas, stream);
 }
 
 int qk_embed(const int* token, const void* table, void* resid, int vocab, int batch, qk_stream_t stream) {

@@ -43,7 +43,6 @@ constexpr int ST_MAX_SPLITS = 1024;                // contexts up to 64k
 // Block-dot slots: a slot holds one open unit's KB x 16*NG block dots (2-6 KiB); 24 KiB gives 12, 6 or 4 slots,
 // enough for the units that can be open at once (see the bound in gemv_phase).
 constexpr int ST_BD_FLOATS = 6144;
-constexpr int ST_MAX_SLOTS = 12;
 constexpr int ST_MERGE_SPLITS = 64;                // splits staged per round of the attention merge
 constexpr int ST_ABATCH = 4;                       // attention items processed together (<= ST_NSTAGE)
 #ifndef ST_SPI
@@ -63,6 +62,16 @@ struct StepLayer {
 __device__ __forceinline__ uint32_t kv_swz(int r, int d) {   // byte offset of (row r, dim d) in a chunk
   return (uint32_t)((d >> 6) * 8192 + r * 128 + ((((d & 63) >> 3) ^ (r & 7)) << 4) + (d & 7) * 2);
 }
+
+// Tensor parallelism: each rank owns one TpArea in memory its peers map (CUDA IPC) and write over NVLink.
+constexpr int ST_MAX_TP = 8;
+struct TpArea {
+  float recv[2][ST_MAX_TP][HIDDEN];                // fp32 partial rows of exchange k: [k % 2][source rank][row]
+  unsigned long long ctr;                          // exchange arrivals: every rank adds 1 per exchange
+  unsigned long long key_ctr;                      // argmax keys received (1 per rank per launch)
+  unsigned long long keys[ST_MAX_TP];              // argmax key of each rank
+  unsigned long long epoch;                        // launches completed by this rank (written by itself)
+};
 
 struct StepParams {
   CUtensorMap tm_k, tm_v;                          // see kv_swz
@@ -90,6 +99,10 @@ struct StepParams {
   int max_seq, max_splits;
   float eps, attn_scale;
   unsigned long long* tl;                          // optional timeline [CTA][phase][8], null when off
+  // tensor parallelism (tp > 1; shapes per rank: see decode_step_kernel)
+  int tp, tp_rank, vocab_offset;                   // this rank's lm_head rows start at global id vocab_offset
+  bf16* resid_alt;                                 // second residual buffer: exchange k reads resid[k % 2]
+  TpArea* const* areas;                            // device array [tp]: every rank's area ([tp_rank] = own)
 };
 
 // Phase p of a step: layer l's qkv, attn, o, gu, down are 5l + 0..4; the lm_head is 5 * n_layers.
@@ -133,6 +146,30 @@ struct StepSmem {
 // ---- small helpers -------------------------------------------------------------------------------------------
 __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(ST_WARPS * 32) : "memory"); }
 __device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+__device__ __forceinline__ void red_add_release_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+// Bounded wait until *p >= target (a counter other GPUs add to); sets DEVERR_GRID_TIMEOUT on timeout.
+__device__ __forceinline__ void wait_sys_counter(const unsigned long long* p, unsigned long long target) {
+  const long long c0 = clock64();
+  while (ld_acquire_sys_u64(p) < target && clock64() - c0 < 500000) {
+  }
+  if (ld_acquire_sys_u64(p) >= target) return;
+  const unsigned long long t0 = globaltimer();
+  while (ld_acquire_sys_u64(p) < target) {
+    if (wait_failed()) return;
+    if (globaltimer() - t0 > WAIT_LIMIT_NS) {
+      atomicOr(&g_dev_error, DEVERR_GRID_TIMEOUT);
+      return;
+    }
+  }
+}
 __device__ __forceinline__ void red_add_relaxed(int* p, int v) {
   asm volatile("red.relaxed.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -263,7 +300,10 @@ struct GemvPhase {
   bf16* out;          // STORE: qkv; RESIDUAL: resid; SWIGLU: h; ARGMAX: logits
   float* part;
   int* counters;
+  int row_offset = 0; // ARGMAX: global id of row 0 (vocabulary shard)
+  int xbuf = 0;       // TP_PARTIAL: exchange buffer (k % 2)
 };
+constexpr int EPI_TP_PARTIAL = 10;   // fp32 row partial into every rank's TpArea (row-parallel shard)
 
 struct Consumer {
   StepSmem* sm;
@@ -347,7 +387,8 @@ __device__ __forceinline__ void fold_unit(Consumer& c, const GemvPhase<EPI, SCAL
                                           int u, const FoldPre& pre) {
   StepSmem& sm = *c.sm;
   constexpr int RPU = 16 * NG, spu = KB * NG, slot_floats = KB * RPU, nslots = ST_BD_FLOATS / slot_floats;
-  static_assert(KB % 16 == 0, "fold batches");
+  constexpr int FB = KB % 16 == 0 ? 16 : (KB % 8 == 0 ? 8 : 4);   // block dots read per batch
+  static_assert(KB % FB == 0, "fold batches");
   const int lo = max(u * spu, r.s0), hi = min((u + 1) * spu, r.s1);
   if (u * spu < r.s0) {
     // The unit started in an earlier CTA, which folds it: publish this CTA's share (already in ph.part). Its
@@ -388,15 +429,15 @@ __device__ __forceinline__ void fold_unit(Consumer& c, const GemvPhase<EPI, SCAL
   float a = 0.f;
   if (active) {
     const float* s = slot + gi * 16 + rr;
-    for (int k0 = 0; k0 < KB; k0 += 16) {
-      float d[16], sw[16];
+    for (int k0 = 0; k0 < KB; k0 += FB) {
+      float d[FB], sw[FB];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
+      for (int j = 0; j < FB; ++j) {
         d[j] = s[(k0 + j) * RPU];
         sw[j] = SCALE == SCALE_CHANNEL ? pre.sw : row_scale<SCALE>(ph.ws, row, k0 + j, KB);
       }
 #pragma unroll
-      for (int j = 0; j < 16; ++j) a += d[j] * sm.xscale[k0 + j] * sw[j];
+      for (int j = 0; j < FB; ++j) a += d[j] * sm.xscale[k0 + j] * sw[j];
     }
   }
   const float resid_in = pre.resid;
@@ -413,10 +454,14 @@ __device__ __forceinline__ void fold_unit(Consumer& c, const GemvPhase<EPI, SCAL
       ph.out[row] = __float2bfloat16_rn(a);
     } else if (EPI == EPI_RESIDUAL) {
       ph.out[row] = __float2bfloat16_rn(resid_in + bf16r(a));
+    } else if (EPI == EPI_TP_PARTIAL) {   // this rank's fp32 partial of the row, to every rank (NVLink stores)
+      const StepParams& p = *c.p;
+      for (int r2 = 0; r2 < p.tp; ++r2) p.areas[r2]->recv[ph.xbuf][p.tp_rank][row] = a;
     } else {  // EPI_ARGMAX
       ph.out[row] = __float2bfloat16_rn(a);
       const float lv = bf16r(a);
-      if (lv > c.best_v || (lv == c.best_v && row < c.best_i)) { c.best_v = lv; c.best_i = row; }
+      const int gid = row + ph.row_offset;
+      if (lv > c.best_v || (lv == c.best_v && gid < c.best_i)) { c.best_v = lv; c.best_i = gid; }
     }
   }
 }
@@ -432,7 +477,6 @@ __device__ void gemv_phase(Consumer& c, const GemvPhase<EPI, SCALE, NG>& ph) {
   // u is folded at the latest when its owner reaches stage (u's last) + ST_NSTAGE, and no warp runs more than
   // ST_NSTAGE stages ahead of the slowest, so writers stay within (2 * ST_NSTAGE + 2) stages of u's last slice.
   static_assert((nslots - 1) * spu > (2 * ST_NSTAGE + 2) * ST_SLICES, "too few block-dot slots");
-  static_assert(nslots <= ST_MAX_SLOTS, "slot count");
   const int units = ph.N / RPU;
   const SliceRange r = slice_range(units * spu);
   const int nst = (r.s1 - r.s0 + ST_SLICES - 1) / ST_SLICES;   // stages of this phase (as the producer issues)
@@ -534,8 +578,12 @@ __device__ void gemv_phase(Consumer& c, const GemvPhase<EPI, SCALE, NG>& ph) {
 // x (global, K values) -> optional RMSNorm (reference 128-thread reduction order) -> e4m3 per 128-group ->
 // f16 fragments in sm.xh + scales in sm.xscale. `embed_row` (layer 0): x is that row of the embedding table
 // and this CTA also writes its slice of it into the residual stream.
+// TP > 1 after an exchange (tp_recv != null, NORM only): x is the residual before the exchange and the value
+// used is bf16(x + bf16(sum of the ranks' fp32 partials, in rank order)), which this CTA also writes, for its
+// slice, to resid_slice_dst (the other residual buffer).
 template <bool NORM>
-__device__ void step_prologue(Consumer& c, const bf16* x, const bf16* norm_w, int K, float eps, bf16* resid_slice_dst) {
+__device__ void step_prologue(Consumer& c, const bf16* x, const bf16* norm_w, int K, float eps, bf16* resid_slice_dst,
+                              const float* tp_recv = nullptr, int tp = 1) {
   StepSmem& sm = *c.sm;
   const int tid = threadIdx.x;
   const int KB = K / QB;
@@ -556,6 +604,28 @@ __device__ void step_prologue(Consumer& c, const bf16* x, const bf16* norm_w, in
     uint4 xv[2];
 #pragma unroll
     for (int i = 0; i < 2; ++i) xv[i] = ldcg_u4(x + (tid + i * ST_WARPS * 32) * 8);
+    if (tp_recv) {   // resid + bf16(sum over ranks), 8 elements per thread and step
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int e0 = (tid + i * ST_WARPS * 32) * 8;
+        float sum[8];
+        for (int r = 0; r < tp; ++r) {
+          const float4 a = __ldcg(reinterpret_cast<const float4*>(tp_recv + (size_t)r * HIDDEN + e0));
+          const float4 b = __ldcg(reinterpret_cast<const float4*>(tp_recv + (size_t)r * HIDDEN + e0 + 4));
+          const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+          for (int j = 0; j < 8; ++j) sum[j] = r == 0 ? v[j] : sum[j] + v[j];
+        }
+        uint32_t w[4] = {xv[i].x, xv[i].y, xv[i].z, xv[i].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float lo = bf16lo(w[j]) + bf16r(sum[2 * j]), hi = bf16hi(w[j]) + bf16r(sum[2 * j + 1]);
+          w[j] = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(lo)) |
+                 ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(hi)) << 16);
+        }
+        xv[i] = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
 #pragma unroll
     for (int i = 0; i < 2; ++i) reinterpret_cast<uint4*>(sm.u.xs)[tid + i * ST_WARPS * 32] = xv[i];
     consumer_sync();
@@ -636,11 +706,12 @@ __device__ __forceinline__ void norm_rope_regs(float (&v)[4], const bf16* nw, co
 // stage each) so that every thread carries independent dot chains of several items: scores with thread =
 // (key, query head) over all items of the batch, softmax with one warp per (item, head) row, P @ V with two
 // warps per item and thread = (2 dims, 4 heads). Every sum keeps the reference's order.
+template <int NKV>   // KV heads of this rank (8 / TP); 4 query heads per KV head
 __device__ void attention_phase(Consumer& c, const StepLayer& L, int l, int pos) {
   StepSmem& sm = *c.sm;
   const StepParams& p = *c.p;
   const int tid = threadIdx.x, lane = c.lane, warp = c.warp;
-  constexpr int NKV = 8, NQ = 32;
+  constexpr int NQ = GQA * NKV;
   const AttnItems it = attn_items(pos, NKV);
   const int ctx = pos + 1;
   const int last_split = it.n_splits - 1;
@@ -814,13 +885,14 @@ __device__ void attention_phase(Consumer& c, const StepLayer& L, int l, int pos)
   }
 }
 
-// Merge of the 64-key splits (after a grid barrier): CTA c < 64 produces dims 64*(c%2) .. +63 of query head
-// c/2. The head's partials of up to 64 splits are prefetched into shared memory at once, then every output is
+// Merge of the 64-key splits (after a grid barrier): CTA c < 2 * NQ produces dims 64*(c%2) .. +63 of query
+// head c/2. The head's partials of up to 64 splits are prefetched into shared memory at once, then every output is
 // the reference's in-order sum over splits: sum_s exp(m_s - M) * o_s[d] / sum_s exp(m_s - M) * l_s.
+template <int NQ>    // query heads of this rank
 __device__ void merge_phase(Consumer& c, int pos) {
   StepSmem& sm = *c.sm;
   const StepParams& p = *c.p;
-  if (blockIdx.x >= 64) return;
+  if (blockIdx.x >= 2 * NQ) return;
   const int tid = threadIdx.x, lane = c.lane, warp = c.warp;
   const int qh = blockIdx.x >> 1, d0 = (blockIdx.x & 1) * 64;
   const int n_splits = (pos + 1 + ST_CHUNK - 1) / ST_CHUNK;
@@ -857,8 +929,31 @@ __device__ void merge_phase(Consumer& c, int pos) {
   if (tid < 64) p.attn[qh * HEAD_DIM + d0 + tid] = __float2bfloat16_rn(o / sm.u.mg.cl);
 }
 
+// ---- tensor-parallel exchange -------------------------------------------------------------------------------------
+// After a row-parallel GEMV phase (o_proj, down) every CTA has stored its rows' fp32 partials into every rank's
+// TpArea. This is the grid barrier of that phase and the cross-GPU one at once: the CTAs arrive on the local
+// barrier counter; the last one (all of this rank's partial stores are then issued and fenced) adds 1 to every
+// rank's exchange counter; every CTA waits until its own rank's counter shows all tp ranks for this exchange.
+// `target` = tp * (exchanges completed since the areas were created, this one included).
+__device__ __forceinline__ void tp_exchange(const StepParams& p, unsigned idx, unsigned long long target) {
+  consumer_sync();
+  if (threadIdx.x == 0) {
+    __threadfence_system();   // this CTA's partial rows, to every rank, before its arrival
+    const unsigned old = atomicAdd(p.sync, 1u);
+    if (old == (idx + 1) * gridDim.x - 1) {
+      fence_acq_rel_sys();    // acquire the other CTAs' arrivals (each released its rows), then release them all
+      for (int r = 0; r < p.tp; ++r) red_add_release_sys(&p.areas[r]->ctr, 1ull);
+    }
+    wait_sys_counter(&p.areas[p.tp_rank]->ctr, target);
+  }
+  consumer_sync();
+}
+
 // ---- the kernel -------------------------------------------------------------------------------------------------
-template <int SCALE>
+// TP = 1: the whole model on one GPU. TP > 1: this rank's shard (query heads 32/TP, KV heads 8/TP, intermediate
+// 12288/TP, vocabulary rows p.vocab from p.vocab_offset); o_proj and down produce fp32 partials that are
+// exchanged (tp_exchange) and added to the residual in the next prologue, in rank order on every rank.
+template <int SCALE, int TP>
 __global__ void __launch_bounds__(ST_THREADS, 1) decode_step_kernel(const __grid_constant__ StepParams p) {
   extern __shared__ __align__(1024) uint8_t smem_step[];
   StepSmem& sm = *reinterpret_cast<StepSmem*>(smem_step);
@@ -876,11 +971,11 @@ __global__ void __launch_bounds__(ST_THREADS, 1) decode_step_kernel(const __grid
     fence_mbar_init();
   }
   __syncthreads();
-  constexpr int H = HIDDEN, I = 12288, QKV_N = 6144;
+  constexpr int H = HIDDEN, I = 12288 / TP, QKV_N = 6144 / TP, NKV = 8 / TP, NQ = 32 / TP, KO = HIDDEN / TP;
   if (warp == ST_WARPS) {   // ---------------- producer ----------------
     if (lane == 0) {
       Producer pr{&sm, 0, policy_evict_first(), true, 0};
-      const AttnItems it = attn_items(pos, 8);
+      const AttnItems it = attn_items(pos, NKV);
       for (int l = 0; l < p.n_layers; ++l) {
         const StepLayer& L = p.layers[l];
         step_stamp(p, 5 * l + 0, 3);
@@ -894,7 +989,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) decode_step_kernel(const __grid
         }
         step_stamp(p, 5 * l + 2, 3);
         step_put(p, 5 * l + 2, 6, pr.wait_cycles);
-        pr.gemv(L.w_o, (H / 16) * (H / QB));
+        pr.gemv(L.w_o, (H / 16) * (KO / QB));
         step_stamp(p, 5 * l + 3, 3);
         step_put(p, 5 * l + 3, 6, pr.wait_cycles);
         pr.gemv(L.w_gu, (2 * I / 16) * (H / QB));
@@ -912,16 +1007,22 @@ __global__ void __launch_bounds__(ST_THREADS, 1) decode_step_kernel(const __grid
   Consumer c{&sm, &p, 0, lane, warp, lane >> 2, lane & 3, -INFINITY, 0x7FFFFFFF, 0, 0};
   unsigned nbar = 0;
   const int tok = p.token[0];
-  const bool tok_ok = tok >= 0 && tok < p.vocab;
+  const bool tok_ok = tok >= 0 && tok < p.vocab * TP;
   if (!tok_ok && threadIdx.x == 0 && blockIdx.x == 0) atomicOr(&g_dev_error, DEVERR_BAD_STATE);
   const bool tl = p.tl != nullptr && threadIdx.x == 0;
+  // TP: exchanges so far (2 per layer per launch), read before this launch's last CTA advances the epoch
+  const unsigned long long x_base = TP > 1 ? __ldcg(&p.areas[p.tp_rank]->epoch) * 2ull * p.n_layers : 0ull;
+  unsigned xk = 0;                                  // exchange index within this launch
+  bf16* const rbuf[2] = {p.resid, TP > 1 ? p.resid_alt : p.resid};
+  auto xrecv = [&](unsigned k) { return &p.areas[p.tp_rank]->recv[k % 2][0][0]; };
   for (int l = 0; l < p.n_layers; ++l) {
     const StepLayer& L = p.layers[l];
     const int ph = 5 * l;
-    // QKV
+    // QKV (TP: after the previous layer's down exchange, the residual update happens here)
     if (tl) step_stamp(p, ph, 0);
     if (l == 0) step_prologue<true>(c, p.embed + (size_t)(tok_ok ? tok : 0) * H, L.ln1, H, p.eps, p.resid);
-    else step_prologue<true>(c, p.resid, L.ln1, H, p.eps, nullptr);
+    else if (TP == 1) step_prologue<true>(c, p.resid, L.ln1, H, p.eps, nullptr);
+    else step_prologue<true>(c, rbuf[(xk - 1) % 2], L.ln1, H, p.eps, rbuf[xk % 2], xrecv(xk - 1), TP);
     if (tl) step_stamp(p, ph, 1);
     c.tl_phase = ph;
     gemv_phase<32>(c, GemvPhase<EPI_STORE, SCALE, 1>{L.s_qkv, QKV_N, H, p.qkv, p.part, p.counters});
@@ -929,44 +1030,59 @@ __global__ void __launch_bounds__(ST_THREADS, 1) decode_step_kernel(const __grid
     grid_barrier(p.sync, nbar++);
     // ATTN: split partials (and the K/V rows at pos), then the merge into the attention output
     if (tl) step_stamp(p, ph + 1, 0);
-    attention_phase(c, L, l, pos);
+    attention_phase<NKV>(c, L, l, pos);
     if (tl) step_stamp(p, ph + 1, 7);
     grid_barrier(p.sync, nbar++);
     if (tl) step_stamp(p, ph + 1, 1);
-    merge_phase(c, pos);
+    merge_phase<NQ>(c, pos);
     if (tl) { step_stamp(p, ph + 1, 2); step_put(p, ph + 1, 4, c.wait_cycles); step_put(p, ph + 1, 5, c.fold_cycles); }
     grid_barrier(p.sync, nbar++);
-    // O: resid += W_o . quant(attn)
+    // O: resid += W_o . quant(attn)   (TP: this rank's fp32 partial, exchanged)
     if (tl) step_stamp(p, ph + 2, 0);
-    step_prologue<false>(c, p.attn, nullptr, H, p.eps, nullptr);
+    step_prologue<false>(c, p.attn, nullptr, KO, p.eps, nullptr);
     if (tl) step_stamp(p, ph + 2, 1);
     c.tl_phase = ph + 2;
-    gemv_phase<32>(c, GemvPhase<EPI_RESIDUAL, SCALE, 1>{L.s_o, H, H, p.resid, p.part, p.counters});
+    if (TP == 1) {
+      gemv_phase<KO / QB>(c, GemvPhase<EPI_RESIDUAL, SCALE, 1>{L.s_o, H, KO, p.resid, p.part, p.counters});
+    } else {
+      gemv_phase<KO / QB>(c, GemvPhase<EPI_TP_PARTIAL, SCALE, 1>{L.s_o, H, KO, nullptr, p.part, p.counters, 0,
+                                                                 (int)(xk % 2)});
+    }
     if (tl) { step_stamp(p, ph + 2, 2); step_put(p, ph + 2, 4, c.wait_cycles); step_put(p, ph + 2, 5, c.fold_cycles); }
-    grid_barrier(p.sync, nbar++);
+    if (TP == 1) grid_barrier(p.sync, nbar++);
+    else { tp_exchange(p, nbar++, (x_base + xk + 1) * TP); ++xk; }
     // GU: h = SwiGLU(W_gu . quant(RMSNorm(resid)))
     if (tl) step_stamp(p, ph + 3, 0);
-    step_prologue<true>(c, p.resid, L.ln2, H, p.eps, nullptr);
+    if (TP == 1) step_prologue<true>(c, p.resid, L.ln2, H, p.eps, nullptr);
+    else step_prologue<true>(c, rbuf[(xk - 1) % 2], L.ln2, H, p.eps, rbuf[xk % 2], xrecv(xk - 1), TP);
     if (tl) step_stamp(p, ph + 3, 1);
     c.tl_phase = ph + 3;
     gemv_phase<32>(c, GemvPhase<EPI_SWIGLU, SCALE, 2>{L.s_gu, 2 * I, H, p.h, p.part, p.counters});
     if (tl) { step_stamp(p, ph + 3, 2); step_put(p, ph + 3, 4, c.wait_cycles); step_put(p, ph + 3, 5, c.fold_cycles); }
     grid_barrier(p.sync, nbar++);
-    // DOWN: resid += W_down . quant(h)
+    // DOWN: resid += W_down . quant(h)   (TP: partial, exchanged)
     if (tl) step_stamp(p, ph + 4, 0);
     step_prologue<false>(c, p.h, nullptr, I, p.eps, nullptr);
     if (tl) step_stamp(p, ph + 4, 1);
     c.tl_phase = ph + 4;
-    gemv_phase<96>(c, GemvPhase<EPI_RESIDUAL, SCALE, 1>{L.s_down, H, I, p.resid, p.part, p.counters});
+    if (TP == 1) {
+      gemv_phase<I / QB>(c, GemvPhase<EPI_RESIDUAL, SCALE, 1>{L.s_down, H, I, p.resid, p.part, p.counters});
+    } else {
+      gemv_phase<I / QB>(c, GemvPhase<EPI_TP_PARTIAL, SCALE, 1>{L.s_down, H, I, nullptr, p.part, p.counters, 0,
+                                                                (int)(xk % 2)});
+    }
     if (tl) { step_stamp(p, ph + 4, 2); step_put(p, ph + 4, 4, c.wait_cycles); step_put(p, ph + 4, 5, c.fold_cycles); }
-    grid_barrier(p.sync, nbar++);
+    if (TP == 1) grid_barrier(p.sync, nbar++);
+    else { tp_exchange(p, nbar++, (x_base + xk + 1) * TP); ++xk; }
   }
   if (tl) step_stamp(p, 5 * p.n_layers, 0);
-  // HEAD: logits + greedy argmax (FP8 per-channel head)
-  step_prologue<true>(c, p.resid, p.final_norm, H, p.eps, nullptr);
+  // HEAD: logits + greedy argmax (FP8 per-channel head; TP: this rank's vocabulary rows)
+  if (TP == 1) step_prologue<true>(c, p.resid, p.final_norm, H, p.eps, nullptr);
+  else step_prologue<true>(c, rbuf[(xk - 1) % 2], p.final_norm, H, p.eps, rbuf[xk % 2], xrecv(xk - 1), TP);
   if (tl) step_stamp(p, 5 * p.n_layers, 1);
   c.tl_phase = 5 * p.n_layers;
-  gemv_phase<32>(c, GemvPhase<EPI_ARGMAX, SCALE_CHANNEL, 1>{p.s_head, p.vocab, H, p.logits, p.part, p.counters});
+  gemv_phase<32>(c, GemvPhase<EPI_ARGMAX, SCALE_CHANNEL, 1>{p.s_head, p.vocab, H, p.logits, p.part, p.counters,
+                                                            p.vocab_offset});
   if (tl) { step_stamp(p, 5 * p.n_layers, 2); step_put(p, 5 * p.n_layers, 4, c.wait_cycles); step_put(p, 5 * p.n_layers, 5, c.fold_cycles); }
   {
     unsigned long long key = (c.best_i == 0x7FFFFFFF) ? 0ull : argmax_key(c.best_v, c.best_i);
@@ -986,7 +1102,20 @@ __global__ void __launch_bounds__(ST_THREADS, 1) decode_step_kernel(const __grid
       // so it also resets the barrier counters for the next launch
       if (atomicAdd(p.sync + 1, 1u) == gridDim.x - 1) {
         __threadfence();
-        const unsigned long long k = atomicAdd(p.best, 0ull);
+        unsigned long long k = atomicAdd(p.best, 0ull);
+        if (TP > 1) {   // every rank's best key to every rank; all ranks then take the same maximum
+          TpArea* own = p.areas[p.tp_rank];
+          const unsigned long long ep = __ldcg(&own->epoch);
+          for (int r = 0; r < TP; ++r) p.areas[r]->keys[p.tp_rank] = k;
+          __threadfence_system();
+          for (int r = 0; r < TP; ++r) red_add_release_sys(&p.areas[r]->key_ctr, 1ull);
+          wait_sys_counter(&own->key_ctr, (ep + 1) * TP);
+          for (int r = 0; r < TP; ++r) {
+            const unsigned long long kr = __ldcg(&own->keys[r]);
+            k = kr > k ? kr : k;
+          }
+          own->epoch = ep + 1;
+        }
         const int next = (int)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
         p.token[0] = next;
         const int step = p.state[1];

@@ -46,6 +46,14 @@ _SIGS = {
     "qk_decode_step": ([_VP, _I, _VP, _VP, ctypes.c_longlong, _VP, _VP, _VP, _VP, _I, _VP, _VP, _VP, _VP, _VP, _I,
                         _VP, _VP, _VP, _VP, _VP, _VP, _VP, ctypes.c_longlong, _VP, _I, _VP, _VP, _VP, _VP, _I, _I,
                         _F, _I, _VP, _VP], _I),
+    "qk_decode_step_tp": ([_VP, _I, _VP, _VP, ctypes.c_longlong, _VP, _VP, _VP, _VP, _I, _VP, _VP, _VP, _VP, _VP,
+                           _I, _VP, _VP, _VP, _VP, _VP, _VP, _VP, ctypes.c_longlong, _VP, _I, _VP, _VP, _VP, _VP,
+                           _I, _I, _F, _VP, _VP, _I, _VP, _VP], _I),
+    "qk_tp_area_bytes": ([], ctypes.c_longlong),
+    "qk_tp_area_alloc": ([ctypes.POINTER(_VP), _VP], _I),
+    "qk_tp_area_open": ([_VP, ctypes.POINTER(_VP)], _I),
+    "qk_tp_area_close": ([_VP], _I),
+    "qk_tp_area_free": ([_VP], _I),
     "qk_residual_add": ([_VP, _VP, _I, _VP], _I),
     "qk_argmax_key_flip": ([_VP, _I, _VP], _I),
     "qk_decode_step_part_floats": ([_I], ctypes.c_longlong),
@@ -65,6 +73,11 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         fn.argtypes = args
         fn.restype = res
     return lib
+
+
+class QkTpComm(ctypes.Structure):
+    """qk_tp_comm_t"""
+    _fields_ = [("tp", ctypes.c_int), ("rank", ctypes.c_int), ("areas", ctypes.c_void_p)]
 
 
 def _p(t):
@@ -183,6 +196,40 @@ class DecodeOps:
                                      _p(ml_part), _p(attn_counters), _p(sync), int(max_seq), o_part.shape[-2],
                                      float(eps), int(scale_mode), _p(timeline), _stream())
         self._check(st, "decode_step")
+
+    def decode_step_tp(self, layer_table, n_layers, k_cache, v_cache, embed, final_norm, w_head, s_head, cos_tab,
+                       sin_tab, token, state, out_tokens, best, resid, qkv, attn, h, logits, part, counters, o_part,
+                       ml_part, attn_counters, sync, max_seq, eps, resid_alt, vocab_offset, comm, timeline=None):
+        """The fused tensor-parallel step of one rank (qk_decode_step_tp); comm: a `TPComm` (areas exchanged)."""
+        stride = k_cache.stride(0) * k_cache.element_size()
+        st = self.lib.qk_decode_step_tp(_p(layer_table), int(n_layers), _p(k_cache), _p(v_cache), stride, _p(embed),
+                                        _p(final_norm), _p(w_head), _p(s_head), logits.numel(), _p(cos_tab),
+                                        _p(sin_tab), _p(token), _p(state), _p(out_tokens), out_tokens.numel(),
+                                        _p(best), _p(resid), _p(qkv), _p(attn), _p(h), _p(logits), _p(part),
+                                        part.numel(), _p(counters), counters.numel(), _p(o_part), _p(ml_part),
+                                        _p(attn_counters), _p(sync), int(max_seq), o_part.shape[-2], float(eps),
+                                        _p(timeline), _p(resid_alt), int(vocab_offset), ctypes.byref(comm),
+                                        _stream())
+        self._check(st, "decode_step_tp")
+
+    def tp_area_alloc(self):
+        """A zeroed TP area on the current device and its 64-byte CUDA IPC handle (bytes)."""
+        area = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(64)
+        self._check(self.lib.qk_tp_area_alloc(ctypes.byref(area), handle), "tp_area_alloc")
+        return area.value, handle.raw
+
+    def tp_area_open(self, handle: bytes):
+        peer = ctypes.c_void_p()
+        buf = ctypes.create_string_buffer(handle, 64)
+        self._check(self.lib.qk_tp_area_open(buf, ctypes.byref(peer)), "tp_area_open")
+        return peer.value
+
+    def tp_area_close(self, peer):
+        self._check(self.lib.qk_tp_area_close(ctypes.c_void_p(peer)), "tp_area_close")
+
+    def tp_area_free(self, area):
+        self._check(self.lib.qk_tp_area_free(ctypes.c_void_p(area)), "tp_area_free")
 
     def residual_add(self, resid, sum_f32):
         """resid = bf16(resid + bf16(sum)) (after the all-reduce of a row-parallel partial)."""

@@ -1,4 +1,8 @@
-"""Tensor-parallel decode: one process per GPU, torch.distributed (NCCL) for the two exchanges per layer.
+"""Tensor-parallel decode: one process per GPU, two exchanges per layer.
+
+Two engines share the partition below: `TPEngine` runs the single-GPU ops on each shard with NCCL
+all-reduces (torch.distributed) between them; `FusedTPEngine` runs the whole token in one persistent kernel
+per rank (qk_decode_step_tp) that exchanges the partials itself over NVLink.
 
 The partition is Megatron-style and follows the reference's 128-blocks, so every rank runs the same kernels
 as the single-GPU engine on its shard:
@@ -265,3 +269,106 @@ class TPEngine:
         """Drop the graph (it holds NCCL work) before the process group is destroyed."""
         self.graph = None
         torch.cuda.synchronize()
+
+
+class FusedTPEngine:
+    """One rank of the fused tensor-parallel step: the whole token in one persistent launch per GPU
+    (qk_decode_step_tp), the o_proj/down partials and the argmax keys exchanged inside the kernel over NVLink
+    (each rank's TP area is mapped into every other rank with CUDA IPC). One CUDA graph per step, no NCCL in
+    the step. `group`: the torch.distributed process group, used only to exchange the IPC handles."""
+
+    def __init__(self, m: M.Qwen3FP8Decode, group=None):
+        import ctypes
+        import torch.distributed as dist
+        from kernels import ops, QkTpComm
+        self.dist, self.group = dist, group
+        self.m = m
+        self.k = k = ops()
+        self.part_ = part = m.partition
+        if not isinstance(m.lm_head, M.Linear) or m.scale_mode != "channel":
+            raise ValueError("the fused TP step needs per-channel scales and an FP8 lm_head")
+        cfg, dev = m.cfg, m.device
+        H = part.cfg.hidden
+        bf = dict(dtype=torch.bfloat16, device=dev)
+        self.max_seq = m.max_seq
+        self.token = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.state = torch.zeros(2, dtype=torch.int32, device=dev)
+        self.out_tokens = torch.zeros(m.max_seq, dtype=torch.int32, device=dev)
+        self.best = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.resid = torch.zeros(H, **bf)
+        self.resid_alt = torch.zeros(H, **bf)
+        self.qkv = torch.zeros((cfg.n_heads + 2 * cfg.n_kv_heads) * cfg.head_dim, **bf)
+        self.attn = torch.zeros(cfg.n_heads * cfg.head_dim, **bf)
+        self.h = torch.zeros(cfg.inter, **bf)
+        self.logits = torch.zeros(cfg.vocab, **bf)
+        self.max_splits = (m.max_seq + 31) // 32
+        self.o_part = torch.zeros(cfg.n_heads, self.max_splits, cfg.head_dim, dtype=torch.float32, device=dev)
+        self.ml_part = torch.zeros(cfg.n_heads, self.max_splits, 2, dtype=torch.float32, device=dev)
+        self.counters = torch.zeros(cfg.n_kv_heads, dtype=torch.int32, device=dev)
+        lib = k.lib
+        self.scratch = torch.empty(lib.qk_decode_step_part_floats(cfg.vocab), dtype=torch.float32, device=dev)
+        self.gemv_counters = torch.zeros(lib.qk_decode_step_counters(cfg.vocab), dtype=torch.int32, device=dev)
+        self.sync = torch.zeros(2, dtype=torch.int32, device=dev)
+        self.layer_table = torch.tensor([[L.qkv.packed.data_ptr(), L.o.packed.data_ptr(), L.gu.packed.data_ptr(),
+                                          L.down.packed.data_ptr(), L.qkv.scale.data_ptr(), L.o.scale.data_ptr(),
+                                          L.gu.scale.data_ptr(), L.down.scale.data_ptr(), L.ln1.data_ptr(),
+                                          L.ln2.data_ptr(), L.q_norm.data_ptr(), L.k_norm.data_ptr()]
+                                         for L in m.layers], dtype=torch.int64, device=dev)
+        # TP areas: allocate, exchange IPC handles, map the peers'
+        torch.cuda.synchronize()
+        self.area, handle = k.tp_area_alloc()
+        handles = [None] * part.tp
+        dist.all_gather_object(handles, handle, group=group)
+        self.peers = [self.area if r == part.rank else k.tp_area_open(handles[r]) for r in range(part.tp)]
+        self.areas = torch.tensor(self.peers, dtype=torch.int64, device=dev)
+        self.comm = QkTpComm(part.tp, part.rank, self.areas.data_ptr())
+        torch.cuda.synchronize()
+        dist.barrier(group=group)          # every area is zeroed and mapped before any rank launches
+        self.graph = None
+        self.step_timeline = None
+
+    def decode_step(self):
+        m, k = self.m, self.k
+        k.decode_step_tp(self.layer_table, len(m.layers), m.k_cache, m.v_cache, m.embed, m.norm, m.lm_head.packed,
+                         m.lm_head.scale, m.cos, m.sin, self.token, self.state, self.out_tokens, self.best,
+                         self.resid, self.qkv, self.attn, self.h, self.logits, self.scratch, self.gemv_counters,
+                         self.o_part, self.ml_part, self.counters, self.sync, m.max_seq, m.cfg.eps, self.resid_alt,
+                         m.vocab_offset, self.comm, self.step_timeline)
+
+    def capture(self):
+        """One step into a CUDA graph. Every rank must capture (the warm-up steps exchange with the peers)."""
+        token, state = self.token.clone(), self.state.clone()
+        for _ in range(2):
+            self.token.copy_(token)
+            self.state.copy_(state)
+            self.decode_step()
+        torch.cuda.synchronize()
+        self.token.copy_(token)
+        self.state.copy_(state)
+        self.graph = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(self.graph, stream=s):
+                self.decode_step()
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+
+    def step(self, n: int = 1, use_graph: bool = True):
+        for _ in range(n):
+            if use_graph:
+                self.graph.replay()
+            else:
+                self.decode_step()
+
+    def release(self):
+        """Unmap the peers' areas and free this rank's (after every rank has finished its launches)."""
+        self.graph = None
+        torch.cuda.synchronize()
+        self.dist.barrier(group=self.group)
+        for r, ptr in enumerate(self.peers):
+            if r != self.part_.rank:
+                self.k.tp_area_close(ptr)
+        self.dist.barrier(group=self.group)
+        self.k.tp_area_free(self.area)
+        self.peers, self.area = [], None

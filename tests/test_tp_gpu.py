@@ -1,6 +1,8 @@
-"""Tensor-parallel decode on 2 GPUs (NCCL) against the single-GPU engine on the same seeded weights.
+"""Tensor-parallel decode on 2 GPUs against the single-GPU engine on the same seeded weights, for both TP
+engines: `tp.TPEngine` (op-by-op, NCCL all-reduces) and `tp.FusedTPEngine` (one persistent launch per token
+and rank, the partials exchanged inside the kernel over NVLink).
 
-Each rank runs `tp.TPEngine` on its shard under a CUDA graph. Both engines are teacher-forced with the
+Each rank runs the engine on its shard under a CUDA graph. Both engines are teacher-forced with the
 single-GPU engine's greedy tokens, so they see the same inputs at every step. The checks:
 * the layer-0 K/V rows the ranks append equal the TP=1 rows of their heads, bit for bit (layer 0 has no
   reduction before its qkv);
@@ -27,7 +29,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank(rank, world, port, out_dir):
+def _rank(rank, world, port, out_dir, fused):
     import datetime
     import torch.distributed as dist
     import model as M
@@ -41,7 +43,7 @@ def _rank(rank, world, port, out_dir):
         dev = f"cuda:{rank}"
         m = TP.synthetic_shard(cfg, world, rank, max_seq=512, device=dev, seed=0)
         tokens = torch.load(os.path.join(out_dir, "tokens.pt"))
-        eng = TP.TPEngine(m)
+        eng = TP.FusedTPEngine(m) if fused else TP.TPEngine(m)
         eng.state.copy_(torch.tensor([POS0, 0], dtype=torch.int32))
         eng.token.fill_(int(tokens[0]))
         eng.capture()
@@ -52,8 +54,9 @@ def _rank(rank, world, port, out_dir):
             logits.append(eng.logits.float().cpu())
             got.append(int(eng.token.item()))
         kv = (m.k_cache[0, 0, :, POS0].cpu(), m.v_cache[0, 0, :, POS0].cpu())
-        torch.save({"logits": torch.stack(logits), "tokens": got, "kv": kv, "vocab_offset": m.vocab_offset},
-                   os.path.join(out_dir, f"rank{rank}.pt"))
+        err = eng.k.device_error()
+        torch.save({"logits": torch.stack(logits), "tokens": got, "kv": kv, "vocab_offset": m.vocab_offset,
+                    "device_error": err}, os.path.join(out_dir, f"rank{rank}.pt"))
     finally:
         if eng is not None:
             eng.release()
@@ -61,7 +64,8 @@ def _rank(rank, world, port, out_dir):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_tp2_matches_single_gpu(tmp_path):
+@pytest.mark.parametrize("fused", [False, True], ids=["nccl", "fused"])
+def test_tp2_matches_single_gpu(tmp_path, fused):
     import torch.multiprocessing as mp
     import model as M
     from generate import Engine
@@ -81,11 +85,13 @@ def test_tp2_matches_single_gpu(tmp_path):
     torch.save(torch.tensor(tokens), str(tmp_path / "tokens.pt"))
     del eng, m
     torch.cuda.empty_cache()
-    mp.start_processes(_rank, args=(2, _free_port(), str(tmp_path)), nprocs=2, start_method="spawn", join=True)
+    mp.start_processes(_rank, args=(2, _free_port(), str(tmp_path), fused), nprocs=2, start_method="spawn",
+                       join=True)
     ref = torch.stack(logits)
     agree = 0
     for r in range(2):
         d = torch.load(str(tmp_path / f"rank{r}.pt"))
+        assert d["device_error"] == 0, d["device_error"]
         a, b = d["vocab_offset"], d["vocab_offset"] + d["logits"].shape[1]
         per_step = [((d["logits"][i] - ref[i, a:b]).norm() / ref[i, a:b].norm()).item() for i in range(STEPS)]
         # the first step differs only through the fp32 partial-sum order of 2 layers; later steps also see
