@@ -75,3 +75,21 @@ def test_fused_step_scratch_sizes(lib):
     assert lib.qk_decode_step_counters(4096) == 768
     assert lib.qk_decode_step_part_floats(151936) == 151936 * 32
     assert lib.qk_decode_step_counters(151936) == 151936 // 16
+
+
+def test_tp_entry_points_check_arguments_without_a_gpu(lib):
+    assert lib.qk_tp_area_bytes() >= 2 * 8 * 4096 * 4
+    p = ctypes.c_void_p(16)
+
+    class Comm(ctypes.Structure):
+        _fields_ = [("tp", ctypes.c_int), ("rank", ctypes.c_int), ("areas", ctypes.c_void_p)]
+
+    args = [p, 1, p, p, ctypes.c_longlong(8 * 4096 * 256), p, p, p, p, 151936, p, p, p, p, p, 4096, p, p, p, p, p,
+            p, p, ctypes.c_longlong(151936 * 32), p, 151936 // 16, p, p, p, p, 4096, 128, ctypes.c_float(1e-6),
+            None, p]
+    for tp, rank, off, msg in ((3, 0, 0, b"tp must be"), (2, 2, 0, b"bad rank"), (2, 0, 8, b"vocab_offset")):
+        comm = Comm(tp, rank, 16)
+        st = lib.qk_decode_step_tp(*args, off, ctypes.byref(comm), None)
+        assert st == 1 and msg in lib.qk_last_error(), lib.qk_last_error()
+    st = lib.qk_decode_step_tp(*args, 0, None, None)
+    assert st == 1 and b"null" in lib.qk_last_error()
