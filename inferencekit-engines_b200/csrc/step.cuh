@@ -205,10 +205,9 @@ __device__ __forceinline__ uint4 ldcg_u4(const void* p) {
 // Consumer-side grid barrier number `idx` (0-based) of this launch. Bounded: on timeout it records the error and
 // lets the CTA continue (wrong results, but no hang).
 __device__ __forceinline__ void grid_barrier(unsigned* ctr, unsigned idx) {
-  consumer_sync();
+  consumer_sync();   // orders the CTA's writes before thread 0's release below
   if (threadIdx.x == 0) {
-    __threadfence();
-    atomicAdd(ctr, 1u);
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(ctr) : "memory");
     const unsigned target = (idx + 1) * gridDim.x;
     const long long c0 = clock64();
     while (ld_acquire_u32(ctr) < target && clock64() - c0 < 500000) {
@@ -223,9 +222,8 @@ __device__ __forceinline__ void grid_barrier(unsigned* ctr, unsigned idx) {
         }
       }
     }
-    __threadfence();
   }
-  consumer_sync();
+  consumer_sync();   // the other threads read what the acquire made visible
 }
 
 // A GEMV phase's share for this CTA: a contiguous range of 2 KiB slices. Slice q of a matrix with NG
