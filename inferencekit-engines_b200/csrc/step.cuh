@@ -366,7 +366,7 @@ __device__ __forceinline__ FoldPre fold_prefetch(const Consumer& c, const GemvPh
 template <int KB, int NG>
 __device__ __forceinline__ void fetch_unit_tail(const Consumer& c, const float* part, float* slot, int u, int hi) {
   constexpr int RPU = 16 * NG, spu = KB * NG;
-  constexpr int MAXV = spu * 16 / 4 / 32;                     // 16-byte vectors per lane for a whole unit
+  constexpr int MAXV = (spu * 4 + 31) / 32;                   // 16-byte vectors per lane for a whole unit
   const int off4 = (hi - u * spu) * 4, n4 = spu * 4;          // in 16-byte vectors
   const uint4* gsrc = reinterpret_cast<const uint4*>(part + (size_t)u * KB * RPU);
 #pragma unroll
