@@ -65,9 +65,11 @@ __device__ __forceinline__ uint32_t kv_swz(int r, int d) {   // byte offset of (
 
 // Tensor parallelism: each rank owns one TpArea in memory its peers map (CUDA IPC) and write over NVLink.
 constexpr int ST_MAX_TP = 8;
+// A partial row travels as one 64-bit word: the fp32 value in the low half and the exchange's tag (its
+// sequence number since the areas were created, never 0) in the high half. An aligned 64-bit store is seen
+// whole or not at all, so a reader that sees the expected tag has the value: no fence, no counter.
 struct TpArea {
-  float recv[2][ST_MAX_TP][HIDDEN];                // fp32 partial rows of exchange k: [k % 2][source rank][row]
-  unsigned long long ctr;                          // exchange arrivals: every rank adds 1 per exchange
+  unsigned long long recv[2][ST_MAX_TP][HIDDEN];   // exchange k: [k % 2][source rank][row]
   unsigned long long key_ctr;                      // argmax keys received (1 per rank per launch)
   unsigned long long keys[ST_MAX_TP];              // argmax key of each rank
   unsigned long long epoch;                        // launches completed by this rank (written by itself)
@@ -146,13 +148,20 @@ struct StepSmem {
 // ---- small helpers -------------------------------------------------------------------------------------------
 __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(ST_WARPS * 32) : "memory"); }
 __device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
-__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 __device__ __forceinline__ void red_add_release_sys(unsigned long long* p, unsigned long long v) {
   asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 __device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
   unsigned long long v;
   asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
 // Bounded wait until *p >= target (a counter other GPUs add to); sets DEVERR_GRID_TIMEOUT on timeout.
@@ -300,6 +309,7 @@ struct GemvPhase {
   int* counters;
   int row_offset = 0; // ARGMAX: global id of row 0 (vocabulary shard)
   int xbuf = 0;       // TP_PARTIAL: exchange buffer (k % 2)
+  unsigned xtag = 0;  // TP_PARTIAL: the exchange's tag
 };
 constexpr int EPI_TP_PARTIAL = 10;   // fp32 row partial into every rank's TpArea (row-parallel shard)
 
@@ -454,7 +464,8 @@ __device__ __forceinline__ void fold_unit(Consumer& c, const GemvPhase<EPI, SCAL
       ph.out[row] = __float2bfloat16_rn(resid_in + bf16r(a));
     } else if (EPI == EPI_TP_PARTIAL) {   // this rank's fp32 partial of the row, to every rank (NVLink stores)
       const StepParams& p = *c.p;
-      for (int r2 = 0; r2 < p.tp; ++r2) p.areas[r2]->recv[ph.xbuf][p.tp_rank][row] = a;
+      const unsigned long long w = ((unsigned long long)ph.xtag << 32) | __float_as_uint(a);
+      for (int r2 = 0; r2 < p.tp; ++r2) st_relaxed_sys_u64(&p.areas[r2]->recv[ph.xbuf][p.tp_rank][row], w);
     } else {  // EPI_ARGMAX
       ph.out[row] = __float2bfloat16_rn(a);
       const float lv = bf16r(a);
@@ -576,12 +587,8 @@ __device__ void gemv_phase(Consumer& c, const GemvPhase<EPI, SCALE, NG>& ph) {
 // x (global, K values) -> optional RMSNorm (reference 128-thread reduction order) -> e4m3 per 128-group ->
 // f16 fragments in sm.xh + scales in sm.xscale. `embed_row` (layer 0): x is that row of the embedding table
 // and this CTA also writes its slice of it into the residual stream.
-// TP > 1 after an exchange (tp_recv != null, NORM only): x is the residual before the exchange and the value
-// used is bf16(x + bf16(sum of the ranks' fp32 partials, in rank order)), which this CTA also writes, for its
-// slice, to resid_slice_dst (the other residual buffer).
 template <bool NORM>
-__device__ void step_prologue(Consumer& c, const bf16* x, const bf16* norm_w, int K, float eps, bf16* resid_slice_dst,
-                              const float* tp_recv = nullptr, int tp = 1) {
+__device__ void step_prologue(Consumer& c, const bf16* x, const bf16* norm_w, int K, float eps, bf16* resid_slice_dst) {
   StepSmem& sm = *c.sm;
   const int tid = threadIdx.x;
   const int KB = K / QB;
@@ -602,28 +609,6 @@ __device__ void step_prologue(Consumer& c, const bf16* x, const bf16* norm_w, in
     uint4 xv[2];
 #pragma unroll
     for (int i = 0; i < 2; ++i) xv[i] = ldcg_u4(x + (tid + i * ST_WARPS * 32) * 8);
-    if (tp_recv) {   // resid + bf16(sum over ranks), 8 elements per thread and step
-#pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        const int e0 = (tid + i * ST_WARPS * 32) * 8;
-        float sum[8];
-        for (int r = 0; r < tp; ++r) {
-          const float4 a = __ldcg(reinterpret_cast<const float4*>(tp_recv + (size_t)r * HIDDEN + e0));
-          const float4 b = __ldcg(reinterpret_cast<const float4*>(tp_recv + (size_t)r * HIDDEN + e0 + 4));
-          const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-#pragma unroll
-          for (int j = 0; j < 8; ++j) sum[j] = r == 0 ? v[j] : sum[j] + v[j];
-        }
-        uint32_t w[4] = {xv[i].x, xv[i].y, xv[i].z, xv[i].w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float lo = bf16lo(w[j]) + bf16r(sum[2 * j]), hi = bf16hi(w[j]) + bf16r(sum[2 * j + 1]);
-          w[j] = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(lo)) |
-                 ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(hi)) << 16);
-        }
-        xv[i] = make_uint4(w[0], w[1], w[2], w[3]);
-      }
-    }
 #pragma unroll
     for (int i = 0; i < 2; ++i) reinterpret_cast<uint4*>(sm.u.xs)[tid + i * ST_WARPS * 32] = xv[i];
     consumer_sync();
@@ -928,29 +913,46 @@ __device__ void merge_phase(Consumer& c, int pos) {
 }
 
 // ---- tensor-parallel exchange -------------------------------------------------------------------------------------
-// After a row-parallel GEMV phase (o_proj, down) every CTA has stored its rows' fp32 partials into every rank's
-// TpArea. This is the grid barrier of that phase and the cross-GPU one at once: the CTAs arrive on the local
-// barrier counter; the last one (all of this rank's partial stores are then issued and fenced) adds 1 to every
-// rank's exchange counter; every CTA waits until its own rank's counter shows all tp ranks for this exchange.
-// `target` = tp * (exchanges completed since the areas were created, this one included).
-__device__ __forceinline__ void tp_exchange(const StepParams& p, unsigned idx, unsigned long long target) {
-  consumer_sync();
-  if (threadIdx.x == 0) {
-    __threadfence_system();   // this CTA's partial rows, to every rank, before its arrival
-    const unsigned old = atomicAdd(p.sync, 1u);
-    if (old == (idx + 1) * gridDim.x - 1) {
-      fence_acq_rel_sys();    // acquire the other CTAs' arrivals (each released its rows), then release them all
-      for (int r = 0; r < p.tp; ++r) red_add_release_sys(&p.areas[r]->ctr, 1ull);
+// After a row-parallel GEMV phase (o_proj, down) every rank has stored its rows' fp32 partials, tagged, into
+// every rank's TpArea. CTAs 0..31 each own 128 rows: a thread waits (bounded) until all tp words of its row
+// carry this exchange's tag, sums them in rank order and writes the new residual row
+// bf16(resid + bf16(sum)) to the other residual buffer. The grid barrier that follows publishes it to the
+// next prologue (and keeps the GEMV scratch of the two phases apart).
+__device__ __forceinline__ void tp_reduce(const StepParams& p, const bf16* resid, bf16* resid_next, int xbuf,
+                                          unsigned tag) {
+  constexpr int ROWS = 128;
+  if (blockIdx.x >= HIDDEN / ROWS || threadIdx.x >= ROWS) return;
+  const int row = blockIdx.x * ROWS + threadIdx.x;
+  const unsigned long long* src = &p.areas[p.tp_rank]->recv[xbuf][0][row];
+  float sum = 0.f;
+  for (int r = 0; r < p.tp; ++r) {
+    const unsigned long long* a = src + (size_t)r * HIDDEN;
+    unsigned long long w = ld_relaxed_sys_u64(a);
+    if ((unsigned)(w >> 32) != tag) {
+      const long long c0 = clock64();
+      while ((unsigned)((w = ld_relaxed_sys_u64(a)) >> 32) != tag && clock64() - c0 < 500000) {
+      }
+      if ((unsigned)(w >> 32) != tag) {
+        const unsigned long long t0 = globaltimer();
+        while ((unsigned)((w = ld_relaxed_sys_u64(a)) >> 32) != tag) {
+          if (wait_failed()) break;
+          if (globaltimer() - t0 > WAIT_LIMIT_NS) {
+            atomicOr(&g_dev_error, DEVERR_GRID_TIMEOUT);
+            break;
+          }
+        }
+      }
     }
-    wait_sys_counter(&p.areas[p.tp_rank]->ctr, target);
+    const float v = __uint_as_float((unsigned)w);
+    sum = r == 0 ? v : sum + v;
   }
-  consumer_sync();
+  resid_next[row] = __float2bfloat16_rn(__bfloat162float(ldcg_bf16(resid + row)) + bf16r(sum));
 }
 
 // ---- the kernel -------------------------------------------------------------------------------------------------
 // TP = 1: the whole model on one GPU. TP > 1: this rank's shard (query heads 32/TP, KV heads 8/TP, intermediate
 // 12288/TP, vocabulary rows p.vocab from p.vocab_offset); o_proj and down produce fp32 partials that are
-// exchanged (tp_exchange) and added to the residual in the next prologue, in rank order on every rank.
+// exchanged (tp_reduce) and added to the residual, in rank order on every rank.
 template <int SCALE, int TP>
 __global__ void __launch_bounds__(ST_THREADS, 1) decode_step_kernel(const __grid_constant__ StepParams p) {
   extern __shared__ __align__(1024) uint8_t smem_step[];
@@ -1011,16 +1013,15 @@ __global__ void __launch_bounds__(ST_THREADS, 1) decode_step_kernel(const __grid
   // TP: exchanges so far (2 per layer per launch), read before this launch's last CTA advances the epoch
   const unsigned long long x_base = TP > 1 ? __ldcg(&p.areas[p.tp_rank]->epoch) * 2ull * p.n_layers : 0ull;
   unsigned xk = 0;                                  // exchange index within this launch
-  bf16* const rbuf[2] = {p.resid, TP > 1 ? p.resid_alt : p.resid};
-  auto xrecv = [&](unsigned k) { return &p.areas[p.tp_rank]->recv[k % 2][0][0]; };
+  // residual buffer k: exchange k reads rbuf(k) and writes rbuf(k + 1) (TP = 1: one buffer, updated in place)
+  auto rbuf = [&](unsigned k) -> bf16* { return (TP > 1 && (k & 1)) ? p.resid_alt : p.resid; };
   for (int l = 0; l < p.n_layers; ++l) {
     const StepLayer& L = p.layers[l];
     const int ph = 5 * l;
     // QKV (TP: after the previous layer's down exchange, the residual update happens here)
     if (tl) step_stamp(p, ph, 0);
     if (l == 0) step_prologue<true>(c, p.embed + (size_t)(tok_ok ? tok : 0) * H, L.ln1, H, p.eps, p.resid);
-    else if (TP == 1) step_prologue<true>(c, p.resid, L.ln1, H, p.eps, nullptr);
-    else step_prologue<true>(c, rbuf[(xk - 1) % 2], L.ln1, H, p.eps, rbuf[xk % 2], xrecv(xk - 1), TP);
+    else step_prologue<true>(c, rbuf(xk), L.ln1, H, p.eps, nullptr);
     if (tl) step_stamp(p, ph, 1);
     c.tl_phase = ph;
     gemv_phase<32>(c, GemvPhase<EPI_STORE, SCALE, 1>{L.s_qkv, QKV_N, H, p.qkv, p.part, p.counters});
@@ -1044,15 +1045,17 @@ __global__ void __launch_bounds__(ST_THREADS, 1) decode_step_kernel(const __grid
       gemv_phase<KO / QB>(c, GemvPhase<EPI_RESIDUAL, SCALE, 1>{L.s_o, H, KO, p.resid, p.part, p.counters});
     } else {
       gemv_phase<KO / QB>(c, GemvPhase<EPI_TP_PARTIAL, SCALE, 1>{L.s_o, H, KO, nullptr, p.part, p.counters, 0,
-                                                                 (int)(xk % 2)});
+                                                                 (int)(xk % 2), (unsigned)(x_base + xk + 1)});
     }
     if (tl) { step_stamp(p, ph + 2, 2); step_put(p, ph + 2, 4, c.wait_cycles); step_put(p, ph + 2, 5, c.fold_cycles); }
-    if (TP == 1) grid_barrier(p.sync, nbar++);
-    else { tp_exchange(p, nbar++, (x_base + xk + 1) * TP); ++xk; }
+    if (TP > 1) {   // the tags tell a reducer when every rank's partial of its row has arrived
+      tp_reduce(p, rbuf(xk), rbuf(xk + 1), (int)(xk % 2), (unsigned)(x_base + xk + 1));
+      ++xk;
+    }
+    grid_barrier(p.sync, nbar++);
     // GU: h = SwiGLU(W_gu . quant(RMSNorm(resid)))
     if (tl) step_stamp(p, ph + 3, 0);
-    if (TP == 1) step_prologue<true>(c, p.resid, L.ln2, H, p.eps, nullptr);
-    else step_prologue<true>(c, rbuf[(xk - 1) % 2], L.ln2, H, p.eps, rbuf[xk % 2], xrecv(xk - 1), TP);
+    step_prologue<true>(c, rbuf(xk), L.ln2, H, p.eps, nullptr);
     if (tl) step_stamp(p, ph + 3, 1);
     c.tl_phase = ph + 3;
     gemv_phase<32>(c, GemvPhase<EPI_SWIGLU, SCALE, 2>{L.s_gu, 2 * I, H, p.h, p.part, p.counters});
@@ -1067,16 +1070,18 @@ __global__ void __launch_bounds__(ST_THREADS, 1) decode_step_kernel(const __grid
       gemv_phase<I / QB>(c, GemvPhase<EPI_RESIDUAL, SCALE, 1>{L.s_down, H, I, p.resid, p.part, p.counters});
     } else {
       gemv_phase<I / QB>(c, GemvPhase<EPI_TP_PARTIAL, SCALE, 1>{L.s_down, H, I, nullptr, p.part, p.counters, 0,
-                                                                (int)(xk % 2)});
+                                                                (int)(xk % 2), (unsigned)(x_base + xk + 1)});
     }
     if (tl) { step_stamp(p, ph + 4, 2); step_put(p, ph + 4, 4, c.wait_cycles); step_put(p, ph + 4, 5, c.fold_cycles); }
-    if (TP == 1) grid_barrier(p.sync, nbar++);
-    else { tp_exchange(p, nbar++, (x_base + xk + 1) * TP); ++xk; }
+    if (TP > 1) {
+      tp_reduce(p, rbuf(xk), rbuf(xk + 1), (int)(xk % 2), (unsigned)(x_base + xk + 1));
+      ++xk;
+    }
+    grid_barrier(p.sync, nbar++);
   }
   if (tl) step_stamp(p, 5 * p.n_layers, 0);
   // HEAD: logits + greedy argmax (FP8 per-channel head; TP: this rank's vocabulary rows)
-  if (TP == 1) step_prologue<true>(c, p.resid, p.final_norm, H, p.eps, nullptr);
-  else step_prologue<true>(c, rbuf[(xk - 1) % 2], p.final_norm, H, p.eps, rbuf[xk % 2], xrecv(xk - 1), TP);
+  step_prologue<true>(c, rbuf(xk), p.final_norm, H, p.eps, nullptr);
   if (tl) step_stamp(p, 5 * p.n_layers, 1);
   c.tl_phase = 5 * p.n_layers;
   gemv_phase<32>(c, GemvPhase<EPI_ARGMAX, SCALE_CHANNEL, 1>{p.s_head, p.vocab, H, p.logits, p.part, p.counters,
