@@ -171,9 +171,11 @@ int qk_decode_step(const qk_layer_t* layers, int n_layers, void* k_cache, void* 
  * GPU: query heads 32/tp, KV heads 8/tp (KV caches [n_layers][8/tp][max_seq][128]), gate|up rows 2*12288/tp,
  * o_proj and down columns 4096/tp and 12288/tp, lm_head rows `vocab` (this rank's) from global id
  * `vocab_offset`. o_proj and down produce fp32 partials that the kernel exchanges itself: it stores them into
- * every rank's TP area over NVLink (plain stores to peer memory mapped with CUDA IPC) and waits on a
- * system-scope counter; each rank adds the partials to its residual in rank order, so all ranks hold the same
- * residual. The argmax keys are exchanged the same way and every rank writes the same token. Results equal
+ * every rank's TP area over NVLink (plain stores to peer memory mapped with CUDA IPC), each as one 64-bit word
+ * that carries the value and the exchange's tag, and waits (bounded) until every rank's word of a row carries
+ * the current tag; each rank adds the partials to its residual in rank order, so all ranks hold the same
+ * residual. The argmax keys go to every rank's area behind a system-scope counter, and every rank writes the
+ * same token. Results equal
  * the single-GPU step up to the order of the fp32 partial sums. Per-channel scales only.
  *   areas      DEVICE array [tp] of every rank's TP area as mapped in this process ([rank] = its own):
  *              qk_tp_area_alloc on each rank, the 64-byte IPC handles exchanged by the caller, then
