@@ -69,6 +69,14 @@ int qk_set_timeline(uint64_t* buf, int n_slots);
  * token id). Synchronises `stream`. No counterpart in the reference (its waits are unbounded). */
 int qk_get_device_error(int* err, qk_stream_t stream);
 
+/* Exercise the failure path of the bounded waits (no counterpart in the reference, whose waits are unbounded):
+ * one thread waits, at most limit_ns (<= 1 s), for something that never happens — phase 0 of an mbarrier nothing
+ * arrives on (mode 0, as a ring stage that never lands) or *counter >= 1 for a zeroed u64 counter nothing adds to
+ * (mode 1, as a peer rank that stopped). The wait gives up, writes 1 to the device int *gave_up, sets the device
+ * error word (bit 1 for mode 0, bit 4 for mode 1; read with qk_get_device_error) and the context stays usable.
+ * Waits skip ahead while the error word already holds a timeout, so read it (which clears it) first. */
+int qk_wait_probe(int mode, void* counter, unsigned long long limit_ns, int* gave_up, qk_stream_t stream);
+
 /*
  * FP8 W8A8 GEMV (reference decode.cu:765-774 fp8_gemv, kernels :128-335).
  *   w          packed fp8 [N x K] (model.pack_fp8; gate|up units interleaved for kind 2/7)

@@ -120,6 +120,25 @@ int launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStr
 
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+// The failure path of the bounded waits, on purpose: thread 0 waits, with the given limit, either for phase 0
+// of a fresh mbarrier that nothing arrives on (mode 0, the ring's wait) or for a counter that nothing adds to
+// (mode 1, the cross-GPU counter wait). Both give up, set the device error word and return.
+__global__ void wait_probe_kernel(int mode, const unsigned long long* counter, unsigned long long limit_ns,
+                                  int* gave_up) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x != 0) return;
+  bool ok;
+  if (mode == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    ok = mbar_wait(&bar, 0u, limit_ns);
+  } else {
+    wait_sys_counter(counter, 1ull, limit_ns);
+    ok = ld_acquire_sys_u64(counter) >= 1ull;
+  }
+  *gave_up = ok ? 0 : 1;
+}
+
 struct GemvShape { int warps, stages, stage_tiles, pre, ctas; };
 
 GemvShape gemv_defaults(int kind) {
@@ -180,6 +199,15 @@ int qk_get_device_error(int* err, qk_stream_t stream) {
   if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
   if (e != cudaSuccess) return cuda_fail(e, "reading the device error word");
   return QK_OK;
+}
+
+int qk_wait_probe(int mode, void* counter, unsigned long long limit_ns, int* gave_up, qk_stream_t stream) {
+  if (mode != 0 && mode != 1) return fail(QK_EINVAL, "mode must be 0 (mbarrier) or 1 (counter)");
+  if (!gave_up || (mode == 1 && !counter)) return fail(QK_EINVAL, "null pointer argument");
+  if (!aligned(gave_up, 4) || (counter && !aligned(counter, 8))) return fail(QK_EINVAL, "misaligned pointer");
+  if (limit_ns == 0 || limit_ns > 1000000000ull) return fail(QK_EINVAL, "limit_ns must be in (0, 1e9]");
+  return launch(wait_probe_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream), mode,
+                static_cast<const unsigned long long*>(counter), limit_ns, gave_up);
 }
 
 int qk_fp8_gemv(int kind, const void* w, const float* w_scale, int scale_mode, const void* x, const void* norm_w,

@@ -165,7 +165,8 @@ __device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned 
   return v;
 }
 // Bounded wait until *p >= target (a counter other GPUs add to); sets DEVERR_GRID_TIMEOUT on timeout.
-__device__ __forceinline__ void wait_sys_counter(const unsigned long long* p, unsigned long long target) {
+__device__ __forceinline__ void wait_sys_counter(const unsigned long long* p, unsigned long long target,
+                                                 unsigned long long limit_ns = WAIT_LIMIT_NS) {
   const long long c0 = clock64();
   while (ld_acquire_sys_u64(p) < target && clock64() - c0 < 500000) {
   }
@@ -173,7 +174,7 @@ __device__ __forceinline__ void wait_sys_counter(const unsigned long long* p, un
   const unsigned long long t0 = globaltimer();
   while (ld_acquire_sys_u64(p) < target) {
     if (wait_failed()) return;
-    if (globaltimer() - t0 > WAIT_LIMIT_NS) {
+    if (globaltimer() - t0 > limit_ns) {
       atomicOr(&g_dev_error, DEVERR_GRID_TIMEOUT);
       return;
     }

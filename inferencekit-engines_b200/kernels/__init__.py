@@ -39,6 +39,7 @@ _SIGS = {
     "qk_set_pdl": ([_I], _I),
     "qk_set_timeline": ([_VP, _I], _I),
     "qk_get_device_error": ([ctypes.POINTER(_I), _VP], _I),
+    "qk_wait_probe": ([_I, _VP, ctypes.c_ulonglong, _VP, _VP], _I),
     "qk_fp8_gemv": ([_I, _VP, _VP, _I, _VP, _VP, _VP, _VP, _VP, _I, _I, _F, _VP, _VP, _I, _I, _I, _I, _I, _VP], _I),
     "qk_attention": ([_VP] * 12 + [_I, _I, _I, _I, _I, _I, _F, _F, _I, _VP], _I),
     "qk_lm_head_argmax": ([_VP, _VP, _I, _VP, _VP, _VP, _VP, _I, _I, _F, _VP, _VP, _I, _VP], _I),
