@@ -62,6 +62,23 @@ def test_fused_step_long_context_and_graph():
     assert_same(got, ref)
 
 
+def test_fused_step_across_a_split_boundary():
+    """Positions 61..66: the new key moves from the last slot of split 0 into a new split 1 (the split count
+    goes from 1 to 2 between two steps), eager launches."""
+    m = build(2, "channel")
+    ref = run_steps(m, fused=False, start_pos=61, steps=6, use_graph=False, fill=61)
+    got = run_steps(m, fused=True, start_pos=61, steps=6, use_graph=False, fill=61)
+    assert_same(got, ref)
+
+
+def test_fused_step_at_the_end_of_a_16k_cache():
+    """256 splits per KV head, and the last three positions of the cache (16381..16383), graph replay."""
+    m = build(2, "channel", max_seq=16384)
+    ref = run_steps(m, fused=False, start_pos=16381, steps=3, use_graph=True, fill=16381)
+    got = run_steps(m, fused=True, start_pos=16381, steps=3, use_graph=True, fill=16381)
+    assert_same(got, ref)
+
+
 def test_fused_step_full_model():
     """All 36 layers and the 151,936-row FP8 head: 8 greedy steps at ~4k context, bit-identical."""
     cfg = M.Config()
