@@ -50,7 +50,7 @@ class Engine:
         self.attn = torch.zeros(cfg.n_heads * cfg.head_dim, **bf)
         self.h = torch.zeros(cfg.inter, **bf)
         self.logits = torch.zeros(cfg.vocab, **bf)
-        self.max_splits = (m.max_seq + 31) // 32
+        self.max_splits = (m.max_seq + attn_chunk - 1) // attn_chunk   # fused: 64-key splits, up to 64k context
         self.o_part = torch.zeros(cfg.n_heads, self.max_splits, cfg.head_dim, dtype=torch.float32, device=dev)
         self.ml_part = torch.zeros(cfg.n_heads, self.max_splits, 2, dtype=torch.float32, device=dev)
         self.counters = torch.zeros(cfg.n_kv_heads, dtype=torch.int32, device=dev)

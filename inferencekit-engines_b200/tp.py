@@ -301,7 +301,7 @@ class FusedTPEngine:
         self.attn = torch.zeros(cfg.n_heads * cfg.head_dim, **bf)
         self.h = torch.zeros(cfg.inter, **bf)
         self.logits = torch.zeros(cfg.vocab, **bf)
-        self.max_splits = (m.max_seq + 31) // 32
+        self.max_splits = (m.max_seq + 63) // 64   # 64-key splits: contexts up to 64k
         self.o_part = torch.zeros(cfg.n_heads, self.max_splits, cfg.head_dim, dtype=torch.float32, device=dev)
         self.ml_part = torch.zeros(cfg.n_heads, self.max_splits, 2, dtype=torch.float32, device=dev)
         self.counters = torch.zeros(cfg.n_kv_heads, dtype=torch.int32, device=dev)

@@ -79,6 +79,14 @@ def test_fused_step_at_the_end_of_a_16k_cache():
     assert_same(got, ref)
 
 
+def test_fused_step_at_the_end_of_a_64k_cache():
+    """The longest context the fused step takes: 1,024 splits per KV head, positions 65533..65535."""
+    m = build(2, "channel", max_seq=65536)
+    ref = run_steps(m, fused=False, start_pos=65533, steps=3, use_graph=True, fill=65533)
+    got = run_steps(m, fused=True, start_pos=65533, steps=3, use_graph=True, fill=65533)
+    assert_same(got, ref)
+
+
 def test_fused_step_full_model():
     """All 36 layers and the 151,936-row FP8 head: 8 greedy steps at ~4k context, bit-identical."""
     cfg = M.Config()
