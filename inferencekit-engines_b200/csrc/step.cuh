@@ -30,8 +30,16 @@
 
 namespace qk {
 
-constexpr int ST_WARPS = 8;                        // consumer warps
-constexpr int ST_THREADS = (ST_WARPS + 1) * 32;    // + one producer warp
+constexpr int ST_WARPS = 8;                        // consumer warps (warpgroups 0 and 1)
+constexpr int ST_THREADS = (ST_WARPS + 4) * 32;    // + a producer warpgroup: one warp loads, three exit
+// Register split (setmaxnreg): the CTA launches with 168 registers a thread (65,536 / 384, rounded down to 8),
+// 384 x 168 = 64,512 in all. The producer warpgroup gives its share back down to ST_PRODUCER_REGS and the two
+// consumer warpgroups grow to ST_CONSUMER_REGS: 128 x 56 + 256 x 216 = 62,464 <= 64,512, so the increase
+// never waits on registers that no one returns.
+constexpr int ST_PRODUCER_REGS = 56;
+constexpr int ST_CONSUMER_REGS = 216;
+static_assert(4 * 32 * ST_PRODUCER_REGS + ST_WARPS * 32 * ST_CONSUMER_REGS <= ST_THREADS * 168,
+              "register split exceeds the launch's registers");
 constexpr int ST_STAGE = 32768;
 constexpr int ST_SLICE = 2048;                     // 16 rows x 128 k of fp8
 constexpr int ST_SLICES = ST_STAGE / ST_SLICE;     // 16 slices per stage
@@ -973,8 +981,9 @@ __global__ void __launch_bounds__(ST_THREADS, 1) decode_step_kernel(const __grid
   }
   __syncthreads();
   constexpr int H = HIDDEN, I = 12288 / TP, QKV_N = 6144 / TP, NKV = 8 / TP, NQ = 32 / TP, KO = HIDDEN / TP;
-  if (warp == ST_WARPS) {   // ---------------- producer ----------------
-    if (lane == 0) {
+  if (warp >= ST_WARPS) {   // ---------------- producer ----------------
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(ST_PRODUCER_REGS) : "memory");
+    if (warp == ST_WARPS && lane == 0) {
       Producer pr{&sm, 0, policy_evict_first(), true, 0};
       const AttnItems it = attn_items(pos, NKV);
       for (int l = 0; l < p.n_layers; ++l) {
@@ -1005,6 +1014,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) decode_step_kernel(const __grid
     return;
   }
   // ---------------- consumers ----------------
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(ST_CONSUMER_REGS) : "memory");
   Consumer c{&sm, &p, 0, lane, warp, lane >> 2, lane & 3, -INFINITY, 0x7FFFFFFF, 0, 0};
   unsigned nbar = 0;
   const int tok = p.token[0];
