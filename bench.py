@@ -162,14 +162,23 @@ def step_traffic(bytes_tok):
     return t["dram_bytes_per_launch"] * bytes_tok / t["algorithmic_bytes_per_launch"]
 
 
-def cpu_baseline(ctx: int, budget_s: float = 25.0, threads: int | None = None):
-    """The reference's CPU path (oracle restatement of Q/model.py forward with the decode kernel's fp32
-    attention) on the host cores: one layer decode step at `ctx` (median of a few) and the FP8 lm_head,
-    extrapolated to the 36-layer step."""
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown"
+
+
+def _cpu_layer(ctx: int):
+    """One synthetic decoder layer (per-channel FP8, unit norms) and a KV cache pre-filled to `ctx`, for the
+    CPU restatement of the reference's forward."""
     import model as M
     from oracle import qwen3_ref as O
-    threads = threads or os.cpu_count() or 1
-    torch.set_num_threads(threads)
     H, I = 4096, 12288
     w = {}
     for name, parts in (("qkv", [("q_proj", 4096), ("k_proj", 1024), ("v_proj", 1024)]),
@@ -181,6 +190,19 @@ def cpu_baseline(ctx: int, budget_s: float = 25.0, threads: int | None = None):
     ones = torch.ones(H, dtype=torch.bfloat16)
     hd1 = torch.ones(128, dtype=torch.bfloat16)
     L = O.LayerW(ones, ones, hd1, hd1, *w["qkv"], *w["o_proj"], *w["gate_up"], *w["down_proj"])
+    return L, ones
+
+
+def cpu_baseline(ctx: int, budget_s: float = 25.0, threads: int | None = None):
+    """The reference's CPU path (oracle restatement of Q/model.py forward with the decode kernel's fp32
+    attention) on the host cores, as a bounded sample: a few one-layer decode steps at `ctx` (median) and one
+    FP8 lm_head call, extrapolated to the 36-layer step (36 x layer + head)."""
+    import model as M
+    from oracle import qwen3_ref as O
+    threads = threads or os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    H = 4096
+    L, ones = _cpu_layer(ctx)
     kc = torch.randn(8, ctx + 1, 128).to(torch.bfloat16)
     vc = torch.randn(8, ctx + 1, 128).to(torch.bfloat16)
     cos, sin = M.rope_tables(ctx + 1, 128, 1e6, "cpu")
@@ -200,26 +222,69 @@ def cpu_baseline(ctx: int, budget_s: float = 25.0, threads: int | None = None):
     O.lm_head_logits(h, ones, hw, hs, 1e-6)
     head_s = time.perf_counter() - t0
     step_s = 36 * layer_s + head_s
-    return {"value": 1.0 / step_s, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{len(times)} one-layer decode steps at ctx {ctx} (median {layer_s * 1e3:.1f} ms) + one FP8 "
-                      f"lm_head ({head_s * 1e3:.0f} ms), extrapolated to 36 layers + head",
+    return {"value": 1.0 / step_s, "unit": UNIT, "cores": threads, "cpu_model": cpu_model(), "kind": "port",
+            "extrapolated": True, "layers_timed": len(times) - 1 if len(times) > 1 else 1, "head_calls_timed": 1,
+            "sample": f"{len(times)} one-layer decode steps at ctx {ctx} (first untimed; median {layer_s * 1e3:.1f} "
+                      f"ms) + one FP8 lm_head call ({head_s * 1e3:.0f} ms), extrapolated to 36 layers + head",
             "layer_ms": layer_s * 1e3, "head_ms": head_s * 1e3}
 
 
 def run_reference(args):
+    """The reference's CPU implementation of the decode step (its model.forward math, restated in oracle/)
+    on all host cores: whole 36-layer tokens (embedding row, 36 layers, final norm, FP8 lm_head, greedy
+    argmax), timed as they run. To keep set-up bounded the 36 layers share one synthetic layer's weights
+    (each layer keeps its own KV cache); the arithmetic per token is the full step's. Steps past a time
+    budget are not run: `steps` is the number actually timed and `steps_requested` the asked-for K."""
     ws, rank, _ = dist_env()
     if rank != 0:
         return
+    import model as M
+    from oracle import qwen3_ref as O
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
     ctx = 4096 - args.steps
-    base = cpu_baseline(ctx, budget_s=max(20.0, 0.5 * (args.steps + args.warmup)))
-    out = {"metric": METRIC, "value": base["value"], "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
-           "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 / base["value"], "higher_is_better": True,
-           "scaling": "weak", "vs_baseline": None, "dtype": "fp8-e4m3 x fp8 -> fp32 (bf16 activations)",
+    H, n_layers = 4096, 36
+    L, ones = _cpu_layer(ctx)
+    g = torch.Generator().manual_seed(1234)
+    kcs = [torch.randn(8, 4096, 128, generator=g).to(torch.bfloat16) for _ in range(n_layers)]
+    vcs = [torch.randn(8, 4096, 128, generator=g).to(torch.bfloat16) for _ in range(n_layers)]
+    cos, sin = M.rope_tables(4096, 128, 1e6, "cpu")
+    embed = M.randn((151936, H), 0, "cpu.embed", std=0.02).to(torch.bfloat16)
+    hw, hs = M.quantize_fp8(M.randn((151936, H), 0, "cpu.head", std=0.02), "channel")
+    layers = [L] * n_layers
+
+    def token_step(tok, pos):
+        nxt, _ = O.decode_step(tok, pos, embed, layers, kcs, vcs, cos, sin, ones, hw, hs, 1e-6, attn_impl="f32")
+        return nxt
+
+    tok, pos = 1, ctx
+    warm = min(args.warmup, 2)
+    for _ in range(warm):
+        tok = token_step(tok, pos)
+    budget_s = float(os.environ.get("QK_REFERENCE_BUDGET_S", "90"))
+    tok, pos, done = 1, ctx, 0
+    t0 = time.perf_counter()
+    while done < args.steps:
+        tok = token_step(tok, pos)
+        pos += 1
+        done += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    t = time.perf_counter() - t0
+    value = done / t
+    base = {"value": value, "unit": UNIT, "cores": threads, "cpu_model": cpu_model(), "kind": "port",
+            "extrapolated": False,
+            "sample": f"{done} whole decode tokens (36 layers sharing one synthetic layer's weights, own KV caches "
+                      f"from ctx {ctx}, FP8 lm_head, greedy argmax) after {warm} untimed"}
+    out = {"metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
+           "steps": done, "steps_requested": args.steps, "warmup": warm, "ms_per_step": t / done * 1e3,
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+           "dtype": "fp8-e4m3 x fp8 -> fp32 (bf16 activations)",
            "data": "synthetic (seeded random-init weights, N(0,1) KV)",
            "config": {"workload": f"reference CPU path: Qwen3-8B-shape decode step at ctx {ctx}", "global_batch": 1,
                       "seq_len": 4096, "parallelism": "cpu"},
            "cpu_baseline": base,
-           "e2e": {"value": base["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+           "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(out), flush=True)
 
 
@@ -430,6 +495,82 @@ def run_profile_kernel(args):
     print(f"profiled {args.profile_kernel} x{args.launches}")
 
 
+PHASES = ("qkv", "attn", "o_proj", "gate_up", "down")
+
+
+def timeline_summary(tl, n_layers: int, clock_ghz: float = 1.965) -> dict:
+    """Per-phase breakdown of one fused-step launch from its timeline (int64 [CTAs, 5*layers+1, 8], words as in
+    csrc/step.cuh: 0 consumers start the phase, 1 prologue done (attention: merge start), 2 phase work done,
+    3 producer's first load of the phase, 4-6 cumulative clock64 cycles (consumer warp 0 waiting for ring
+    stages, folding units; producer waiting for free slots), 7 stage loop left (attention: partials done)).
+    Times in us: medians over CTAs, then over layers 1..n-1 (layer 0 includes the launch ramp). `barrier` is
+    the time from a CTA's end of the phase to its start of the next one; `ring_wait` the consumer's stage waits
+    inside the phase; `producer_wait` the producer's waits for free slots while issuing the phase."""
+    import numpy as np
+    t = tl.cpu().numpy().astype(np.int64)
+    G, P = t.shape[0], t.shape[1]
+    us = lambda a: a / 1e3                 # noqa: E731  (globaltimer: ns)
+    cyc = lambda a: a / (clock_ghz * 1e3)  # noqa: E731  (clock64 cycles -> us)
+    cw = np.diff(np.concatenate([np.zeros((G, 1), np.int64), t[:, :, 4]], axis=1), axis=1)   # per phase
+    pw = np.diff(np.concatenate([t[:, :, 6], t[:, -1:, 6]], axis=1), axis=1)                 # phase -> next phase
+    start = lambda ph: t[:, ph, 0] if ph < P else None   # noqa: E731
+    names = {0: "qkv", 2: "o_proj", 3: "gate_up", 4: "down"}
+    per = {k: [] for k in ("qkv", "attn", "merge", "o_proj", "gate_up", "down")}
+    layer_us = []
+    for l in (range(1, n_layers) if n_layers > 1 else range(n_layers)):
+        b = 5 * l
+        for j, name in names.items():
+            ph = t[:, b + j]
+            nxt = start(b + j + 1)
+            per[name].append(dict(prologue=us(ph[:, 1] - ph[:, 0]), stage_loop=us(ph[:, 7] - ph[:, 1]),
+                                  tail=us(ph[:, 2] - ph[:, 7]), barrier=us(nxt - ph[:, 2]),
+                                  ring_wait=cyc(cw[:, b + j]), producer_wait=cyc(pw[:, b + j])))
+        a = t[:, b + 1]
+        per["attn"].append(dict(work=us(a[:, 7] - a[:, 0]), barrier=us(a[:, 1] - a[:, 7]),
+                                producer_wait=cyc(pw[:, b + 1])))
+        per["merge"].append(dict(work=us(a[:64, 2] - a[:64, 1]), barrier=us(t[:, b + 2, 0] - a[:, 2]),
+                                 ring_wait_attn_and_merge=cyc(cw[:, b + 1])))
+        layer_us.append(np.median(us(start(b + 5) - t[:, b, 0])))
+    out = {"ctas": G, "layers": n_layers, "layer_us": float(np.median(layer_us))}
+    for k, v in per.items():
+        out[k] = {f: round(float(np.median([np.median(d[f]) for d in v])), 3) for f in v[0]}
+    h = t[:, 5 * n_layers]
+    out["head"] = {"prologue": float(np.median(us(h[:, 1] - h[:, 0]))),
+                   "stage_loop": float(np.median(us(h[:, 7] - h[:, 1]))),
+                   "tail": float(np.median(us(h[:, 2] - h[:, 7])))}
+    out["launch_us"] = float(us(h[:, 2].max() - t[:, 0, 0].min()))
+    # how far ahead of the consumers the producer issued each phase's first load
+    lead = [np.median(us(t[:, p, 0] - t[:, p, 3])) for p in range(5, 5 * n_layers)]
+    out["producer_lead_us"] = float(np.median(lead))
+    return out
+
+
+def run_timeline(args):
+    """Fused step with its timeline on: warm-up launches, then one launch whose per-phase stamps are summarised
+    (the 36-layer model at the bench's 4k context unless --layers is given)."""
+    import model as M
+    from generate import Engine
+    cfg = M.Config(layers=args.layers if args.layers != 2 else 36)
+    max_seq = 4096
+    start = max_seq - 64
+    m = M.Qwen3FP8Decode.synthetic(cfg, max_seq=max_seq, device="cuda", seed=0, scale_mode="channel", head_dtype="fp8",
+                                   norm_init="ones")
+    m.fill_cache_random(start, seed=1234)
+    eng = Engine(m, fused=True)
+    n = len(m.layers)
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    eng.step_timeline = torch.zeros(sms, 5 * n + 1, 8, dtype=torch.int64, device="cuda")
+    eng.token.fill_(1)
+    eng.state.copy_(torch.tensor([start, 0], dtype=torch.int32))
+    for _ in range(args.launches):
+        eng.decode_step()
+    torch.cuda.synchronize()
+    eng.check()
+    summ = timeline_summary(eng.step_timeline, n)
+    summ["ctx"] = start + args.launches - 1
+    print(json.dumps({"timeline": summ}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--profile-kernel", choices=["qkv", "o_proj", "gate_up", "down", "lm_head", "attention", "decode_step"],
@@ -448,7 +589,11 @@ def main():
     ap.add_argument("--path", default="fused", choices=["fused", "ops"],
                     help="fused: one persistent kernel per token; ops: the reference's 183 per-op launches")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--timeline", action="store_true",
+                    help="one fused-step launch with per-phase timeline stamps, summarised (36 layers unless --layers)")
     args = ap.parse_args()
+    if args.timeline:
+        return run_timeline(args)
     if args.profile_kernel:
         return run_profile_kernel(args)
     if args.warmup < 3:

@@ -190,7 +190,9 @@ int qk_decode_step(const qk_layer_t* layers, int n_layers, void* k_cache, void* 
  *              qk_tp_area_open on each peer's handle. Areas start zeroed and must not be reset between launches.
  *   resid_alt  a second bf16 [4096] residual buffer
  * All ranks must launch the same number of steps; a rank that stops makes the others' bounded waits time out
- * and set the device error word (qk_get_device_error).
+ * and set the device error word (qk_get_device_error). After such a timeout the ranks' launch epochs differ
+ * and every later step would time out as well: every rank then resets its own area with qk_tp_area_reset
+ * (and zeroes its step scratch counters, sync and best), between two host barriers with no launch in flight.
  */
 typedef struct {
   int tp;                   /* ranks: 2, 4 or 8 */
@@ -203,6 +205,8 @@ int qk_tp_area_alloc(void** area, void* ipc_handle /* 64 bytes out */);
 int qk_tp_area_open(const void* ipc_handle, void** peer_area);
 int qk_tp_area_close(void* peer_area);
 int qk_tp_area_free(void* area);
+/* Zero this rank's own TP area (receive words, key counter, epoch) on `stream`: recovery after a failed step. */
+int qk_tp_area_reset(void* area, qk_stream_t stream);
 int qk_decode_step_tp(const qk_layer_t* layers, int n_layers, void* k_cache, void* v_cache, long long kv_layer_stride,
                       const void* embed, const void* final_norm, const void* w_head, const float* s_head, int vocab,
                       const void* cos_tab, const void* sin_tab, int* token, int* state, int* out_tokens,

@@ -161,6 +161,34 @@ int launch_gemv_scaled(int scale_mode, const GemvParams& p, const GemvShape& sh,
   return launch(k, grid, block, smem, stream, p);
 }
 
+
+// Every argument check of qk_fp8_gemv, before anything is enqueued (also run by qk_fp8_gemv_noalloc ahead of
+// its counter reset, so a rejected call leaves nothing on the stream).
+int gemv_check(int kind, const void* w, const float* w_scale, int scale_mode, const void* x, const void* norm_w,
+               const float* resadd, const void* resid_out, const void* out, int N, int K, const float* part,
+               const int* counters, const GemvShape& sh, bool library_scratch = false) {
+  if (sh.warps < 4 || sh.warps > 16) return fail(QK_EINVAL, "warps must be in [4, 16], got %d", sh.warps);
+  if (sh.stages < 1 || sh.stages > 16 || sh.stage_tiles < 1 || sh.stage_tiles > 64 || sh.ctas < 1 || sh.ctas > 8)
+    return fail(QK_EINVAL, "bad launch shape stages=%d stage_tiles=%d ctas_per_sm=%d", sh.stages, sh.stage_tiles, sh.ctas);
+  if (!w || !w_scale || !x || !out || (!library_scratch && (!part || !counters)))
+    return fail(QK_EINVAL, "null pointer argument");
+  if (scale_mode != QK_SCALE_BLOCK128 && scale_mode != QK_SCALE_CHANNEL) return fail(QK_EINVAL, "bad scale_mode %d", scale_mode);
+  if (K <= 0 || K % QB || K > 16384) return fail(QK_EINVAL, "K=%d must be a positive multiple of 128, at most 16384", K);
+  const bool pairs = (kind == QK_GEMV_GATE_UP || kind == QK_GEMV_GATE_UP_RESADD);
+  if (N <= 0 || N % (pairs ? 32 : 16)) return fail(QK_EINVAL, "N=%d must be a positive multiple of %d", N, pairs ? 32 : 16);
+  if (scale_mode == QK_SCALE_BLOCK128 && N % QB) return fail(QK_EINVAL, "block-128 scales need N %% 128 == 0 (N=%d)", N);
+  const bool norm = (kind == QK_GEMV_QKV || kind == QK_GEMV_GATE_UP || kind == QK_GEMV_QKV_RESADD || kind == QK_GEMV_GATE_UP_RESADD);
+  const bool resadd_k = (kind == QK_GEMV_QKV_RESADD || kind == QK_GEMV_GATE_UP_RESADD);
+  const bool known = norm || kind == QK_GEMV_O || kind == QK_GEMV_DOWN || kind == QK_GEMV_PARTIAL;
+  if (!known) return fail(QK_EINVAL, "unknown gemv kind %d", kind);
+  if (norm && !norm_w) return fail(QK_EINVAL, "kind %d needs norm_w", kind);
+  if (resadd_k && (!resadd || !resid_out)) return fail(QK_EINVAL, "kind %d needs resadd and resid_out", kind);
+  if (!aligned(w, 16) || !aligned(x, 16) || !aligned(out, 16) || !aligned(w_scale, 8) ||
+      (!library_scratch && !aligned(part, 16)) || (norm_w && !aligned(norm_w, 16)) || (resadd && !aligned(resadd, 16)) ||
+      (resid_out && !aligned(resid_out, 16)))
+    return fail(QK_EINVAL, "tensor pointers must be 16-byte aligned");
+  return QK_OK;
+}
 }  // namespace
 
 extern "C" {
@@ -219,22 +247,8 @@ int qk_fp8_gemv(int kind, const void* w, const float* w_scale, int scale_mode, c
   if (stage_tiles) sh.stage_tiles = stage_tiles;
   if (pre >= 0) sh.pre = pre;
   if (ctas_per_sm) sh.ctas = ctas_per_sm;
-  if (sh.warps < 4 || sh.warps > 16) return fail(QK_EINVAL, "warps must be in [4, 16], got %d", sh.warps);
-  if (sh.stages < 1 || sh.stages > 16 || sh.stage_tiles < 1 || sh.stage_tiles > 64 || sh.ctas < 1 || sh.ctas > 8)
-    return fail(QK_EINVAL, "bad launch shape stages=%d stage_tiles=%d ctas_per_sm=%d", sh.stages, sh.stage_tiles, sh.ctas);
-  if (!w || !w_scale || !x || !out || !part || !counters) return fail(QK_EINVAL, "null pointer argument");
-  if (scale_mode != QK_SCALE_BLOCK128 && scale_mode != QK_SCALE_CHANNEL) return fail(QK_EINVAL, "bad scale_mode %d", scale_mode);
-  if (K <= 0 || K % QB || K > 16384) return fail(QK_EINVAL, "K=%d must be a positive multiple of 128, at most 16384", K);
-  const bool pairs = (kind == QK_GEMV_GATE_UP || kind == QK_GEMV_GATE_UP_RESADD);
-  if (N <= 0 || N % (pairs ? 32 : 16)) return fail(QK_EINVAL, "N=%d must be a positive multiple of %d", N, pairs ? 32 : 16);
-  if (scale_mode == QK_SCALE_BLOCK128 && N % QB) return fail(QK_EINVAL, "block-128 scales need N %% 128 == 0 (N=%d)", N);
-  const bool norm = (kind == QK_GEMV_QKV || kind == QK_GEMV_GATE_UP || kind == QK_GEMV_QKV_RESADD || kind == QK_GEMV_GATE_UP_RESADD);
-  const bool resadd_k = (kind == QK_GEMV_QKV_RESADD || kind == QK_GEMV_GATE_UP_RESADD);
-  if (norm && !norm_w) return fail(QK_EINVAL, "kind %d needs norm_w", kind);
-  if (resadd_k && (!resadd || !resid_out)) return fail(QK_EINVAL, "kind %d needs resadd and resid_out", kind);
-  if (!aligned(w, 16) || !aligned(x, 16) || !aligned(out, 16) || !aligned(w_scale, 8) || !aligned(part, 16) ||
-      (norm_w && !aligned(norm_w, 16)) || (resadd && !aligned(resadd, 16)) || (resid_out && !aligned(resid_out, 16)))
-    return fail(QK_EINVAL, "tensor pointers must be 16-byte aligned");
+  if (int r = gemv_check(kind, w, w_scale, scale_mode, x, norm_w, resadd, resid_out, out, N, K, part, counters, sh))
+    return r;
   GemvParams p = {};
   p.w = static_cast<const uint8_t*>(w);
   p.ws = w_scale;
@@ -519,6 +533,12 @@ int qk_tp_area_free(void* area) {
   return e == cudaSuccess ? QK_OK : cuda_fail(e, "cudaFree (TP area)");
 }
 
+int qk_tp_area_reset(void* area, qk_stream_t stream) {
+  if (!area) return fail(QK_EINVAL, "null pointer argument");
+  const cudaError_t e = cudaMemsetAsync(area, 0, sizeof(TpArea), static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? QK_OK : cuda_fail(e, "cudaMemsetAsync (TP area reset)");
+}
+
 int qk_decode_step_tp(const qk_layer_t* layers, int n_layers, void* k_cache, void* v_cache, long long kv_layer_stride,
                       const void* embed, const void* final_norm, const void* w_head, const float* s_head, int vocab,
                       const void* cos_tab, const void* sin_tab, int* token, int* state, int* out_tokens,
@@ -582,24 +602,15 @@ constexpr size_t NOALLOC_COUNTERS = 4096;          // max N/16
 constexpr size_t NOALLOC_BYTES = NOALLOC_PART_FLOATS * 4 + NOALLOC_COUNTERS * 4;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[NOALLOC_BYTES];
 
-std::mutex g_noalloc_mu;
-unsigned char* g_noalloc_addr[64] = {nullptr};   // device address of the array, per device
-
-// The array's name in host code is only a host-side stand-in: its device address has to be looked up, once
-// per device, with that device current.
+// The array's name in host code is only a host-side stand-in: its device address is looked up with the
+// device current. The lookup is repeated on every call (it is cheap and allocates nothing), so the address
+// stays right after a cudaDeviceReset reloads the module at another address. The first call on a device
+// loads the library's module there, so make it before any stream capture.
 int noalloc_scratch(unsigned char** out) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
-  if (dev < 0 || dev >= 64) return fail(QK_EINVAL, "device index %d out of range", dev);
-  std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  if (g_noalloc_addr[dev] == nullptr) {
-    void* ptr = nullptr;
-    e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress of the no-alloc scratch");
-    g_noalloc_addr[dev] = static_cast<unsigned char*>(ptr);
-  }
-  *out = g_noalloc_addr[dev];
+  void* ptr = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress of the no-alloc scratch");
+  *out = static_cast<unsigned char*>(ptr);
   return QK_OK;
 }
 }  // namespace
@@ -612,6 +623,10 @@ extern "C" int qk_fp8_gemv_noalloc(int kind, const void* w, const float* w_scale
   if (part > NOALLOC_PART_FLOATS || units > NOALLOC_COUNTERS)
     return fail(QK_EINVAL, "N=%d K=%d exceeds the no-alloc scratch (N*K/128 <= %zu, N/16 <= %zu); use qk_fp8_gemv",
                 N, K, NOALLOC_PART_FLOATS, NOALLOC_COUNTERS);
+  // every check of qk_fp8_gemv first, so that a rejected call enqueues nothing (not even the counter reset)
+  if (int r = gemv_check(kind, w, w_scale, scale_mode, x, norm_w, resadd, resid_out, out, N, K, nullptr, nullptr,
+                         gemv_defaults(kind), true))
+    return r;
   unsigned char* base = nullptr;
   if (int r = noalloc_scratch(&base)) return r;
   float* part_ptr = reinterpret_cast<float*>(base);

@@ -162,13 +162,38 @@ class Engine:
         self.state[1].fill_(0)
         return self.token.clone()
 
+    def check(self):
+        """Raise RuntimeError if a kernel recorded a device error since the last check: a bounded wait that
+        gave up (its step's outputs are not valid) or a position / token id out of range. Reads and clears
+        the error word (a host sync). After a wait has timed out, every later wait gives up at once until
+        this read clears the word, so a caller that sees the error should stop and rebuild its state."""
+        err = self.k.device_error()
+        if err:
+            raise RuntimeError(f"decode step failed on the device (error word {err:#x}: 1 = a ring wait timed out, "
+                               "2 = bad position or token, 4 = a grid or peer wait timed out)")
+
+    def recover(self):
+        """Reset the step's scratch counters after a failed step (a wait that gave up leaves them mid-count):
+        the fused step's grid-barrier, GEMV-unit and attention counters and the argmax key, or the op path's
+        counters. Call it between steps, with no launch in flight; clears the device error word."""
+        torch.cuda.synchronize()
+        for t in (self.counters, self.best) + ((self.sync, self.gemv_counters) if self.fused else ()):
+            t.zero_()
+        if not self.fused:
+            for _, cnt in self.k._scratch.values():
+                cnt.zero_()
+        torch.cuda.synchronize()
+        self.k.device_error()
+
     @torch.no_grad()
     def generate(self, prompt_ids, gen_len: int, use_graph: bool = True):
-        """Greedy generation of exactly gen_len tokens (no early stop). Returns a list of ids."""
+        """Greedy generation of exactly gen_len tokens (no early stop). Returns a list of ids; raises
+        RuntimeError if any step recorded a device error (see `check`)."""
         assert len(prompt_ids) + gen_len <= self.max_seq
         first = self.prefill(prompt_ids, use_graph)
         if gen_len > 1:
             self.step(gen_len - 1, use_graph)
         out = [int(first.item())]
         out += self.out_tokens[: gen_len - 1].tolist()
+        self.check()
         return out

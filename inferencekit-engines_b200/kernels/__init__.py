@@ -8,10 +8,13 @@ CUDA graph exactly as before. There is no fallback: if the library is missing or
 sm_100 GPU, `ops()` raises.
 
 Differences a caller must know:
-  * FP8 weights must be in `model.pack_fp8` layout (the B200 kernels' tile order). The reference's
-    `kmajor` argument is accepted and ignored; `depth` maps to ring stages per warp, `warps` to warps per
-    CTA, `pre` to ring stages issued before waiting on the previous kernel; `trig` is accepted and ignored
-    (every kernel lets its successor launch right after its own wait).
+  * FP8 weights must be in `model.pack_fp8` layout (the B200 kernels' tile order). `pack_fp8` returns a
+    `PackedFP8` tensor (`PackedFP8Pairs` for gate|up); `fp8_gemv` and the FP8 `lm_head_argmax` raise
+    RuntimeError for any other tensor, e.g. weights in the reference's `tile_fp8` layout (convert those
+    with `model.pack_reference_tiled`). `depth` maps to ring stages per warp, `warps` to warps per CTA,
+    `pre` to ring stages issued before waiting on the previous kernel. `kmajor` must be 0 or 1 and `trig`
+    must be -1 or a K block in [0, K/128), as in the reference; neither changes anything here (the layout
+    is fixed by the tag, and every kernel lets its successor launch right after its own wait).
   * Scales may be 128x128 blocks [N/128, K/128] or per output channel [N]; the layout is read off the
     tensor's shape.
   * `lm_head_argmax` also takes an FP8 head: pass `w_scale=` (fp32 [V]) with packed fp8 weights.
@@ -55,6 +58,7 @@ _SIGS = {
     "qk_tp_area_open": ([_VP, ctypes.POINTER(_VP)], _I),
     "qk_tp_area_close": ([_VP], _I),
     "qk_tp_area_free": ([_VP], _I),
+    "qk_tp_area_reset": ([_VP, _VP], _I),
     "qk_residual_add": ([_VP, _VP, _I, _VP], _I),
     "qk_argmax_key_flip": ([_VP, _I, _VP], _I),
     "qk_decode_step_part_floats": ([_I], ctypes.c_longlong),
@@ -62,6 +66,25 @@ _SIGS = {
     "qk_fp8_gemv_noalloc": ([_I, _VP, _VP, _I, _VP, _VP, _VP, _VP, _VP, _I, _I, _F, _VP], _I),
     "qk_finalize": ([_VP, _VP, _VP, _VP, _I, _I, _VP], _I),
 }
+
+
+class PackedFP8(torch.Tensor):
+    """uint8 weights in the `model.pack_fp8` layout (16-row units of 2 KiB tiles). The type survives
+    `.to()`, `.cuda()`, views and slicing, so the ops can tell packed weights from any other fp8/uint8
+    tensor of the same size."""
+
+
+class PackedFP8Pairs(PackedFP8):
+    """gate|up weights packed as 16 gate rows + the matching 16 up rows per unit (`pack_fp8(w, pairs=True)`)."""
+
+
+def check_packed(w, pairs: bool, what: str):
+    """Raise RuntimeError unless `w` is a pack_fp8 tensor of the right kind (gate|up pairs or plain)."""
+    if not isinstance(w, PackedFP8) or isinstance(w, PackedFP8Pairs) != pairs:
+        want = "pack_fp8(w, pairs=True)" if pairs else "pack_fp8(w)"
+        got = type(w).__name__ if isinstance(w, PackedFP8) else f"an untagged {getattr(w, 'dtype', type(w))} tensor"
+        raise RuntimeError(f"{what}: weights must be in the model.{want} layout, got {got} (weights in the "
+                           "reference's tile_fp8 layout convert with model.pack_reference_tiled)")
 
 
 def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
@@ -140,7 +163,12 @@ class DecodeOps:
     def fp8_gemv(self, kind, w, ws, x, norm_w, out, N, eps, depth=0, warps=0, pre=-1, trig=-1, kmajor=1,
                  resadd=None, resid_out=None, stage_tiles=0, ctas_per_sm=0):
         N = int(N)
+        check_packed(w, int(kind) in (GEMV_GATE_UP, GEMV_GATE_UP_RESADD), "fp8_gemv")
         K = w.numel() // N
+        if int(kmajor) not in (0, 1):
+            raise RuntimeError(f"fp8_gemv: kmajor must be 0 or 1, got {kmajor}")
+        if int(trig) != -1 and not 0 <= int(trig) < K // 128:
+            raise RuntimeError(f"fp8_gemv: trig must be -1 or a K block in [0, {K // 128}), got {trig}")
         scale_mode = SCALE_CHANNEL if ws.dim() == 1 else SCALE_BLOCK128
         part, counters = self.scratch(w.device, N * K // 128, N // 8)
         st = self.lib.qk_fp8_gemv(int(kind), _p(w), _p(ws), scale_mode, _p(x), _p(norm_w), _p(resadd),
@@ -173,7 +201,10 @@ class DecodeOps:
         fp8 = w_scale is not None
         part = counters = None
         if fp8:
+            check_packed(w, False, "lm_head_argmax")
             part, counters = self.scratch(w.device, V * 4096 // 128, V // 8)
+        elif w.dtype != torch.bfloat16 or isinstance(w, PackedFP8):
+            raise RuntimeError("lm_head_argmax: a bf16 [V, 4096] head, or packed fp8 weights with w_scale=")
         st = self.lib.qk_lm_head_argmax(_p(w), _p(w_scale), int(fp8), _p(x), _p(norm_w), _p(logits), _p(best), V,
                                         int(row_offset), float(eps), _p(part), _p(counters), int(ctas), _stream())
         self._check(st, "lm_head_argmax")
@@ -231,6 +262,10 @@ class DecodeOps:
 
     def tp_area_free(self, area):
         self._check(self.lib.qk_tp_area_free(ctypes.c_void_p(area)), "tp_area_free")
+
+    def tp_area_reset(self, area):
+        """Zero this rank's own TP area on the current stream (recovery after a failed step)."""
+        self._check(self.lib.qk_tp_area_reset(ctypes.c_void_p(area), _stream()), "tp_area_reset")
 
     def residual_add(self, resid, sum_f32):
         """resid = bf16(resid + bf16(sum)) (after the all-reduce of a row-parallel partial)."""

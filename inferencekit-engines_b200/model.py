@@ -25,6 +25,8 @@ from dataclasses import dataclass, field
 
 import torch
 
+from kernels import PackedFP8, PackedFP8Pairs
+
 FP8 = torch.float8_e4m3fn
 FP8_MAX = 448.0
 QBLOCK = 128
@@ -124,23 +126,39 @@ def pack_fp8(w: torch.Tensor, pairs: bool = False) -> torch.Tensor:
     """
     N, K = w.shape
     assert w.dtype == FP8 and N % 16 == 0 and K % QBLOCK == 0
+    w = w.as_subclass(torch.Tensor)
     KB = K // QBLOCK
     u8 = w.contiguous().view(torch.uint8)
     if pairs:
         assert N % 32 == 0
         half = N // 2
-        g = pack_fp8(w[:half]).view(half // 16, KB, 1, 2048)
-        u = pack_fp8(w[half:]).view(half // 16, KB, 1, 2048)
-        return torch.cat([g, u], dim=2).reshape(-1).contiguous()
+        g = pack_fp8(w[:half]).as_subclass(torch.Tensor).view(half // 16, KB, 1, 2048)
+        u = pack_fp8(w[half:]).as_subclass(torch.Tensor).view(half // 16, KB, 1, 2048)
+        return torch.cat([g, u], dim=2).reshape(-1).contiguous().as_subclass(PackedFP8Pairs)
     # element (n, k): n = 16*u + 8*hh + g, k = 128*kb + 32*c + 16*hi + 4*t + b
     v = u8.view(N // 16, 2, 8, KB, 4, 2, 4, 4)           # [u, hh, g, kb, c, hi, t, b]
     v = v.permute(0, 3, 4, 2, 6, 5, 1, 7)                 # [u, kb, c, g, t, hi, hh, b]
-    return v.contiguous().view(-1)
+    return v.contiguous().view(-1).as_subclass(PackedFP8)
+
+
+def pack_reference_tiled(wt: torch.Tensor, kmajor: bool, pairs: bool = False) -> torch.Tensor:
+    """Weights in the reference's mma-tiled layout (qwen3-8b-fp8_rtx-5090/model.py:92-104, `tile_fp8`, fp8
+    [N, K]) -> `pack_fp8` layout. That layout groups 8 rows and 64-wide K chunks into 512-byte tiles, either
+    group-major ([ng, kc, g, t, q, b]) or K-major ([kc, ng, g, t, q, b]), with element (n, k) at
+    n = 8*ng + g, k = 64*kc + 16*q + 4*t + b; undoing that order gives the row-major matrix."""
+    N, K = wt.shape
+    v = wt.as_subclass(torch.Tensor).contiguous().view(torch.uint8)
+    if kmajor:
+        v = v.view(K // 64, N // 8, 8, 4, 4, 4).permute(1, 2, 0, 4, 3, 5)   # -> [ng, g, kc, q, t, b]
+    else:
+        v = v.view(N // 8, K // 64, 8, 4, 4, 4).permute(0, 2, 1, 4, 3, 5)
+    return pack_fp8(v.contiguous().view(N, K).view(FP8), pairs)
 
 
 def unpack_fp8(p: torch.Tensor, N: int, K: int, pairs: bool = False) -> torch.Tensor:
     """Inverse of pack_fp8 (tests and TP re-sharding)."""
     KB = K // QBLOCK
+    p = p.as_subclass(torch.Tensor)
     if pairs:
         half = N // 2
         v = p.view(torch.uint8).view(half // 16, KB, 2, 2048)
@@ -170,7 +188,7 @@ class Layer:
 
 @dataclass
 class Linear:
-    packed: torch.Tensor        # uint8, pack_fp8 layout
+    packed: torch.Tensor        # PackedFP8 (uint8, pack_fp8 layout)
     scale: torch.Tensor         # fp32 [N] (channel) or [N/128, K/128] (block)
     N: int
     K: int

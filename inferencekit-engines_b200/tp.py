@@ -265,6 +265,12 @@ class TPEngine:
             else:
                 self.decode_step()
 
+    def check(self):
+        """Raise RuntimeError if a kernel of this rank recorded a device error (reads and clears the word)."""
+        err = self.k.device_error()
+        if err:
+            raise RuntimeError(f"rank {self.part.rank}: decode step failed on the device (error word {err:#x})")
+
     def release(self):
         """Drop the graph (it holds NCCL work) before the process group is destroyed."""
         self.graph = None
@@ -360,6 +366,29 @@ class FusedTPEngine:
                 self.graph.replay()
             else:
                 self.decode_step()
+
+    def check(self):
+        """Raise RuntimeError if this rank's kernel recorded a device error (reads and clears the word). A
+        timed-out exchange (a peer that did not run the step) leaves the ranks' launch epochs apart, so
+        every later step would time out too: call `recover()` on every rank before stepping again."""
+        err = self.k.device_error()
+        if err:
+            raise RuntimeError(f"rank {self.part_.rank}: fused TP step failed on the device (error word {err:#x}); "
+                               "call recover() on every rank before the next step")
+
+    def recover(self):
+        """Bring every rank back to a clean exchange state after a failed step. Collective: every rank calls
+        it, between steps, with no launch in flight. Each rank zeroes its own TP area (receive words, key
+        counter, epoch) and its step scratch counters between two barriers, so no peer store of the failed
+        step can land after the reset and all ranks restart from epoch 0."""
+        torch.cuda.synchronize()
+        self.dist.barrier(group=self.group)
+        self.k.tp_area_reset(self.area)
+        for t in (self.gemv_counters, self.counters, self.sync, self.best):
+            t.zero_()
+        torch.cuda.synchronize()
+        self.k.device_error()
+        self.dist.barrier(group=self.group)
 
     def release(self):
         """Unmap the peers' areas and free this rank's (after every rank has finished its launches)."""

@@ -4,7 +4,8 @@ Test infrastructure only: the result is the GPU checker for bit-exactness tests 
 source is read where it lies in the reference checkout; nothing is copied into this repository. This is a
 direct nvcc command of our own (not the reference's JIT loader): sm_100a, -O3, the same flags the reference
 passes to its JIT build (-O3 -lineinfo), torch's extension headers for its pybind11 module.
-    python oracle/build_ref.py [--ref /root/reference/qwen3-8b-fp8_rtx-5090]
+    python oracle/build_ref.py [--ref <reference checkout>/qwen3-8b-fp8_rtx-5090]
+(default: refpath.engine_dir(), i.e. $QK_REFERENCE_DIR or a `reference` folder beside the repository)
 """
 import argparse
 import os
@@ -16,11 +17,13 @@ import torch
 from torch.utils import cpp_extension
 
 HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+import refpath  # noqa: E402
 
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference/qwen3-8b-fp8_rtx-5090")
+    ap.add_argument("--ref", default=refpath.engine_dir())
     args = ap.parse_args()
     src = os.path.join(args.ref, "kernels", "decode.cu")
     out_dir = os.path.join(HERE, "_ref")

@@ -76,7 +76,7 @@ def fp8_linear_f32(x: torch.Tensor, w: torch.Tensor, w_scale: torch.Tensor) -> t
     KB = K // QBLOCK
     d = block_dots(q, w)                                           # [M, N, KB]
     terms = d * s[:, None, :] * scale_rows(w_scale, N, KB)[None]
-    acc = torch.zeros(M, N, dtype=torch.float32)
+    acc = torch.zeros(M, N, dtype=torch.float32, device=x.device)
     for kb in range(KB):                                           # in K order, like the kernels
         acc = acc + terms[..., kb]
     return acc

@@ -1,7 +1,8 @@
 """Generate the golden fixtures in this folder from the reference's own Python forward pass.
 
 Runs ONLY where the reference checkout exists (it is read, never modified):
-    python tests/golden/make_golden.py [--ref /root/reference/qwen3-8b-fp8_rtx-5090]
+    python tests/golden/make_golden.py [--ref <reference checkout>/qwen3-8b-fp8_rtx-5090]
+(default: oracle/refpath.py's engine_dir(), i.e. $QK_REFERENCE_DIR or a `reference` folder beside the repo)
 
 What it does: imports the reference's `model.py` (qwen3-8b-fp8_rtx-5090/model.py), replaces its module-level
 `fp8_linear` (imported from the Triton kernels at model.py:18) with the CPU restatement in
@@ -36,6 +37,7 @@ sys.path.insert(0, REPO)
 sys.path.insert(0, os.path.join(REPO, "inferencekit-engines_b200"))
 
 from oracle import qwen3_ref as O  # noqa: E402
+from oracle import refpath  # noqa: E402
 import model as M  # noqa: E402  (the package's synthetic generator)
 
 sys.path.pop(0)  # keep the package's `model` out of the way of the reference's
@@ -54,12 +56,16 @@ def checksum(*ts) -> str:
 
 def load_reference(ref_dir: str):
     """Import the reference's model.py with its Triton GEMM swapped for the CPU restatement."""
+    # the package's `model` and `kernels` share their names with the reference's modules: set them aside
+    ours = {k: sys.modules.pop(k) for k in list(sys.modules) if k in ("model", "kernels") or k.startswith("kernels.")}
     sys.path.insert(0, ref_dir)
     try:
-        sys.modules.pop("model", None)
         import model as ref_model  # the reference's file
     finally:
         sys.path.remove(ref_dir)
+        for k in [k for k in sys.modules if k in ("model", "kernels") or k.startswith("kernels.")]:
+            sys.modules.pop(k)
+        sys.modules.update(ours)
     ref_model.fp8_linear = O.fp8_linear
     return ref_model
 
@@ -173,7 +179,7 @@ def steps(ref_model, out_path: str, seed: int = 7, vocab: int = 1024, n_layers: 
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference/qwen3-8b-fp8_rtx-5090")
+    ap.add_argument("--ref", default=refpath.engine_dir())
     args = ap.parse_args()
     torch.set_num_threads(os.cpu_count() or 1)
     ref_model = load_reference(args.ref)

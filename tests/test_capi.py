@@ -93,3 +93,83 @@ def test_tp_entry_points_check_arguments_without_a_gpu(lib):
         assert st == 1 and msg in lib.qk_last_error(), lib.qk_last_error()
     st = lib.qk_decode_step_tp(*args, 0, None, None)
     assert st == 1 and b"null" in lib.qk_last_error()
+
+
+def _ref_tile_fp8(w, kmajor):
+    """The reference's weight layout (qwen3-8b-fp8_rtx-5090/model.py:92-104), restated for the boundary test:
+    8-row groups of 64-wide K chunks, group-major or K-major."""
+    import torch
+    N, K = w.shape
+    v = w.view(torch.uint8).view(N // 8, 8, K // 64, 4, 4, 4)
+    order = (2, 0, 1, 4, 3, 5) if kmajor else (0, 2, 1, 4, 3, 5)
+    return v.permute(*order).contiguous().view(torch.float8_e4m3fn).view(N, K)
+
+
+def test_boundary_rejects_weights_not_in_pack_fp8_layout(lib):
+    """A reference caller handing its tile_fp8 weights (or any untagged fp8 tensor) to fp8_gemv gets the
+    reference's RuntimeError instead of wrong numbers; pack_reference_tiled converts them."""
+    import torch
+    import kernels
+    import model as M
+    ops = kernels.DecodeOps(lib)    # no GPU needed: the layout check comes before any launch
+    w = (torch.randn(256, 4096) * 4).to(torch.float8_e4m3fn)
+    s = torch.ones(256)
+    x = torch.zeros(4096, dtype=torch.bfloat16)
+    out = torch.zeros(256, dtype=torch.bfloat16)
+    for bad in (_ref_tile_fp8(w, True), w, M.pack_fp8(w).as_subclass(torch.Tensor)):
+        with pytest.raises(RuntimeError, match="pack_fp8"):
+            ops.fp8_gemv(0, bad, s, x, x, out, 256, 1e-6, 4, 4, 2, 24, 1)
+    # gate|up needs the pairs packing, every other kind the plain one
+    with pytest.raises(RuntimeError, match="pairs=True"):
+        ops.fp8_gemv(2, M.pack_fp8(w), s, x, x, out, 256, 1e-6)
+    with pytest.raises(RuntimeError, match="PackedFP8Pairs"):
+        ops.fp8_gemv(0, M.pack_fp8(w, pairs=True), s, x, x, out, 256, 1e-6)
+    with pytest.raises(RuntimeError, match="pack_fp8"):
+        ops.lm_head_argmax(w, x, x, out, torch.zeros(1, dtype=torch.int64), 1e-6, 0, w_scale=s)
+    with pytest.raises(RuntimeError, match="bf16"):
+        ops.lm_head_argmax(M.pack_fp8(w), x, x, out, torch.zeros(1, dtype=torch.int64), 1e-6, 0)
+    # the converter gives exactly pack_fp8 of the row-major matrix, for both reference orders
+    for km in (False, True):
+        got = M.pack_reference_tiled(_ref_tile_fp8(w, km), km)
+        assert isinstance(got, kernels.PackedFP8)
+        assert torch.equal(got.view(torch.uint8), M.pack_fp8(w).view(torch.uint8))
+    # the tag survives moves and views
+    assert isinstance(M.pack_fp8(w).to("cpu").view(-1), kernels.PackedFP8)
+
+
+def test_boundary_validates_the_reference_tuning_knobs(lib):
+    import torch
+    import kernels
+    import model as M
+    ops = kernels.DecodeOps(lib)
+    w = M.pack_fp8(torch.zeros(256, 4096).to(torch.float8_e4m3fn))
+    s = torch.ones(256)
+    x = torch.zeros(4096, dtype=torch.bfloat16)
+    out = torch.zeros(256, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="kmajor"):
+        ops.fp8_gemv(0, w, s, x, x, out, 256, 1e-6, 4, 4, 2, 24, 2)
+    with pytest.raises(RuntimeError, match="trig"):
+        ops.fp8_gemv(0, w, s, x, x, out, 256, 1e-6, 4, 4, 2, 32, 1)
+    with pytest.raises(RuntimeError, match="trig"):
+        ops.fp8_gemv(0, w, s, x, x, out, 256, 1e-6, 4, 4, 2, -2, 1)
+
+
+def test_noalloc_rejects_bad_arguments_before_enqueuing_anything(lib):
+    """Every check of qk_fp8_gemv runs before the no-alloc entry point touches the device: these calls need
+    no GPU, so nothing (not even its counter reset) was enqueued."""
+    p = ctypes.c_void_p(16)
+    # null weights
+    st = lib.qk_fp8_gemv_noalloc(0, None, p, 1, p, p, None, None, p, 6144, 4096, 1e-6, None)
+    assert st == 1 and b"null" in lib.qk_last_error()
+    # gate|up with N not a multiple of 32
+    st = lib.qk_fp8_gemv_noalloc(2, p, p, 1, p, p, None, None, p, 4112, 4096, 1e-6, None)
+    assert st == 1 and b"multiple of 32" in lib.qk_last_error()
+    # block-128 scales with N % 128 != 0
+    st = lib.qk_fp8_gemv_noalloc(0, p, p, 0, p, p, None, None, p, 6160, 4096, 1e-6, None)
+    assert st == 1 and b"block-128" in lib.qk_last_error()
+    # misaligned output
+    st = lib.qk_fp8_gemv_noalloc(1, p, p, 1, p, None, None, None, ctypes.c_void_p(18), 4096, 4096, 1e-6, None)
+    assert st == 1 and b"aligned" in lib.qk_last_error()
+    # the unknown kind is refused too
+    st = lib.qk_fp8_gemv_noalloc(4, p, p, 1, p, p, None, None, p, 4096, 4096, 1e-6, None)
+    assert st == 1 and b"kind" in lib.qk_last_error()
