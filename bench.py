@@ -391,7 +391,7 @@ def run_ours(args):
                      f"lm_head, partials exchanged in-kernel over NVLink")
             traffic = None
         elif ws > 1:
-            kname = (f"one TP rank's step ({3 + 5 * len(m.layers)} kernels on 1/{ws} of the weights, KV and "
+            kname = (f"one TP rank's step ({6 + 6 * len(m.layers)} kernels on 1/{ws} of the weights, KV and "
                      f"lm_head, {2 * len(m.layers) + 1} NCCL all-reduces)")
             traffic = None
         elif fused:
@@ -414,7 +414,9 @@ def run_ours(args):
                        "path": ("fused-tp" if fused else "ops+nccl") if ws > 1 else args.path,
                        "l2": "inputs larger than L2 (8.2 GB read per step), no flush"},
             "e2e": {"value": K / t_e2e, "unit": UNIT, "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
-            "gpu_launches": K * (1 if fused else (3 + 5 * len(m.layers) + (3 if ws > 1 else 0))),
+            # ops path: embed, per layer qkv + attention (partials, merge) + o + gate_up + down, lm_head, finalize
+            # (TP also residual_add and two argmax-key flips); NCCL kernels are not counted
+            "gpu_launches": K * (1 if fused else (3 + 6 * len(m.layers) + (3 if ws > 1 else 0))),
             "roofline": {"bound": "hbm", "kernel": kname, "achieved": achieved, "peak": peak,
                          "peak_source": f"{peak_src} hbm_gbs (burst copy)", "unit": "GB/s", "frac": achieved / peak,
                          "traffic": traffic, "bytes_per_launch_algorithmic": k_bytes, "launch_us": k_s * 1e6,
@@ -516,7 +518,7 @@ def timeline_summary(tl, n_layers: int, clock_ghz: float = 1.965) -> dict:
     start = lambda ph: t[:, ph, 0] if ph < P else None   # noqa: E731
     names = {0: "qkv", 2: "o_proj", 3: "gate_up", 4: "down"}
     per = {k: [] for k in ("qkv", "attn", "merge", "o_proj", "gate_up", "down")}
-    layer_us = []
+    layer_us, bar_stats = [], []
     for l in (range(1, n_layers) if n_layers > 1 else range(n_layers)):
         b = 5 * l
         for j, name in names.items():
@@ -531,7 +533,20 @@ def timeline_summary(tl, n_layers: int, clock_ghz: float = 1.965) -> dict:
         per["merge"].append(dict(work=us(a[:64, 2] - a[:64, 1]), barrier=us(t[:, b + 2, 0] - a[:, 2]),
                                  ring_wait_attn_and_merge=cyc(cw[:, b + 1])))
         layer_us.append(np.median(us(start(b + 5) - t[:, b, 0])))
+        # each grid barrier of the layer: spread of the CTAs' arrivals, and the release latency (first CTA to
+        # leave the barrier after the last one arrived)
+        for end_ph, end_w, nxt in ((b, 2, b + 1), (b + 1, 7, None), (b + 1, 2, b + 2), (b + 2, 2, b + 3),
+                                   (b + 3, 2, b + 4), (b + 4, 2, b + 5)):
+            arrive = t[:, end_ph, end_w] if end_w != 2 or end_ph != b + 1 else t[:64, end_ph, 2]
+            leave = t[:, b + 1, 1] if nxt is None else start(nxt)
+            bar_stats.append((us(arrive.max() - np.median(arrive)), us(leave.min() - arrive.max()),
+                              us(leave.max() - leave.min())))
     out = {"ctas": G, "layers": n_layers, "layer_us": float(np.median(layer_us))}
+    names_b = ["qkv->attn", "attn->merge", "merge->o", "o->gu", "gu->down", "down->qkv"]
+    bs = np.array(bar_stats).reshape(-1, 6, 3)
+    out["barriers"] = {n: {"last_arrival_after_median_us": round(float(np.median(bs[:, i, 0])), 3),
+                           "release_after_last_arrival_us": round(float(np.median(bs[:, i, 1])), 3),
+                           "leave_spread_us": round(float(np.median(bs[:, i, 2])), 3)} for i, n in enumerate(names_b)}
     for k, v in per.items():
         out[k] = {f: round(float(np.median([np.median(d[f]) for d in v])), 3) for f in v[0]}
     h = t[:, 5 * n_layers]

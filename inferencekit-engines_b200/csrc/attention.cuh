@@ -1,26 +1,38 @@
-// Decode attention for one token per sequence: q/k RMSNorm + RoPE, KV-cache append, GQA split-KV
-// ("flash-decoding") attention, in-kernel merge of the splits.
+// Decode attention for one new token per sequence: q/k RMSNorm + RoPE, KV-cache append, GQA split-KV
+// attention over a bf16 cache, split merge. Two kernels per call (the second launched with programmatic
+// dependent launch):
 //
-// Grid (kv_head, split, sequence), 128 threads. A CTA owns CHUNK keys of one KV head and its 4 query heads.
-//  * Before griddepcontrol.wait (the qkv GEMV may still be running) the CTA loads its cached keys into
-//    registers (16-byte loads, one key per CHUNK threads' slice) and issues one bulk async copy of its
-//    cached values into shared memory. Those rows were written by earlier steps.
-//  * After the wait: 4 warps RMS-normalise + rotate the 4 query heads; the CTA whose chunk holds the new
-//    position normalises + rotates the new key and writes K and V into the cache slot `pos` (exactly one
-//    slot per KV head per token), and patches its shared copies.
-//  * fp32 scores, softmax over the chunk (probabilities stay fp32), P @ V, and the unnormalised partial
-//    (m, l, o) per query head to `o_part` / `ml_part`. The last CTA of a KV head (atomic counter) merges
-//    the splits and resets the counter.
-// The arithmetic is in the same order as the reference decode kernel (decode.cu:343-360, :462-567) for
-// the same CHUNK, so cache rows and outputs are bit-identical to it; the number of splits is not bounded
-// by a compile-time constant (long contexts), only by `max_splits` of the scratch the caller passes.
+//  attn_partials_kernel<CHUNK>   grid (n_kv * key blocks, batch), 128 threads. A CTA owns one block of 128
+//    consecutive keys of one (sequence, KV head): 128/CHUNK reference splits. Its K and V rows arrive by four
+//    TMA box loads ({64 dims, 128 keys}, 128-byte swizzle, issued before griddepcontrol.wait: they are earlier
+//    tokens' rows) so that 8 keys read at the same dims hit 8 different bank groups. After the wait the four
+//    query heads of the KV head are normalised and rotated (one warp each); the CTA whose block holds `pos`
+//    also writes the new K (normalised + rotated) and V rows to the cache and into its shared copy. Then
+//    thread = key computes the 4 heads' scores, one warp per (split, head) row takes the softmax (fp32
+//    probabilities), thread = dim computes P @ V for every split and head, and each split's unnormalised
+//    partial (m, l, o[128]) goes to o_part / ml_part.
+//  attn_merge_kernel             grid (2 * n_q, batch), 128 threads: CTA (query head, 64-dim half) combines
+//    that head's split partials: M = max m_s, w_s = exp(m_s - M), out = bf16(sum_s w_s o_s / sum_s w_s l_s).
+//
+// Numerics: for CHUNK in {32, 64, 128} every sum runs in the order of the reference decode kernel
+// (Q/kernels/decode.cu:343-360 head norm + RoPE, :462-527 scores / softmax / P@V per CHUNK-key split,
+// :537-567 merge): a score is the in-order dot over each CHUNK-wide slice of the head dims, slices added left
+// to right; probabilities and sums stay fp32; the merge sums over splits in split order. Cache rows and outputs
+// are therefore bit-identical to the reference kernel's for the same CHUNK. The number of splits is bounded
+// only by the caller's o_part (max_splits), not by a compile-time constant.
 #pragma once
+#include <cuda.h>   // CUtensorMap
 #include "common.cuh"
 
 namespace qk {
 
+constexpr int ATT_KEYS = 128;          // keys per partials CTA (the rows of one TMA box)
+constexpr int ATT_THREADS = 128;
+constexpr int ATT_MERGE_ROUND = 128;   // splits staged per round of the merge
+
 struct AttnParams {
-  const bf16* qkv;           // [B][qkv_stride]: q heads | k heads | v heads of this rank, 128 each
+  CUtensorMap tm_k, tm_v;    // K / V cache of the layer: bf16 {128 dims, max_seq, n_kv, batch}, box {64, 128}
+  const bf16* qkv;           // [B][qkv_stride]: q heads | k heads | v heads, 128 each
   const bf16* q_norm_w;      // [128]
   const bf16* k_norm_w;      // [128]
   const bf16* cos_tab;       // [max_seq, 128]
@@ -30,22 +42,24 @@ struct AttnParams {
   bf16* v_cache;
   float* o_part;             // [B][n_q][max_splits][128]
   float* ml_part;            // [B][n_q][max_splits][2]
-  int* counters;             // [B][n_kv], zero between launches
   bf16* out;                 // [B][n_q * 128]
-  int max_seq, max_splits, qkv_stride, state_stride;
+  int n_kv, max_seq, max_splits, qkv_stride, state_stride, chunk;
   float scale, eps;
-  int tl_slot;               // timeline region of this launch, -1 when off
+  int tl_slot;               // timeline region of this call, -1 when off (words 0-2 partials, 3-4 merge)
 };
 
-// Per-head RMSNorm (eps) + RoPE (rotate_half pairs d and d+64 = lane l and l^16), one warp, 4 dims per
-// lane, each step rounded to bf16 as in the reference forward (model.py:121-125, :265-266).
-__device__ __forceinline__ void head_norm_rope(const bf16* __restrict__ src, const bf16* __restrict__ nw,
-                                               const bf16* __restrict__ cos_row, const bf16* __restrict__ sin_row,
+// Byte offset of (key r, dim d) in a swizzled K or V block: dims 0-63 in the first 16 KiB box, 64-127 in the
+// second; 16-byte chunk c of a 128-byte row r sits at chunk c ^ (r % 8).
+__device__ __forceinline__ uint32_t att_off(int r, int d) {
+  return (uint32_t)((d >> 6) * (ATT_KEYS * 128) + r * 128 + ((((d & 63) >> 3) ^ (r & 7)) << 4) + (d & 7) * 2);
+}
+
+// Per-head RMSNorm (eps) + RoPE of one head held as 4 values per lane (dims 4*lane .. 4*lane+3): the sum of
+// squares over the warp, each step rounded to bf16 as the reference forward does (Q/model.py:121-130, :265-266),
+// the rotation partner of dim d being d +- 64 (lane ^ 16). Shared with the fused step.
+__device__ __forceinline__ void head_norm_rope(float (&v)[4], const bf16* nw, const bf16* cos_row, const bf16* sin_row,
                                                int lane, float eps, float (&o)[4]) {
   const int d0 = lane * 4;
-  float v[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) v[j] = __bfloat162float(src[d0 + j]);
   const float ss = warp_sum(v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3]);
   const float rstd = rsqrtf(ss / (float)HEAD_DIM + eps);
 #pragma unroll
@@ -57,217 +71,240 @@ __device__ __forceinline__ void head_norm_rope(const bf16* __restrict__ src, con
     o[j] = bf16r(v[j] * __bfloat162float(cos_row[d0 + j])) + bf16r(rot * __bfloat162float(sin_row[d0 + j]));
   }
 }
+// The same from 4 bf16 values at `src` (global memory written by an earlier kernel or phase, read through L2).
+__device__ __forceinline__ void head_norm_rope_from(const bf16* src, const bf16* nw, const bf16* cos_row,
+                                                    const bf16* sin_row, int lane, float eps, float (&o)[4]) {
+  uint2 raw;
+  asm volatile("ld.global.cg.v2.u32 {%0,%1}, [%2];" : "=r"(raw.x), "=r"(raw.y) : "l"(src + lane * 4));
+  float v[4] = {bf16lo(raw.x), bf16hi(raw.x), bf16lo(raw.y), bf16hi(raw.y)};
+  head_norm_rope(v, nw, cos_row, sin_row, lane, eps, o);
+}
 
-template <int CHUNK>
 struct AttnSmem {
-  static constexpr int TPK = HEAD_DIM / CHUNK;
-  float qs[GQA][HEAD_DIM];
-  float sc[GQA][CHUNK];
-  float part[TPK > 1 ? TPK - 1 : 1][GQA][CHUNK];
-  __align__(16) bf16 vs[CHUNK][HEAD_DIM];
-  __align__(16) bf16 knew[HEAD_DIM];
-  float m_s[GQA], l_s[GQA], cl[GQA];
-  uint64_t vbar;
-  int is_last;
-  // followed by cw[GQA][max_splits] floats (dynamic)
+  uint8_t k[2 * ATT_KEYS * 128];         // swizzled K block (two 16 KiB boxes)
+  uint8_t v[2 * ATT_KEYS * 128];         // swizzled V block
+  float q[GQA][HEAD_DIM];                // the 4 query heads after norm + RoPE (bf16 values)
+  float p[GQA][ATT_KEYS];                // scores, then probabilities, per head and key of the block
+  float m[ATT_KEYS / 32][GQA], l[ATT_KEYS / 32][GQA];   // per (split of the block, head)
+  uint64_t bar;
 };
 
 template <int CHUNK>
-__global__ void __launch_bounds__(128) attention_kernel(const __grid_constant__ AttnParams p) {
-  constexpr int TPK = HEAD_DIM / CHUNK;    // threads per key
-  constexpr int DPT = HEAD_DIM / TPK;      // dims per thread in the score dot
-  constexpr int PER_LANE = CHUNK / 32;     // softmax values per lane
-  extern __shared__ __align__(128) uint8_t smem_raw[];
-  AttnSmem<CHUNK>& sm = *reinterpret_cast<AttnSmem<CHUNK>*>(smem_raw);
-  float* cw = reinterpret_cast<float*>(smem_raw + ((sizeof(AttnSmem<CHUNK>) + 15) / 16) * 16);
-
-  const int kvh = blockIdx.x, split = blockIdx.y, b = blockIdx.z;
-  const int n_kv = gridDim.x, n_q = n_kv * GQA;
+__global__ void __launch_bounds__(ATT_THREADS) attn_partials_kernel(const __grid_constant__ AttnParams p) {
+  constexpr int NSPLIT = ATT_KEYS / CHUNK;         // reference splits per block
+  constexpr int PER_LANE = CHUNK / 32;             // softmax values per lane
+  extern __shared__ __align__(1024) uint8_t att_smem[];
+  AttnSmem& sm = *reinterpret_cast<AttnSmem*>(att_smem);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int pos = p.state[b * p.state_stride];   // written by the previous step's last kernel
+  const int n_blocks = (p.max_seq + ATT_KEYS - 1) / ATT_KEYS;
+  const int kvh = blockIdx.x / n_blocks, blk = blockIdx.x - kvh * n_blocks, b = blockIdx.y;
+  const int n_q = p.n_kv * GQA;
+  const int pos = p.state[(size_t)b * p.state_stride];   // written by the previous step's finalize
   if (pos < 0 || pos >= p.max_seq) {
-    if (tid == 0 && split == 0) atomicOr(&g_dev_error, DEVERR_BAD_STATE);
+    if (tid == 0 && blk == 0 && kvh == 0) atomicOr(&g_dev_error, DEVERR_BAD_STATE);
     return;
   }
-  const int ctx = pos + 1;
-  const int n_splits = (ctx + CHUNK - 1) / CHUNK;
-  if (split >= n_splits) return;
-  const int j0 = split * CHUNK;
-  const int nj = min(CHUNK, ctx - j0);
-  const bool owns_new = (split == n_splits - 1);
-  const int jn = pos - j0;
-
-  const size_t head_base = ((size_t)b * n_kv + kvh) * p.max_seq;
-  const bf16* kb = p.k_cache + (head_base + j0) * HEAD_DIM;
-  const bf16* vb = p.v_cache + (head_base + j0) * HEAD_DIM;
-  const int key = tid % CHUNK, slice = tid / CHUNK;
-  const bool is_new = owns_new && key == jn;
-
-  // ---- 1. cached K -> registers, cached V -> shared memory (bulk copy), before the wait ----
-  uint4 kr[DPT / 8];
-  if (key < nj && !is_new) {
-#pragma unroll
-    for (int i = 0; i < DPT / 8; ++i) kr[i] = ldg_stream(kb + key * HEAD_DIM + slice * DPT + i * 8);
-  }
+  const int ctx = pos + 1, key0 = blk * ATT_KEYS;
+  if (key0 >= ctx) return;    // a block past the context (the grid covers max_seq): nothing to do
   if (tid == 0) {
     tl_stamp(p.tl_slot, 0);
-    mbar_init(&sm.vbar, 1);
+    mbar_init(&sm.bar, 1);
     fence_mbar_init();
-    mbar_arrive_expect_tx(&sm.vbar, (uint32_t)(nj * HEAD_DIM * 2));
-    bulk_g2s(&sm.vs[0][0], vb, (uint32_t)(nj * HEAD_DIM * 2), &sm.vbar);
+    mbar_arrive_expect_tx(&sm.bar, 4 * ATT_KEYS * 128);
+    tma_load_4d(sm.k, &p.tm_k, 0, key0, kvh, b, &sm.bar);
+    tma_load_4d(sm.k + ATT_KEYS * 128, &p.tm_k, 64, key0, kvh, b, &sm.bar);
+    tma_load_4d(sm.v, &p.tm_v, 0, key0, kvh, b, &sm.bar);
+    tma_load_4d(sm.v + ATT_KEYS * 128, &p.tm_v, 64, key0, kvh, b, &sm.bar);
   }
-  grid_dep_wait();
-  grid_dep_launch();
+  grid_dep_wait();            // qkv comes from the kernel before
   if (tid == 0) tl_stamp(p.tl_slot, 1);
-  __syncthreads();                          // barrier init visible to all threads
-  const bool v_ok = mbar_wait(&sm.vbar, 0); // the copy must land before the new row is patched in
-
-  // ---- 2. q (and the new k, v): norm + RoPE; KV append ----
   const bf16* qkv = p.qkv + (size_t)b * p.qkv_stride;
   const bf16* cos_row = p.cos_tab + (size_t)pos * HEAD_DIM;
   const bf16* sin_row = p.sin_tab + (size_t)pos * HEAD_DIM;
-  {
+  {   // warp h: query head 4*kvh + h
     float o[4];
-    head_norm_rope(qkv + (kvh * GQA + warp) * HEAD_DIM, p.q_norm_w, cos_row, sin_row, lane, p.eps, o);
+    head_norm_rope_from(qkv + (size_t)(kvh * GQA + warp) * HEAD_DIM, p.q_norm_w, cos_row, sin_row, lane, p.eps, o);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) sm.qs[warp][lane * 4 + j] = bf16r(o[j]);
+    for (int j = 0; j < 4; ++j) sm.q[warp][lane * 4 + j] = bf16r(o[j]);
   }
-  if (owns_new && warp == 0) {
-    float o[4];
-    head_norm_rope(qkv + (n_q + kvh) * HEAD_DIM, p.k_norm_w, cos_row, sin_row, lane, p.eps, o);
-    bf16* dst = p.k_cache + (head_base + pos) * HEAD_DIM + lane * 4;
+  __syncthreads();            // also publishes the barrier's initialisation
+  const bool ok = mbar_wait(&sm.bar, 0);
+  const bool owns_new = pos - key0 < ATT_KEYS;
+  if (owns_new && warp < 2) { // the new token's K (warp 0) and V (warp 1) rows: cache slot `pos` and the copy here
+    const int r = pos - key0;
+    const size_t row = (((size_t)b * p.n_kv + kvh) * p.max_seq + pos) * HEAD_DIM + lane * 4;
+    if (warp == 0) {
+      float o[4];
+      head_norm_rope_from(qkv + (size_t)(n_q + kvh) * HEAD_DIM, p.k_norm_w, cos_row, sin_row, lane, p.eps, o);
+      bf16* dst = p.k_cache + row;
+      bf16* sdst = reinterpret_cast<bf16*>(sm.k + att_off(r, lane * 4));
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      dst[j] = __float2bfloat16_rn(o[j]);
-      sm.knew[lane * 4 + j] = __float2bfloat16_rn(o[j]);
-    }
-  } else if (owns_new && warp == 1) {
-    const bf16* src = qkv + (n_q + n_kv + kvh) * HEAD_DIM + lane * 4;
-    bf16* dst = p.v_cache + (head_base + pos) * HEAD_DIM + lane * 4;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      dst[j] = src[j];
-      sm.vs[jn][lane * 4 + j] = src[j];
+      for (int j = 0; j < 4; ++j) dst[j] = sdst[j] = __float2bfloat16_rn(o[j]);
+    } else {
+      uint2 raw;
+      const bf16* src = qkv + (size_t)(n_q + p.n_kv + kvh) * HEAD_DIM + lane * 4;
+      asm volatile("ld.global.cg.v2.u32 {%0,%1}, [%2];" : "=r"(raw.x), "=r"(raw.y) : "l"(src));
+      *reinterpret_cast<uint2*>(p.v_cache + row) = raw;
+      *reinterpret_cast<uint2*>(sm.v + att_off(r, lane * 4)) = raw;
     }
   }
   __syncthreads();
 
-  // ---- 3. scores: thread (key, slice) sums DPT dims in order for all 4 heads ----
-  float dot[GQA] = {0.f, 0.f, 0.f, 0.f};
-  if (key < nj) {
-    if (is_new) {
+  // scores: thread = key j of the block, all 4 heads; per head the CHUNK-dim slices summed in order, then added
+  {
+    const int j = tid, sp = j / CHUNK, split = key0 / CHUNK + sp;
+    const bool valid = j - sp * CHUNK < min(CHUNK, ctx - split * CHUNK);
+    float total[GQA];
 #pragma unroll
-      for (int i = 0; i < DPT / 8; ++i) kr[i] = *reinterpret_cast<const uint4*>(sm.knew + slice * DPT + i * 8);
+    for (int sl = 0; sl < HEAD_DIM / CHUNK; ++sl) {
+      float d[GQA] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+      for (int i = 0; i < CHUNK / 8; ++i) {
+        const int d0 = sl * CHUNK + i * 8;
+        const uint4 kv = lds128(sm.k + att_off(j, d0));
+        const float kf[8] = {bf16lo(kv.x), bf16hi(kv.x), bf16lo(kv.y), bf16hi(kv.y),
+                             bf16lo(kv.z), bf16hi(kv.z), bf16lo(kv.w), bf16hi(kv.w)};
+#pragma unroll
+        for (int h = 0; h < GQA; ++h) {
+          const float4 qa = *reinterpret_cast<const float4*>(&sm.q[h][d0]);
+          const float4 qb = *reinterpret_cast<const float4*>(&sm.q[h][d0 + 4]);
+          d[h] += qa.x * kf[0];
+          d[h] += qa.y * kf[1];
+          d[h] += qa.z * kf[2];
+          d[h] += qa.w * kf[3];
+          d[h] += qb.x * kf[4];
+          d[h] += qb.y * kf[5];
+          d[h] += qb.z * kf[6];
+          d[h] += qb.w * kf[7];
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < GQA; ++h) total[h] = sl == 0 ? d[h] : total[h] + d[h];
     }
 #pragma unroll
-    for (int i = 0; i < DPT / 8; ++i) {
-      const bf16* e = reinterpret_cast<const bf16*>(&kr[i]);
+    for (int h = 0; h < GQA; ++h) sm.p[h][j] = valid ? total[h] * p.scale : -INFINITY;
+  }
+  __syncthreads();
+  // softmax: one warp per (split, head) row of CHUNK scores
+  const int n_splits = (ctx + CHUNK - 1) / CHUNK;
+  for (int r = warp; r < NSPLIT * GQA; r += ATT_THREADS / 32) {
+    const int sp = r / GQA, h = r - sp * GQA;
+    if (key0 / CHUNK + sp >= n_splits) continue;
+    float* row = &sm.p[h][sp * CHUNK];
+    float pr[PER_LANE];
+    float mx = -INFINITY;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float kf = __bfloat162float(e[j]);
+    for (int i = 0; i < PER_LANE; ++i) {
+      pr[i] = row[lane + 32 * i];
+      mx = fmaxf(mx, pr[i]);
+    }
+    mx = warp_max(mx);
+    float ls = 0.f;
 #pragma unroll
-        for (int h = 0; h < GQA; ++h) dot[h] += sm.qs[h][slice * DPT + i * 8 + j] * kf;
+    for (int i = 0; i < PER_LANE; ++i) {
+      pr[i] = expf(pr[i] - mx);
+      ls += pr[i];
+      row[lane + 32 * i] = pr[i];
+    }
+    ls = warp_sum(ls);
+    if (lane == 0) {
+      sm.m[sp][h] = mx;
+      sm.l[sp][h] = ls;
+    }
+  }
+  __syncthreads();
+  // P @ V: thread = output dim d, every split of the block and every head; keys in order
+  {
+    const int d = tid;
+#pragma unroll
+    for (int sp = 0; sp < NSPLIT; ++sp) {
+      const int split = key0 / CHUNK + sp;
+      if (split >= n_splits) break;
+      const int nj = min(CHUNK, ctx - split * CHUNK);
+      float acc[GQA] = {0.f, 0.f, 0.f, 0.f};
+      for (int j = 0; j < nj; ++j) {
+        const int r = sp * CHUNK + j;
+        const float vf = __bfloat162float(*reinterpret_cast<const bf16*>(sm.v + att_off(r, d)));
+#pragma unroll
+        for (int h = 0; h < GQA; ++h) acc[h] += sm.p[h][r] * vf;
+      }
+#pragma unroll
+      for (int h = 0; h < GQA; ++h) {
+        const size_t row = ((size_t)b * n_q + kvh * GQA + h) * p.max_splits + split;
+        p.o_part[row * HEAD_DIM + d] = acc[h];
+        if (d == 0) {
+          p.ml_part[row * 2 + 0] = sm.m[sp][h];
+          p.ml_part[row * 2 + 1] = sm.l[sp][h];
+        }
       }
     }
   }
-  if (TPK > 1 && slice > 0) {
-#pragma unroll
-    for (int h = 0; h < GQA; ++h) sm.part[slice - 1][h][key] = dot[h];
-  }
-  if (TPK > 1) __syncthreads();
-  if (slice == 0) {
-#pragma unroll
-    for (int h = 0; h < GQA; ++h) {
-      float s = dot[h];
-#pragma unroll
-      for (int q = 0; q + 1 < TPK; ++q) s += sm.part[q][h][key];
-      sm.sc[h][key] = (key < nj) ? s * p.scale : -INFINITY;
-    }
-  }
-  __syncthreads();
+  if (!ok && tid == 0) atomicOr(&g_dev_error, DEVERR_MBAR_TIMEOUT);
+  if (tid == 0) tl_stamp(p.tl_slot, 2);
+  grid_dep_launch();          // the merge kernel may start; it waits for this grid's completion and writes
+}
 
-  {  // softmax over the chunk, one warp per query head
-    float pr[PER_LANE];
-    float m = -INFINITY;
-#pragma unroll
-    for (int i = 0; i < PER_LANE; ++i) { pr[i] = sm.sc[warp][lane + 32 * i]; m = fmaxf(m, pr[i]); }
-    m = warp_max(m);
-    float l = 0.f;
-#pragma unroll
-    for (int i = 0; i < PER_LANE; ++i) { pr[i] = expf(pr[i] - m); l += pr[i]; sm.sc[warp][lane + 32 * i] = pr[i]; }
-    l = warp_sum(l);
-    if (lane == 0) { sm.m_s[warp] = m; sm.l_s[warp] = l; }
-  }
-  __syncthreads();
+// Merge of one query head's split partials, dims [64 * half, 64 * half + 64): warp 0 takes the max of the
+// split maxima and the weights w_s = exp(m_s - M) and their l-weighted sum (lane-strided over the splits, then a
+// butterfly, as the reference); all warps stage the partial rows in shared memory (cp.async, rounds of
+// ATT_MERGE_ROUND splits) and threads 0-63 sum w_s * o_s[d] over the splits in order.
+struct MergeSmem {
+  float o[ATT_MERGE_ROUND * 64];
+  float cl;
+  // followed by w[max_splits] (dynamic)
+};
 
-  // ---- P @ V: thread d owns output dim d for the 4 heads ----
-  const int d = tid;
-  float acc[GQA] = {0.f, 0.f, 0.f, 0.f};
-  for (int j = 0; j < nj; ++j) {
-    const float vf = __bfloat162float(sm.vs[j][d]);
-#pragma unroll
-    for (int h = 0; h < GQA; ++h) acc[h] += sm.sc[h][j] * vf;
-  }
-  const size_t qbase = (size_t)b * n_q;
-#pragma unroll
-  for (int h = 0; h < GQA; ++h) {
-    const size_t row = (qbase + kvh * GQA + h) * p.max_splits + split;
-    p.o_part[row * HEAD_DIM + d] = acc[h];
-    if (tid == 0) {
-      p.ml_part[row * 2 + 0] = sm.m_s[h];
-      p.ml_part[row * 2 + 1] = sm.l_s[h];
-    }
-  }
-  if (!v_ok) atomicOr(&g_dev_error, DEVERR_MBAR_TIMEOUT);
-
-  // ---- 4. the last CTA of this KV head merges all splits ----
-  __threadfence();
-  __syncthreads();
-  int* counter = p.counters + (size_t)b * n_kv + kvh;
-  if (tid == 0) {
-    tl_stamp(p.tl_slot, 2);
-    sm.is_last = (atomicAdd(counter, 1) == n_splits - 1);
-  }
-  __syncthreads();
-  if (!sm.is_last) return;
-  __threadfence();
-  {
-    const int qh = kvh * GQA + warp;
-    const float* ml = p.ml_part + (qbase + qh) * p.max_splits * 2;
+__global__ void __launch_bounds__(ATT_THREADS) attn_merge_kernel(const __grid_constant__ AttnParams p) {
+  extern __shared__ __align__(16) uint8_t mg_smem[];
+  MergeSmem& sm = *reinterpret_cast<MergeSmem*>(mg_smem);
+  float* w = reinterpret_cast<float*>(mg_smem + sizeof(MergeSmem));
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int qh = blockIdx.x >> 1, half = blockIdx.x & 1, b = blockIdx.y;
+  const int n_q = p.n_kv * GQA;
+  const int pos = p.state[(size_t)b * p.state_stride];
+  grid_dep_wait();            // every partial of this call is written
+  grid_dep_launch();
+  if (pos < 0 || pos >= p.max_seq) return;   // reported by the partials kernel
+  if (tid == 0 && qh == 0 && half == 0) tl_stamp(p.tl_slot, 3);
+  const int n_splits = (pos + p.chunk) / p.chunk;
+  const size_t hrow = ((size_t)b * n_q + qh) * p.max_splits;
+  if (warp == 0) {
+    const float* ml = p.ml_part + hrow * 2;
     float mloc = -INFINITY;
     for (int s = lane; s < n_splits; s += 32) mloc = fmaxf(mloc, __ldcg(ml + 2 * s));
     const float M = warp_max(mloc);
     float lsum = 0.f;
     for (int s = lane; s < n_splits; s += 32) {
-      const float wgt = expf(__ldcg(ml + 2 * s) - M);
-      cw[warp * p.max_splits + s] = wgt;
-      lsum += wgt * __ldcg(ml + 2 * s + 1);
+      const float wt = expf(__ldcg(ml + 2 * s) - M);
+      w[s] = wt;
+      lsum += wt * __ldcg(ml + 2 * s + 1);
     }
     lsum = warp_sum(lsum);
-    if (lane == 0) sm.cl[warp] = lsum;
+    if (lane == 0) sm.cl = lsum;
   }
-  __syncthreads();
-  float o[GQA] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 8
-  for (int s = 0; s < n_splits; ++s) {
-#pragma unroll
-    for (int h = 0; h < GQA; ++h)
-      o[h] += cw[h * p.max_splits + s] *
-              __ldcg(p.o_part + ((qbase + kvh * GQA + h) * p.max_splits + s) * HEAD_DIM + d);
+  const float* op = p.o_part + hrow * HEAD_DIM + half * 64;
+  float acc = 0.f;
+  for (int s0 = 0; s0 < n_splits; s0 += ATT_MERGE_ROUND) {
+    const int ns = min(ATT_MERGE_ROUND, n_splits - s0);
+    for (int i = tid; i < ns * 16; i += ATT_THREADS) {   // 16 x 16 bytes per split row of 64 dims
+      const int s = i >> 4, f = i & 15;
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(&sm.o[s * 64 + f * 4])),
+                   "l"(op + (size_t)(s0 + s) * HEAD_DIM + f * 4)
+                   : "memory");
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncthreads();
+    if (tid < 64) {
+      for (int s = 0; s < ns; ++s) acc += w[s0 + s] * sm.o[s * 64 + tid];
+    }
+    __syncthreads();
   }
-#pragma unroll
-  for (int h = 0; h < GQA; ++h)
-    p.out[(qbase + kvh * GQA + h) * HEAD_DIM + d] = __float2bfloat16_rn(o[h] / sm.cl[h]);
-  if (tid == 0) {
-    *counter = 0;
-    tl_stamp(p.tl_slot, 3);
-  }
+  if (tid < 64) p.out[(size_t)b * n_q * HEAD_DIM + qh * HEAD_DIM + half * 64 + tid] = __float2bfloat16_rn(acc / sm.cl);
+  if (tid == 0 && qh == 0 && half == 0) tl_stamp(p.tl_slot, 4);
 }
 
-template <int CHUNK>
-inline size_t attention_smem_bytes(int max_splits) {
-  return ((sizeof(AttnSmem<CHUNK>) + 15) / 16) * 16 + (size_t)GQA * max_splits * 4;
-}
+inline size_t attn_partials_smem_bytes() { return sizeof(AttnSmem); }
+inline size_t attn_merge_smem_bytes(int max_splits) { return sizeof(MergeSmem) + (size_t)max_splits * 4; }
 
 // ---- step bookkeeping ----------------------------------------------------------------------------------------
 // resid[b] = table[token[b]]   (512 threads x 16 bytes = one 4096-wide bf16 row per sequence)

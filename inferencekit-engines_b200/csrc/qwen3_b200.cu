@@ -51,20 +51,25 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
-// TMA map of a whole-model K or V cache: bf16 {128 dims, max_seq keys, n_kv heads, n_layers}, box {64, 64, 1, 1}
-// (8 KiB), 128-byte swizzle, out-of-range rows zero-filled.
-int encode_kv_map(CUtensorMap* map, void* base, int max_seq, int n_kv, int n_layers, long long layer_stride_bytes) {
+// TMA map of a K or V cache: bf16 {128 dims, max_seq keys, n_kv heads, n_outer} (n_outer = layers for the fused
+// step, sequences for the attention op), box {64, box_rows, 1, 1}, 128-byte swizzle, rows past max_seq
+// zero-filled. outer_stride_bytes: distance between consecutive outer indices.
+int encode_cache_map(CUtensorMap* map, void* base, int max_seq, int n_kv, int n_outer, long long outer_stride_bytes,
+                     int box_rows) {
   auto enc = tensor_map_encoder();
   if (!enc) return fail(QK_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
-  const cuuint64_t dims[4] = {HEAD_DIM, (cuuint64_t)max_seq, (cuuint64_t)n_kv, (cuuint64_t)n_layers};
-  const cuuint64_t strides[3] = {HEAD_DIM * 2, (cuuint64_t)max_seq * HEAD_DIM * 2, (cuuint64_t)layer_stride_bytes};
-  const cuuint32_t box[4] = {64, 64, 1, 1};
+  const cuuint64_t dims[4] = {HEAD_DIM, (cuuint64_t)max_seq, (cuuint64_t)n_kv, (cuuint64_t)n_outer};
+  const cuuint64_t strides[3] = {HEAD_DIM * 2, (cuuint64_t)max_seq * HEAD_DIM * 2, (cuuint64_t)outer_stride_bytes};
+  const cuuint32_t box[4] = {64, (cuuint32_t)box_rows, 1, 1};
   const cuuint32_t estr[4] = {1, 1, 1, 1};
   const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, base, dims, strides, box, estr,
                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(QK_EINVAL, "cuTensorMapEncodeTiled failed for the KV cache (CUresult %d)", (int)r);
+  if (r != CUDA_SUCCESS) return fail(QK_EINVAL, "cuTensorMapEncodeTiled failed for a KV cache (CUresult %d)", (int)r);
   return QK_OK;
+}
+int encode_kv_map(CUtensorMap* map, void* base, int max_seq, int n_kv, int n_layers, long long layer_stride_bytes) {
+  return encode_cache_map(map, base, max_seq, n_kv, n_layers, layer_stride_bytes, 64);
 }
 
 int device_sms() {
@@ -293,8 +298,17 @@ int qk_attention(const void* qkv, const void* q_norm_w, const void* k_norm_w, co
   if ((long long)max_splits * chunk < max_seq) return fail(QK_EINVAL, "o_part too small: max_splits*chunk < max_seq");
   if (max_splits > 4096) return fail(QK_EINVAL, "max_splits %d > 4096", max_splits);
   if (qkv_stride < n_kv * 6 * HEAD_DIM || state_stride < 1) return fail(QK_EINVAL, "bad qkv_stride/state_stride");
-  if (!aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(qkv, 16)) return fail(QK_EINVAL, "caches and qkv must be 16-byte aligned");
+  if (!aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(qkv, 16) || !aligned(o_part, 16))
+    return fail(QK_EINVAL, "caches, qkv and o_part must be 16-byte aligned");
+  if ((long long)n_kv * ((max_seq + ATT_KEYS - 1) / ATT_KEYS) > 0x7fffffff) return fail(QK_EINVAL, "max_seq too large");
   AttnParams p = {};
+  // the layer's caches as 4-D tensors {128 dims, max_seq keys, n_kv heads, batch}
+  if (int r = encode_cache_map(&p.tm_k, k_cache, max_seq, n_kv, batch, (long long)n_kv * max_seq * HEAD_DIM * 2,
+                               ATT_KEYS))
+    return r;
+  if (int r = encode_cache_map(&p.tm_v, v_cache, max_seq, n_kv, batch, (long long)n_kv * max_seq * HEAD_DIM * 2,
+                               ATT_KEYS))
+    return r;
   p.qkv = static_cast<const bf16*>(qkv);
   p.q_norm_w = static_cast<const bf16*>(q_norm_w);
   p.k_norm_w = static_cast<const bf16*>(k_norm_w);
@@ -305,25 +319,25 @@ int qk_attention(const void* qkv, const void* q_norm_w, const void* k_norm_w, co
   p.v_cache = static_cast<bf16*>(v_cache);
   p.o_part = o_part;
   p.ml_part = ml_part;
-  p.counters = counters;
   p.out = static_cast<bf16*>(out);
+  p.n_kv = n_kv;
   p.max_seq = max_seq;
   p.max_splits = max_splits;
   p.qkv_stride = qkv_stride;
   p.state_stride = state_stride;
+  p.chunk = chunk;
   p.scale = scale;
   p.eps = eps;
   p.tl_slot = next_tl_slot();
-  const dim3 grid(n_kv, (max_seq + chunk - 1) / chunk, batch);
-  auto run = [&](auto kernel, size_t smem) -> int {
-    if (int r = ensure_smem((const void*)kernel, (int)smem)) return r;
-    return launch(kernel, grid, dim3(128), smem, stream, p);
-  };
-  switch (chunk) {
-    case 32: return run(attention_kernel<32>, attention_smem_bytes<32>(max_splits));
-    case 64: return run(attention_kernel<64>, attention_smem_bytes<64>(max_splits));
-    default: return run(attention_kernel<128>, attention_smem_bytes<128>(max_splits));
-  }
+  (void)counters;   // the reference's last-CTA merge counters: the separate merge kernel needs none
+  const dim3 grid(n_kv * ((max_seq + ATT_KEYS - 1) / ATT_KEYS), batch);
+  auto partials = chunk == 32 ? attn_partials_kernel<32> : chunk == 64 ? attn_partials_kernel<64> : attn_partials_kernel<128>;
+  const int smem_p = (int)attn_partials_smem_bytes();
+  if (int r = ensure_smem((const void*)partials, smem_p)) return r;
+  if (int r = launch(partials, grid, dim3(ATT_THREADS), smem_p, stream, p)) return r;
+  const int smem_m = (int)attn_merge_smem_bytes(max_splits);
+  if (int r = ensure_smem((const void*)attn_merge_kernel, smem_m)) return r;
+  return launch(attn_merge_kernel, dim3(2 * n_kv * GQA, batch), dim3(ATT_THREADS), smem_m, stream, p);
 }
 
 int qk_lm_head_argmax(const void* w, const float* w_scale, int head_fp8, const void* x, const void* norm_w,

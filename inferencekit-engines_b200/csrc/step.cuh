@@ -677,22 +677,6 @@ __device__ void step_prologue(Consumer& c, const bf16* x, const bf16* norm_w, in
 }
 
 // ---- consumer: attention phase ---------------------------------------------------------------------------------
-// Per-head RMSNorm + RoPE of 4 values per lane already in registers (the arithmetic of head_norm_rope).
-__device__ __forceinline__ void norm_rope_regs(float (&v)[4], const bf16* nw, const bf16* cos_row, const bf16* sin_row,
-                                               int lane, float eps, float (&o)[4]) {
-  const int d0 = lane * 4;
-  const float ss = warp_sum(v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3]);
-  const float rstd = rsqrtf(ss / (float)HEAD_DIM + eps);
-#pragma unroll
-  for (int j = 0; j < 4; ++j) v[j] = bf16r(__bfloat162float(nw[d0 + j]) * bf16r(v[j] * rstd));
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const float partner = __shfl_xor_sync(0xffffffffu, v[j], 16);
-    const float rot = (lane < 16) ? -partner : partner;
-    o[j] = bf16r(v[j] * __bfloat162float(cos_row[d0 + j])) + bf16r(rot * __bfloat162float(sin_row[d0 + j]));
-  }
-}
-
 // Attention items (kv head, 64-key split) of this CTA: partial (m, l, o) per query head into o_part/ml_part.
 // The item owning position `pos` appends the new K/V row. Items go in batches of up to ST_ABATCH (one ring
 // stage each) so that every thread carries independent dot chains of several items: scores with thread =
@@ -728,7 +712,7 @@ __device__ void attention_phase(Consumer& c, const StepLayer& L, int l, int pos)
         const bf16* e = reinterpret_cast<const bf16*>(&raw);
         float v[4] = {__bfloat162float(e[0]), __bfloat162float(e[1]), __bfloat162float(e[2]), __bfloat162float(e[3])};
         float o[4];
-        norm_rope_regs(v, L.q_norm, cos_row, sin_row, lane, p.eps, o);
+        head_norm_rope(v, L.q_norm, cos_row, sin_row, lane, p.eps, o);
 #pragma unroll
         for (int j = 0; j < 4; ++j) sm.u.at.qs[slot][qh][lane * 4 + j] = bf16r(o[j]);
       } else {
@@ -742,7 +726,7 @@ __device__ void attention_phase(Consumer& c, const StepLayer& L, int l, int pos)
           const bf16* e = reinterpret_cast<const bf16*>(&raw);
           float v[4] = {__bfloat162float(e[0]), __bfloat162float(e[1]), __bfloat162float(e[2]), __bfloat162float(e[3])};
           float o[4];
-          norm_rope_regs(v, L.k_norm, cos_row, sin_row, lane, p.eps, o);
+          head_norm_rope(v, L.k_norm, cos_row, sin_row, lane, p.eps, o);
           bf16* dst = k_cache + ((size_t)kvh * p.max_seq + pos) * HEAD_DIM + lane * 4;
           bf16* sdst = reinterpret_cast<bf16*>(st + kv_swz(jn, lane * 4));
 #pragma unroll
