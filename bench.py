@@ -505,8 +505,10 @@ def timeline_summary(tl, n_layers: int, clock_ghz: float = 1.965) -> dict:
     csrc/step.cuh: 0 consumers start the phase, 1 prologue done (attention: merge start), 2 phase work done,
     3 producer's first load of the phase, 4-6 cumulative clock64 cycles (consumer warp 0 waiting for ring
     stages, folding units; producer waiting for free slots), 7 stage loop left (attention: partials done)).
+    Word 2 is stamped inside the grid barrier after the CTA's consumer warps have all finished the phase.
     Times in us: medians over CTAs, then over layers 1..n-1 (layer 0 includes the launch ramp). `barrier` is
-    the time from a CTA's end of the phase to its start of the next one; `ring_wait` the consumer's stage waits
+    the time from a CTA's end of the phase to its start of the next one; `tail` the time from consumer warp 0
+    leaving the stage loop to the whole CTA being done; `ring_wait` the consumer's stage waits
     inside the phase; `producer_wait` the producer's waits for free slots while issuing the phase."""
     import numpy as np
     t = tl.cpu().numpy().astype(np.int64)
@@ -537,7 +539,7 @@ def timeline_summary(tl, n_layers: int, clock_ghz: float = 1.965) -> dict:
         # leave the barrier after the last one arrived)
         for end_ph, end_w, nxt in ((b, 2, b + 1), (b + 1, 7, None), (b + 1, 2, b + 2), (b + 2, 2, b + 3),
                                    (b + 3, 2, b + 4), (b + 4, 2, b + 5)):
-            arrive = t[:, end_ph, end_w] if end_w != 2 or end_ph != b + 1 else t[:64, end_ph, 2]
+            arrive = t[:, end_ph, end_w]
             leave = t[:, b + 1, 1] if nxt is None else start(nxt)
             bar_stats.append((us(arrive.max() - np.median(arrive)), us(leave.min() - arrive.max()),
                               us(leave.max() - leave.min())))

@@ -2,15 +2,15 @@
 // attention over a bf16 cache, split merge. Two kernels per call (the second launched with programmatic
 // dependent launch):
 //
-//  attn_partials_kernel<CHUNK>   grid (n_kv * key blocks, batch), 128 threads. A CTA owns one block of 128
+//  attn_partials_kernel<CHUNK>   grid (n_kv * key blocks, batch), 256 threads. A CTA owns one block of 128
 //    consecutive keys of one (sequence, KV head): 128/CHUNK reference splits. Its K and V rows arrive by four
 //    TMA box loads ({64 dims, 128 keys}, 128-byte swizzle, issued before griddepcontrol.wait: they are earlier
 //    tokens' rows) so that 8 keys read at the same dims hit 8 different bank groups. After the wait the four
 //    query heads of the KV head are normalised and rotated (one warp each); the CTA whose block holds `pos`
 //    also writes the new K (normalised + rotated) and V rows to the cache and into its shared copy. Then
-//    thread = key computes the 4 heads' scores, one warp per (split, head) row takes the softmax (fp32
-//    probabilities), thread = dim computes P @ V for every split and head, and each split's unnormalised
-//    partial (m, l, o[128]) goes to o_part / ml_part.
+//    thread = (key, pair of query heads) computes the scores, one warp per (split, head) row takes the
+//    softmax (fp32 probabilities), thread = (dim, pair of heads) computes P @ V for every split, and each
+//    split's unnormalised partial (m, l, o[128]) goes to o_part / ml_part.
 //  attn_merge_kernel             grid (2 * n_q, batch), 128 threads: CTA (query head, 64-dim half) combines
 //    that head's split partials: M = max m_s, w_s = exp(m_s - M), out = bf16(sum_s w_s o_s / sum_s w_s l_s).
 //
@@ -27,7 +27,8 @@
 namespace qk {
 
 constexpr int ATT_KEYS = 128;          // keys per partials CTA (the rows of one TMA box)
-constexpr int ATT_THREADS = 128;
+constexpr int ATT_THREADS = 256;      // partials: thread = (key or dim, pair of query heads)
+constexpr int ATT_MERGE_THREADS = 128;
 constexpr int ATT_MERGE_ROUND = 128;   // splits staged per round of the merge
 
 struct AttnParams {
@@ -116,48 +117,54 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_partials_kernel(const __grid
     tma_load_4d(sm.v, &p.tm_v, 0, key0, kvh, b, &sm.bar);
     tma_load_4d(sm.v + ATT_KEYS * 128, &p.tm_v, 64, key0, kvh, b, &sm.bar);
   }
+  __syncthreads();            // the barrier's initialisation is visible to every thread
   grid_dep_wait();            // qkv comes from the kernel before
   if (tid == 0) tl_stamp(p.tl_slot, 1);
   const bf16* qkv = p.qkv + (size_t)b * p.qkv_stride;
   const bf16* cos_row = p.cos_tab + (size_t)pos * HEAD_DIM;
   const bf16* sin_row = p.sin_tab + (size_t)pos * HEAD_DIM;
-  {   // warp h: query head 4*kvh + h
+  const bool owns_new = pos - key0 < ATT_KEYS;
+  bool ok = true;
+  if (warp < GQA) {           // warp h: query head 4*kvh + h
     float o[4];
     head_norm_rope_from(qkv + (size_t)(kvh * GQA + warp) * HEAD_DIM, p.q_norm_w, cos_row, sin_row, lane, p.eps, o);
 #pragma unroll
     for (int j = 0; j < 4; ++j) sm.q[warp][lane * 4 + j] = bf16r(o[j]);
-  }
-  __syncthreads();            // also publishes the barrier's initialisation
-  const bool ok = mbar_wait(&sm.bar, 0);
-  const bool owns_new = pos - key0 < ATT_KEYS;
-  if (owns_new && warp < 2) { // the new token's K (warp 0) and V (warp 1) rows: cache slot `pos` and the copy here
+  } else if (owns_new && warp < GQA + 2) {
+    // the new token's K (warp 4: normalised + rotated) and V (warp 5) rows: cache slot `pos`, and the copy here
+    // once the block's TMA load has landed
     const int r = pos - key0;
     const size_t row = (((size_t)b * p.n_kv + kvh) * p.max_seq + pos) * HEAD_DIM + lane * 4;
-    if (warp == 0) {
+    if (warp == GQA) {
       float o[4];
       head_norm_rope_from(qkv + (size_t)(n_q + kvh) * HEAD_DIM, p.k_norm_w, cos_row, sin_row, lane, p.eps, o);
-      bf16* dst = p.k_cache + row;
-      bf16* sdst = reinterpret_cast<bf16*>(sm.k + att_off(r, lane * 4));
+      bf16 kb[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) dst[j] = sdst[j] = __float2bfloat16_rn(o[j]);
+      for (int j = 0; j < 4; ++j) kb[j] = __float2bfloat16_rn(o[j]);
+      *reinterpret_cast<uint2*>(p.k_cache + row) = *reinterpret_cast<const uint2*>(kb);
+      ok = mbar_wait(&sm.bar, 0);
+      *reinterpret_cast<uint2*>(sm.k + att_off(r, lane * 4)) = *reinterpret_cast<const uint2*>(kb);
     } else {
       uint2 raw;
       const bf16* src = qkv + (size_t)(n_q + p.n_kv + kvh) * HEAD_DIM + lane * 4;
       asm volatile("ld.global.cg.v2.u32 {%0,%1}, [%2];" : "=r"(raw.x), "=r"(raw.y) : "l"(src));
       *reinterpret_cast<uint2*>(p.v_cache + row) = raw;
+      ok = mbar_wait(&sm.bar, 0);
       *reinterpret_cast<uint2*>(sm.v + att_off(r, lane * 4)) = raw;
     }
   }
+  ok = mbar_wait(&sm.bar, 0) && ok;
   __syncthreads();
 
-  // scores: thread = key j of the block, all 4 heads; per head the CHUNK-dim slices summed in order, then added
+  // scores: thread = (key j of the block, query heads 2*hp, 2*hp+1); per head the CHUNK-dim slices summed in
+  // order, then added left to right
   {
-    const int j = tid, sp = j / CHUNK, split = key0 / CHUNK + sp;
+    const int j = tid & (ATT_KEYS - 1), hp = tid / ATT_KEYS, sp = j / CHUNK, split = key0 / CHUNK + sp;
     const bool valid = j - sp * CHUNK < min(CHUNK, ctx - split * CHUNK);
-    float total[GQA];
+    float total[2];
 #pragma unroll
     for (int sl = 0; sl < HEAD_DIM / CHUNK; ++sl) {
-      float d[GQA] = {0.f, 0.f, 0.f, 0.f};
+      float d[2] = {0.f, 0.f};
 #pragma unroll 4
       for (int i = 0; i < CHUNK / 8; ++i) {
         const int d0 = sl * CHUNK + i * 8;
@@ -165,9 +172,9 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_partials_kernel(const __grid
         const float kf[8] = {bf16lo(kv.x), bf16hi(kv.x), bf16lo(kv.y), bf16hi(kv.y),
                              bf16lo(kv.z), bf16hi(kv.z), bf16lo(kv.w), bf16hi(kv.w)};
 #pragma unroll
-        for (int h = 0; h < GQA; ++h) {
-          const float4 qa = *reinterpret_cast<const float4*>(&sm.q[h][d0]);
-          const float4 qb = *reinterpret_cast<const float4*>(&sm.q[h][d0 + 4]);
+        for (int h = 0; h < 2; ++h) {
+          const float4 qa = *reinterpret_cast<const float4*>(&sm.q[2 * hp + h][d0]);
+          const float4 qb = *reinterpret_cast<const float4*>(&sm.q[2 * hp + h][d0 + 4]);
           d[h] += qa.x * kf[0];
           d[h] += qa.y * kf[1];
           d[h] += qa.z * kf[2];
@@ -179,10 +186,10 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_partials_kernel(const __grid
         }
       }
 #pragma unroll
-      for (int h = 0; h < GQA; ++h) total[h] = sl == 0 ? d[h] : total[h] + d[h];
+      for (int h = 0; h < 2; ++h) total[h] = sl == 0 ? d[h] : total[h] + d[h];
     }
 #pragma unroll
-    for (int h = 0; h < GQA; ++h) sm.p[h][j] = valid ? total[h] * p.scale : -INFINITY;
+    for (int h = 0; h < 2; ++h) sm.p[2 * hp + h][j] = valid ? total[h] * p.scale : -INFINITY;
   }
   __syncthreads();
   // softmax: one warp per (split, head) row of CHUNK scores
@@ -213,28 +220,28 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_partials_kernel(const __grid
     }
   }
   __syncthreads();
-  // P @ V: thread = output dim d, every split of the block and every head; keys in order
+  // P @ V: thread = (output dim d, query heads 2*hp, 2*hp+1), every split of the block; keys in order
   {
-    const int d = tid;
+    const int d = tid & (HEAD_DIM - 1), hp = tid / HEAD_DIM;
 #pragma unroll
     for (int sp = 0; sp < NSPLIT; ++sp) {
       const int split = key0 / CHUNK + sp;
       if (split >= n_splits) break;
       const int nj = min(CHUNK, ctx - split * CHUNK);
-      float acc[GQA] = {0.f, 0.f, 0.f, 0.f};
+      float acc[2] = {0.f, 0.f};
       for (int j = 0; j < nj; ++j) {
         const int r = sp * CHUNK + j;
         const float vf = __bfloat162float(*reinterpret_cast<const bf16*>(sm.v + att_off(r, d)));
 #pragma unroll
-        for (int h = 0; h < GQA; ++h) acc[h] += sm.p[h][r] * vf;
+        for (int h = 0; h < 2; ++h) acc[h] += sm.p[2 * hp + h][r] * vf;
       }
 #pragma unroll
-      for (int h = 0; h < GQA; ++h) {
-        const size_t row = ((size_t)b * n_q + kvh * GQA + h) * p.max_splits + split;
+      for (int h = 0; h < 2; ++h) {
+        const size_t row = ((size_t)b * n_q + kvh * GQA + 2 * hp + h) * p.max_splits + split;
         p.o_part[row * HEAD_DIM + d] = acc[h];
         if (d == 0) {
-          p.ml_part[row * 2 + 0] = sm.m[sp][h];
-          p.ml_part[row * 2 + 1] = sm.l[sp][h];
+          p.ml_part[row * 2 + 0] = sm.m[sp][2 * hp + h];
+          p.ml_part[row * 2 + 1] = sm.l[sp][2 * hp + h];
         }
       }
     }
@@ -254,7 +261,7 @@ struct MergeSmem {
   // followed by w[max_splits] (dynamic)
 };
 
-__global__ void __launch_bounds__(ATT_THREADS) attn_merge_kernel(const __grid_constant__ AttnParams p) {
+__global__ void __launch_bounds__(ATT_MERGE_THREADS) attn_merge_kernel(const __grid_constant__ AttnParams p) {
   extern __shared__ __align__(16) uint8_t mg_smem[];
   MergeSmem& sm = *reinterpret_cast<MergeSmem*>(mg_smem);
   float* w = reinterpret_cast<float*>(mg_smem + sizeof(MergeSmem));
@@ -286,7 +293,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_merge_kernel(const __grid_co
   float acc = 0.f;
   for (int s0 = 0; s0 < n_splits; s0 += ATT_MERGE_ROUND) {
     const int ns = min(ATT_MERGE_ROUND, n_splits - s0);
-    for (int i = tid; i < ns * 16; i += ATT_THREADS) {   // 16 x 16 bytes per split row of 64 dims
+    for (int i = tid; i < ns * 16; i += ATT_MERGE_THREADS) {   // 16 x 16 bytes per split row of 64 dims
       const int s = i >> 4, f = i & 15;
       asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(&sm.o[s * 64 + f * 4])),
                    "l"(op + (size_t)(s0 + s) * HEAD_DIM + f * 4)

@@ -337,7 +337,7 @@ int qk_attention(const void* qkv, const void* q_norm_w, const void* k_norm_w, co
   if (int r = launch(partials, grid, dim3(ATT_THREADS), smem_p, stream, p)) return r;
   const int smem_m = (int)attn_merge_smem_bytes(max_splits);
   if (int r = ensure_smem((const void*)attn_merge_kernel, smem_m)) return r;
-  return launch(attn_merge_kernel, dim3(2 * n_kv * GQA, batch), dim3(ATT_THREADS), smem_m, stream, p);
+  return launch(attn_merge_kernel, dim3(2 * n_kv * GQA, batch), dim3(ATT_MERGE_THREADS), smem_m, stream, p);
 }
 
 int qk_lm_head_argmax(const void* w, const float* w_scale, int head_fp8, const void* x, const void* norm_w,

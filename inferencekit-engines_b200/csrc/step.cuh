@@ -52,6 +52,7 @@ constexpr int ST_MAX_SPLITS = 1024;                // contexts up to 64k
 // enough for the units that can be open at once (see the bound in gemv_phase).
 constexpr int ST_BD_FLOATS = 6144;
 constexpr int ST_MERGE_SPLITS = 64;                // splits staged per round of the attention merge
+constexpr int ST_TAIL_FLOATS = 96 * 16;            // StepSmem::tail: the remote block dots of a split unit
 constexpr int ST_ABATCH = 4;                       // attention items processed together (<= ST_NSTAGE)
 #ifndef ST_SPI
 #define ST_SPI 1                                   // GEMV stages a consumer warp takes per iteration
@@ -128,6 +129,9 @@ __device__ __forceinline__ void step_put(const StepParams& p, int phase, int i, 
 __device__ __forceinline__ void step_stamp(const StepParams& p, int phase, int i) {
   if (p.tl) step_put(p, phase, i, globaltimer());
 }
+__device__ __forceinline__ unsigned long long* step_word(const StepParams& p, int phase, int i) {
+  return p.tl ? p.tl + ((size_t)blockIdx.x * (5 * p.n_layers + 1) + phase) * ST_TL_WORDS + i : nullptr;
+}
 
 struct StepSmem {
   uint8_t ring[ST_NSTAGE][ST_STAGE];
@@ -147,11 +151,16 @@ struct StepSmem {
       float cl;                                    // sum_s exp(m_s - M) * l_s
     } mg;
   } u;
+  // block dots of the last unit of a GEMV phase that continue in the next CTA, fetched from `part` as soon as
+  // that CTA has published them (a unit has at most 96 * 16 of them; the folding warp fetches KB * NG - 1 at most)
+  __align__(16) float tail[ST_TAIL_FLOATS];
   float red[8];
   unsigned long long bestbuf[ST_WARPS];
   uint64_t full[ST_NSTAGE], empty[ST_NSTAGE];
   int flag;
 };
+
+static_assert(sizeof(StepSmem) <= 227 * 1024, "the fused step's shared memory exceeds a CTA's 227 KB");
 
 // ---- small helpers -------------------------------------------------------------------------------------------
 __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(ST_WARPS * 32) : "memory"); }
@@ -222,9 +231,10 @@ __device__ __forceinline__ uint4 ldcg_u4(const void* p) {
 
 // Consumer-side grid barrier number `idx` (0-based) of this launch. Bounded: on timeout it records the error and
 // lets the CTA continue (wrong results, but no hang).
-__device__ __forceinline__ void grid_barrier(unsigned* ctr, unsigned idx) {
+__device__ __forceinline__ void grid_barrier(unsigned* ctr, unsigned idx, unsigned long long* tl_word = nullptr) {
   consumer_sync();   // orders the CTA's writes before thread 0's release below
   if (threadIdx.x == 0) {
+    if (tl_word) *tl_word = globaltimer();   // every consumer warp of the CTA has finished the phase
     asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(ctr) : "memory");
     const unsigned target = (idx + 1) * gridDim.x;
     const long long c0 = clock64();
@@ -395,13 +405,28 @@ __device__ __forceinline__ void fetch_unit_tail(const Consumer& c, const float* 
   }
 }
 
+// Issue the copy of unit u's block dots of slices [hi, end of unit), published by the following CTA(s), into
+// sm.tail (cp.async through L2; the folding warp waits for it when it folds the unit).
+template <int KB, int NG>
+__device__ __forceinline__ void prefetch_unit_tail(const Consumer& c, const float* part, float* tail, int u, int hi) {
+  constexpr int spu = KB * NG, RPU = 16 * NG;
+  constexpr int MAXV = (spu * 4 + 31) / 32;
+  const int off4 = (hi - u * spu) * 4, n4 = spu * 4 - off4;    // 16-byte vectors to copy
+  const uint4* gsrc = reinterpret_cast<const uint4*>(part + (size_t)u * KB * RPU) + off4;
+#pragma unroll
+  for (int j = 0; j < MAXV; ++j) {
+    const int i4 = c.lane + 32 * j;
+    if (i4 < n4) cp_async16_cg(reinterpret_cast<uint4*>(tail) + i4, gsrc + i4);
+  }
+}
+
 // Fold of one 16-row unit (32 rows for gate|up) once this CTA's block dots of it are complete: the per-op
 // kernel's in-order sum acc += d * sx * sw over K blocks, then the epilogue. Gate rows fold on lanes 0-15 and
 // up rows on lanes 16-31. A unit shared with a neighbouring CTA is folded by whichever CTA completes it last,
 // from the global scratch. The block dots are read 16 at a time (independent loads), then summed in order.
 template <int KB, int EPI, int SCALE, int NG>
 __device__ __forceinline__ void fold_unit(Consumer& c, const GemvPhase<EPI, SCALE, NG>& ph, const SliceRange& r,
-                                          int u, const FoldPre& pre) {
+                                          int u, const FoldPre& pre, bool tail_fetched = false) {
   StepSmem& sm = *c.sm;
   constexpr int RPU = 16 * NG, spu = KB * NG, slot_floats = KB * RPU, nslots = ST_BD_FLOATS / slot_floats;
   constexpr int FB = KB % 16 == 0 ? 16 : (KB % 8 == 0 ? 8 : 4);   // block dots read per batch
@@ -423,20 +448,29 @@ __device__ __forceinline__ void fold_unit(Consumer& c, const GemvPhase<EPI, SCAL
     // start with it): wait for them, then copy their block dots behind this CTA's own in the slot. A slice is
     // 16 consecutive floats of the unit's [KB][NG][16] layout, so the rest is one contiguous run.
     const int need = (u + 1) * spu - hi;
-    const unsigned* ctr = reinterpret_cast<const unsigned*>(ph.counters + u);
-    bool ok = __all_sync(0xffffffffu, ld_acquire_u32(ctr) >= (unsigned)need);
-    if (!ok) {
-      const unsigned long long t0 = globaltimer();
-      while (!(ok = __all_sync(0xffffffffu, ld_acquire_u32(ctr) >= (unsigned)need))) {
-        if (wait_failed()) break;
-        if (globaltimer() - t0 > WAIT_LIMIT_NS) {
-          if (c.lane == 0) atomicOr(&g_dev_error, DEVERR_GRID_TIMEOUT);
-          break;
+    bool ok = true;
+    if (tail_fetched) {   // already copied into sm.tail during the phase: move it behind this CTA's dots
+      cp_async_wait_all();
+      __syncwarp();
+      const int off4 = (hi - u * spu) * 4, n4 = spu * 4 - off4;
+      for (int i4 = c.lane; i4 < n4; i4 += 32)
+        reinterpret_cast<uint4*>(slot)[off4 + i4] = reinterpret_cast<const uint4*>(sm.tail)[i4];
+    } else {
+      const unsigned* ctr = reinterpret_cast<const unsigned*>(ph.counters + u);
+      ok = __all_sync(0xffffffffu, ld_acquire_u32(ctr) >= (unsigned)need);
+      if (!ok) {
+        const unsigned long long t0 = globaltimer();
+        while (!(ok = __all_sync(0xffffffffu, ld_acquire_u32(ctr) >= (unsigned)need))) {
+          if (wait_failed()) break;
+          if (globaltimer() - t0 > WAIT_LIMIT_NS) {
+            if (c.lane == 0) atomicOr(&g_dev_error, DEVERR_GRID_TIMEOUT);
+            break;
+          }
         }
       }
+      if (ok) fetch_unit_tail<KB, NG>(c, ph.part, slot, u, hi);
+      cp_async_wait_all();
     }
-    if (ok) fetch_unit_tail<KB, NG>(c, ph.part, slot, u, hi);
-    cp_async_wait_all();
     __syncwarp();
     if (c.lane == 0 && ok) ph.counters[u] = 0;
   }
@@ -508,9 +542,21 @@ __device__ void gemv_phase(Consumer& c, const GemvPhase<EPI, SCALE, NG>& ph) {
   int fu = u_lo + c.warp;                                       // next unit this warp folds
   auto last_stage = [&](int u) { return (min((u + 1) * spu, r.s1) - 1 - r.s0) / ST_SLICES; };
   FoldPre pre = fold_prefetch(c, ph, fu, fu <= u_hi);
+  // The last unit continues in the next CTA when it ends past this range; the CTA holding its first block
+  // folds it. The next CTA publishes its share early in the phase, so the folding warp copies it into sm.tail
+  // as soon as the counter shows it (polled once per iteration) instead of fetching it at the end.
+  const int tail_need = (u_hi + 1) * spu - r.s1;
+  int tail_state = (u_hi >= u_lo && tail_need > 0 && u_hi * spu >= r.s0 && c.warp == (u_hi - u_lo) % ST_WARPS) ? 1 : 0;
+  auto poll_tail = [&]() {   // 1: not fetched yet, 2: copy issued
+    const unsigned* ctr = reinterpret_cast<const unsigned*>(ph.counters + u_hi);
+    if (__all_sync(0xffffffffu, ld_acquire_u32(ctr) >= (unsigned)tail_need)) {
+      prefetch_unit_tail<KB, NG>(c, ph.part, sm.tail, u_hi, r.s1);
+      tail_state = 2;
+    }
+  };
   auto fold_next = [&]() {   // fold unit fu, move on to this warp's next unit and prefetch its row inputs
     const long long t0 = clock64();
-    fold_unit<KB>(c, ph, r, fu, pre);
+    fold_unit<KB>(c, ph, r, fu, pre, fu == u_hi && tail_state == 2);
     fu += ST_WARPS;
     pre = fold_prefetch(c, ph, fu, fu <= u_hi);
     c.fold_cycles += clock64() - t0;
@@ -580,6 +626,7 @@ __device__ void gemv_phase(Consumer& c, const GemvPhase<EPI, SCALE, NG>& ph) {
     for (int j = 0; j < ST_SPI; ++j)
       if (j < ns) c.release_stage((n0 + i + j) % ST_NSTAGE);
     c.n = n0 + i_hi + 1;
+    if (tail_state == 1) poll_tail();
     while (fu <= u_hi && last_stage(fu) <= i_hi && c.released_test(n0 + last_stage(fu))) {
       fold_next();
     }
@@ -1020,8 +1067,8 @@ __global__ void __launch_bounds__(ST_THREADS, 1) decode_step_kernel(const __grid
     if (tl) step_stamp(p, ph, 1);
     c.tl_phase = ph;
     gemv_phase<32>(c, GemvPhase<EPI_STORE, SCALE, 1>{L.s_qkv, QKV_N, H, p.qkv, p.part, p.counters});
-    if (tl) { step_stamp(p, ph, 2); step_put(p, ph, 4, c.wait_cycles); step_put(p, ph, 5, c.fold_cycles); }
-    grid_barrier(p.sync, nbar++);
+    if (tl) { step_put(p, ph, 4, c.wait_cycles); step_put(p, ph, 5, c.fold_cycles); }
+    grid_barrier(p.sync, nbar++, step_word(p, ph, 2));
     // ATTN: split partials (and the K/V rows at pos), then the merge into the attention output
     if (tl) step_stamp(p, ph + 1, 0);
     attention_phase<NKV>(c, L, l, pos);
@@ -1029,8 +1076,8 @@ __global__ void __launch_bounds__(ST_THREADS, 1) decode_step_kernel(const __grid
     grid_barrier(p.sync, nbar++);
     if (tl) step_stamp(p, ph + 1, 1);
     merge_phase<NQ>(c, pos);
-    if (tl) { step_stamp(p, ph + 1, 2); step_put(p, ph + 1, 4, c.wait_cycles); step_put(p, ph + 1, 5, c.fold_cycles); }
-    grid_barrier(p.sync, nbar++);
+    if (tl) { step_put(p, ph + 1, 4, c.wait_cycles); step_put(p, ph + 1, 5, c.fold_cycles); }
+    grid_barrier(p.sync, nbar++, step_word(p, ph + 1, 2));
     // O: resid += W_o . quant(attn)   (TP: this rank's fp32 partial, exchanged)
     if (tl) step_stamp(p, ph + 2, 0);
     step_prologue<false>(c, p.attn, nullptr, KO, p.eps, nullptr);
@@ -1042,20 +1089,20 @@ __global__ void __launch_bounds__(ST_THREADS, 1) decode_step_kernel(const __grid
       gemv_phase<KO / QB>(c, GemvPhase<EPI_TP_PARTIAL, SCALE, 1>{L.s_o, H, KO, nullptr, p.part, p.counters, 0,
                                                                  (int)(xk % 2), (unsigned)(x_base + xk + 1)});
     }
-    if (tl) { step_stamp(p, ph + 2, 2); step_put(p, ph + 2, 4, c.wait_cycles); step_put(p, ph + 2, 5, c.fold_cycles); }
+    if (tl) { step_put(p, ph + 2, 4, c.wait_cycles); step_put(p, ph + 2, 5, c.fold_cycles); }
     if (TP > 1) {   // the tags tell a reducer when every rank's partial of its row has arrived
       tp_reduce(p, rbuf(xk), rbuf(xk + 1), (int)(xk % 2), (unsigned)(x_base + xk + 1));
       ++xk;
     }
-    grid_barrier(p.sync, nbar++);
+    grid_barrier(p.sync, nbar++, step_word(p, ph + 2, 2));
     // GU: h = SwiGLU(W_gu . quant(RMSNorm(resid)))
     if (tl) step_stamp(p, ph + 3, 0);
     step_prologue<true>(c, rbuf(xk), L.ln2, H, p.eps, nullptr);
     if (tl) step_stamp(p, ph + 3, 1);
     c.tl_phase = ph + 3;
     gemv_phase<32>(c, GemvPhase<EPI_SWIGLU, SCALE, 2>{L.s_gu, 2 * I, H, p.h, p.part, p.counters});
-    if (tl) { step_stamp(p, ph + 3, 2); step_put(p, ph + 3, 4, c.wait_cycles); step_put(p, ph + 3, 5, c.fold_cycles); }
-    grid_barrier(p.sync, nbar++);
+    if (tl) { step_put(p, ph + 3, 4, c.wait_cycles); step_put(p, ph + 3, 5, c.fold_cycles); }
+    grid_barrier(p.sync, nbar++, step_word(p, ph + 3, 2));
     // DOWN: resid += W_down . quant(h)   (TP: partial, exchanged)
     if (tl) step_stamp(p, ph + 4, 0);
     step_prologue<false>(c, p.h, nullptr, I, p.eps, nullptr);
@@ -1067,12 +1114,12 @@ __global__ void __launch_bounds__(ST_THREADS, 1) decode_step_kernel(const __grid
       gemv_phase<I / QB>(c, GemvPhase<EPI_TP_PARTIAL, SCALE, 1>{L.s_down, H, I, nullptr, p.part, p.counters, 0,
                                                                 (int)(xk % 2), (unsigned)(x_base + xk + 1)});
     }
-    if (tl) { step_stamp(p, ph + 4, 2); step_put(p, ph + 4, 4, c.wait_cycles); step_put(p, ph + 4, 5, c.fold_cycles); }
+    if (tl) { step_put(p, ph + 4, 4, c.wait_cycles); step_put(p, ph + 4, 5, c.fold_cycles); }
     if (TP > 1) {
       tp_reduce(p, rbuf(xk), rbuf(xk + 1), (int)(xk % 2), (unsigned)(x_base + xk + 1));
       ++xk;
     }
-    grid_barrier(p.sync, nbar++);
+    grid_barrier(p.sync, nbar++, step_word(p, ph + 4, 2));
   }
   if (tl) step_stamp(p, 5 * p.n_layers, 0);
   // HEAD: logits + greedy argmax (FP8 per-channel head; TP: this rank's vocabulary rows)
