@@ -501,15 +501,17 @@ PHASES = ("qkv", "attn", "o_proj", "gate_up", "down")
 
 
 def timeline_summary(tl, n_layers: int, clock_ghz: float = 1.965) -> dict:
-    """Per-phase breakdown of one fused-step launch from its timeline (int64 [CTAs, 5*layers+1, 8], words as in
-    csrc/step.cuh: 0 consumers start the phase, 1 prologue done (attention: merge start), 2 phase work done,
-    3 producer's first load of the phase, 4-6 cumulative clock64 cycles (consumer warp 0 waiting for ring
-    stages, folding units; producer waiting for free slots), 7 stage loop left (attention: partials done)).
-    Word 2 is stamped inside the grid barrier after the CTA's consumer warps have all finished the phase.
-    Times in us: medians over CTAs, then over layers 1..n-1 (layer 0 includes the launch ramp). `barrier` is
-    the time from a CTA's end of the phase to its start of the next one; `tail` the time from consumer warp 0
-    leaving the stage loop to the whole CTA being done; `ring_wait` the consumer's stage waits
-    inside the phase; `producer_wait` the producer's waits for free slots while issuing the phase."""
+    """Per-phase breakdown of one fused-step launch from its timeline (int64 [CTAs, 5*layers+1, 16], words as in
+    csrc/step.cuh: 0 consumers start the phase, 1 prologue done (attention: arrival counted and, on the CTA
+    that completed a KV head, its merge done), 2 the whole CTA done (stamped inside the grid barrier), 3
+    producer's first load of the phase, 4-6 cumulative clock64 cycles (consumer warp 0 waiting for ring
+    stages, folding units; producer waiting for free slots), 7 consumer warp 0 leaves the stage loop
+    (attention: partials done), 8 cumulative cycles warp 0 waited for the slowest warp to release a stage it
+    folds, 9-15 warps 1-7 leave the stage loop). Times in us: medians over CTAs, then over layers 1..n-1 (layer 0 includes the
+    launch ramp). `barrier` is the time from a CTA's end of the phase to its start of the next one; `tail` from
+    warp 0 leaving the stage loop to the whole CTA being done; `ring_wait` the consumer's stage waits inside
+    the phase; `producer_wait` the producer's waits for free slots while issuing the phase. For every grid
+    barrier: how long after the median CTA the last one arrived, and how long after that the first CTA left."""
     import numpy as np
     t = tl.cpu().numpy().astype(np.int64)
     G, P = t.shape[0], t.shape[1]
@@ -517,38 +519,37 @@ def timeline_summary(tl, n_layers: int, clock_ghz: float = 1.965) -> dict:
     cyc = lambda a: a / (clock_ghz * 1e3)  # noqa: E731  (clock64 cycles -> us)
     cw = np.diff(np.concatenate([np.zeros((G, 1), np.int64), t[:, :, 4]], axis=1), axis=1)   # per phase
     pw = np.diff(np.concatenate([t[:, :, 6], t[:, -1:, 6]], axis=1), axis=1)                 # phase -> next phase
-    start = lambda ph: t[:, ph, 0] if ph < P else None   # noqa: E731
     names = {0: "qkv", 2: "o_proj", 3: "gate_up", 4: "down"}
-    per = {k: [] for k in ("qkv", "attn", "merge", "o_proj", "gate_up", "down")}
+    per = {k: [] for k in ("qkv", "attn", "o_proj", "gate_up", "down")}
     layer_us, bar_stats = [], []
     for l in (range(1, n_layers) if n_layers > 1 else range(n_layers)):
         b = 5 * l
         for j, name in names.items():
             ph = t[:, b + j]
-            nxt = start(b + j + 1)
+            exits = np.concatenate([ph[:, 7:8], ph[:, 9:16]], axis=1)      # loop exit of warps 0..7
+            rw = np.diff(np.concatenate([np.zeros((G, 1), np.int64), t[:, :, 8]], axis=1), axis=1)
             per[name].append(dict(prologue=us(ph[:, 1] - ph[:, 0]), stage_loop=us(ph[:, 7] - ph[:, 1]),
-                                  tail=us(ph[:, 2] - ph[:, 7]), barrier=us(nxt - ph[:, 2]),
-                                  ring_wait=cyc(cw[:, b + j]), producer_wait=cyc(pw[:, b + j])))
+                                  tail=us(ph[:, 2] - ph[:, 7]), barrier=us(t[:, b + j + 1, 0] - ph[:, 2]),
+                                  ring_wait=cyc(cw[:, b + j]), producer_wait=cyc(pw[:, b + j]),
+                                  warp_exit_spread=us(exits.max(1) - exits.min(1)),
+                                  last_warp_to_done=us(ph[:, 2] - exits.max(1)),
+                                  fold=cyc(np.diff(np.concatenate([np.zeros((G, 1), np.int64), t[:, :, 5]], axis=1),
+                                                   axis=1)[:, b + j]),
+                                  slowest_warp_wait=cyc(rw[:, b + j])))
         a = t[:, b + 1]
-        per["attn"].append(dict(work=us(a[:, 7] - a[:, 0]), barrier=us(a[:, 1] - a[:, 7]),
-                                producer_wait=cyc(pw[:, b + 1])))
-        per["merge"].append(dict(work=us(a[:64, 2] - a[:64, 1]), barrier=us(t[:, b + 2, 0] - a[:, 2]),
-                                 ring_wait_attn_and_merge=cyc(cw[:, b + 1])))
-        layer_us.append(np.median(us(start(b + 5) - t[:, b, 0])))
-        # each grid barrier of the layer: spread of the CTAs' arrivals, and the release latency (first CTA to
-        # leave the barrier after the last one arrived)
-        for end_ph, end_w, nxt in ((b, 2, b + 1), (b + 1, 7, None), (b + 1, 2, b + 2), (b + 2, 2, b + 3),
-                                   (b + 3, 2, b + 4), (b + 4, 2, b + 5)):
-            arrive = t[:, end_ph, end_w]
-            leave = t[:, b + 1, 1] if nxt is None else start(nxt)
-            bar_stats.append((us(arrive.max() - np.median(arrive)), us(leave.min() - arrive.max()),
-                              us(leave.max() - leave.min())))
+        merged = us(a[:, 1] - a[:, 7])
+        per["attn"].append(dict(partials=us(a[:, 7] - a[:, 0]), arrive=merged,
+                                merge_on_merging_ctas=np.sort(merged)[-4:], tail=us(a[:, 2] - a[:, 1]),
+                                barrier=us(t[:, b + 2, 0] - a[:, 2]), producer_wait=cyc(pw[:, b + 1])))
+        layer_us.append(np.median(us(t[:, b + 5, 0] - t[:, b, 0])))
+        for end_ph in (b, b + 1, b + 2, b + 3, b + 4):
+            arrive, leave = t[:, end_ph, 2], t[:, end_ph + 1, 0]
+            bar_stats.append((us(arrive.max() - np.median(arrive)), us(leave.min() - arrive.max())))
     out = {"ctas": G, "layers": n_layers, "layer_us": float(np.median(layer_us))}
-    names_b = ["qkv->attn", "attn->merge", "merge->o", "o->gu", "gu->down", "down->qkv"]
-    bs = np.array(bar_stats).reshape(-1, 6, 3)
+    bs = np.array(bar_stats).reshape(-1, 5, 2)
     out["barriers"] = {n: {"last_arrival_after_median_us": round(float(np.median(bs[:, i, 0])), 3),
-                           "release_after_last_arrival_us": round(float(np.median(bs[:, i, 1])), 3),
-                           "leave_spread_us": round(float(np.median(bs[:, i, 2])), 3)} for i, n in enumerate(names_b)}
+                           "release_after_last_arrival_us": round(float(np.median(bs[:, i, 1])), 3)}
+                       for i, n in enumerate(["qkv->attn", "attn->o", "o->gu", "gu->down", "down->qkv"])}
     for k, v in per.items():
         out[k] = {f: round(float(np.median([np.median(d[f]) for d in v])), 3) for f in v[0]}
     h = t[:, 5 * n_layers]
@@ -556,7 +557,6 @@ def timeline_summary(tl, n_layers: int, clock_ghz: float = 1.965) -> dict:
                    "stage_loop": float(np.median(us(h[:, 7] - h[:, 1]))),
                    "tail": float(np.median(us(h[:, 2] - h[:, 7])))}
     out["launch_us"] = float(us(h[:, 2].max() - t[:, 0, 0].min()))
-    # how far ahead of the consumers the producer issued each phase's first load
     lead = [np.median(us(t[:, p, 0] - t[:, p, 3])) for p in range(5, 5 * n_layers)]
     out["producer_lead_us"] = float(np.median(lead))
     return out
@@ -576,7 +576,7 @@ def run_timeline(args):
     eng = Engine(m, fused=True)
     n = len(m.layers)
     sms = torch.cuda.get_device_properties(0).multi_processor_count
-    eng.step_timeline = torch.zeros(sms, 5 * n + 1, 8, dtype=torch.int64, device="cuda")
+    eng.step_timeline = torch.zeros(sms, 5 * n + 1, 16, dtype=torch.int64, device="cuda")
     eng.token.fill_(1)
     eng.state.copy_(torch.tensor([start, 0], dtype=torch.int32))
     for _ in range(args.launches):

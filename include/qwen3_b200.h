@@ -154,16 +154,20 @@ typedef struct {
  *               [8][max_seq][128] (16-byte aligned, stride a multiple of 16); read through TMA tensor maps
  *   state       [pos, step]; token [1]; out_tokens [out_len]; best u64 [1] zero before the first launch
  *   resid/qkv/attn/h/logits  bf16 activations [4096]/[6144]/[4096]/[12288]/[vocab]
- *   part        fp32 scratch of part_floats >= qk_decode_step_part_floats(vocab) floats; counters int
+ *   part        scratch of part_floats >= qk_decode_step_part_floats(vocab) floats (tagged block dots of the
+ *               GEMV units two CTAs share), zeroed once before the first launch; counters int
  *               [n_counters >= qk_decode_step_counters(vocab)], zero before the first launch
  *   o_part/ml_part  fp32 [32][max_splits][128] / [32][max_splits][2]; attn_counters int [8] zero
- *   sync        unsigned [2] zero before the first launch (left zero)
+ *   sync        unsigned [4] zeroed once before the first launch: [0], [1] barrier counters (left zero), [2] the
+ *               launches completed (tags of the shared block dots; zero it only together with `part`)
  *   max_splits  >= ceil(max_seq/64), <= 1024
- *   timeline    NULL, or a device buffer of (#SMs) x (5*n_layers + 1) x 8 u64: per CTA and phase (layer l:
+ *   timeline    NULL, or a device buffer of (#SMs) x (5*n_layers + 1) x 16 u64: per CTA and phase (layer l:
  *               qkv, attn, o, gu, down = 5l+0..4; lm_head = 5*n_layers) the %globaltimer of 0 consumers start,
- *               1 prologue done (attention: split partials done), 2 work done, 3 producer issues the phase's
- *               first load; then cumulative clock64 cycles: 4 consumer warp 0 waiting for data, 5 consumer
- *               warp 0 folding units, 6 producer waiting for free ring stages.
+ *               1 prologue done (attention: arrivals counted and, on merging CTAs, the merge done), 2 the whole
+ *               CTA done (inside the grid barrier), 3 producer issues the phase's first load, 7 consumer warp 0
+ *               leaves the stage loop (attention: partials done), 9-15 consumer warps 1-7 leave it; cumulative
+ *               clock64 cycles: 4 consumer warp 0 waiting for data, 5 consumer warp 0 folding units, 6 producer
+ *               waiting for free ring stages, 8 consumer warp 0 waiting for the slowest warp to release a stage.
  */
 int qk_decode_step(const qk_layer_t* layers, int n_layers, void* k_cache, void* v_cache, long long kv_layer_stride,
                    const void* embed, const void* final_norm, const void* w_head, const float* s_head, int vocab,

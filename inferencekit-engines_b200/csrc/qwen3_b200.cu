@@ -388,13 +388,13 @@ int qk_lm_head_argmax(const void* w, const float* w_scale, int head_fp8, const v
   return launch(lm_head_bf16_kernel, dim3(ctas > 0 ? ctas : sms), dim3(HEAD_WARPS * 32), smem, stream, p);
 }
 
-// Scratch of the fused step: block dots of the GEMV units shared by two CTAs, indexed by unit, so sized for
-// the largest N*K/128 (gate|up: 24576*4096/128, or the head: vocab*32) and the most units (gate|up pairs: 768,
-// or the head: vocab/16).
+// Scratch of the fused step: the tagged block dots (one u64 = two floats each) of the GEMV units shared by two
+// CTAs, indexed by unit, so sized for the largest N*K/128 (gate|up: 24576*4096/128, or the head: vocab*32); and
+// the unit counters, sized for the most units (gate|up pairs: 768, or the head: vocab/16).
 long long qk_decode_step_part_floats(int vocab) {
   const long long gu = 24576LL * 4096 / 128, down = 4096LL * 12288 / 128, head = (long long)vocab * 4096 / 128;
   long long m = gu > down ? gu : down;
-  return m > head ? m : head;
+  return 2 * (m > head ? m : head);
 }
 int qk_decode_step_counters(int vocab) {
   const int head = vocab / 16;

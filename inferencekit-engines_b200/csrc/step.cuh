@@ -51,7 +51,7 @@ constexpr int ST_MAX_SPLITS = 1024;                // contexts up to 64k
 // Block-dot slots: a slot holds one open unit's KB x 16*NG block dots (2-6 KiB); 24 KiB gives 12, 6 or 4 slots,
 // enough for the units that can be open at once (see the bound in gemv_phase).
 constexpr int ST_BD_FLOATS = 6144;
-constexpr int ST_MERGE_SPLITS = 64;                // splits staged per round of the attention merge
+constexpr int ST_MERGE_ROUND = 128;                // splits staged per round of the attention merge
 constexpr int ST_TAIL_FLOATS = 96 * 16;            // StepSmem::tail: the remote block dots of a split unit
 constexpr int ST_ABATCH = 4;                       // attention items processed together (<= ST_NSTAGE)
 #ifndef ST_SPI
@@ -102,11 +102,12 @@ struct StepParams {
   int out_len;
   unsigned long long* best;                        // [1], zero between launches
   bf16 *resid, *qkv, *attn, *h, *logits;           // activations [4096], [6144], [4096], [12288], [vocab]
-  float* part;                                     // GEMV boundary-unit block dots [max N*K/128]
+  float* part;                                     // tagged block dots of split units: u64 [max N*K/128], zeroed once
   int* counters;                                   // [max N/16], zero between launches
   float *o_part, *ml_part;                         // attention partials [32][max_splits][128], [32][max_splits][2]
   int* attn_counters;                              // [8], zero between launches
-  unsigned* sync;                                  // [2]: grid barrier counter, end counter; zero between launches
+  unsigned* sync;                                  // [4]: grid barrier counter, end counter (zero between
+                                                   // launches), launches completed (never reset), unused
   int max_seq, max_splits;
   float eps, attn_scale;
   unsigned long long* tl;                          // optional timeline [CTA][phase][8], null when off
@@ -122,7 +123,9 @@ struct StepParams {
 // Words 4-6 are cumulative clock64 cycles up to the end of the phase: 4 consumer warp 0 waiting for stages,
 // 5 consumer warp 0 folding units, 6 producer waiting for free stages (cumulative at the phase's first load).
 // Word 7: warp 0 leaves a GEMV phase's stage loop (before its last folds); the attention partials are done.
-constexpr int ST_TL_WORDS = 8;
+// Word 8: cumulative clock64 cycles consumer warp 0 spent waiting for the slowest warp to release a stage it
+// must fold. Words 9-15: GEMV phases: consumer warps 1-7 leave the stage loop (%globaltimer).
+constexpr int ST_TL_WORDS = 16;
 __device__ __forceinline__ void step_put(const StepParams& p, int phase, int i, unsigned long long v) {
   if (p.tl) p.tl[((size_t)blockIdx.x * (5 * p.n_layers + 1) + phase) * ST_TL_WORDS + i] = v;
 }
@@ -146,14 +149,17 @@ struct StepSmem {
       float m_s[ST_ABATCH][GQA], l_s[ST_ABATCH][GQA];
     } at;
     struct {
-      float o[ST_MERGE_SPLITS * 64];               // partial outputs of up to 64 splits, 64 dims each
-      float cw[ST_MAX_SPLITS];                     // exp(m_s - M) per split
+      float o[ST_MERGE_ROUND * 32];                // partial outputs of up to ST_MERGE_ROUND splits, 32 dims each
+      float w[ST_MAX_SPLITS];                      // exp(m_s - M) per split
       float cl;                                    // sum_s exp(m_s - M) * l_s
     } mg;
   } u;
-  // block dots of the last unit of a GEMV phase that continue in the next CTA, fetched from `part` as soon as
-  // that CTA has published them (a unit has at most 96 * 16 of them; the folding warp fetches KB * NG - 1 at most)
-  __align__(16) float tail[ST_TAIL_FLOATS];
+  // Block dots of the last unit of a GEMV phase when it continues in the next CTA: the tail-fetcher warp copies
+  // them (tagged words in `part`) into tail[n % 2] as soon as that CTA has published them (a unit has KB * NG <= 96 slices of
+  // 16 dots; at most all but one come from the next CTA). tail_full[b]: the copy landed (32 lane arrivals);
+  // tail_empty[b]: the folding warp has used it.
+  __align__(16) float tail[2][ST_TAIL_FLOATS];
+  uint64_t tail_full[2], tail_empty[2];
   float red[8];
   unsigned long long bestbuf[ST_WARPS];
   uint64_t full[ST_NSTAGE], empty[ST_NSTAGE];
@@ -196,6 +202,20 @@ __device__ __forceinline__ void wait_sys_counter(const unsigned long long* p, un
       return;
     }
   }
+}
+__device__ __forceinline__ void st_relaxed_gpu_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_gpu_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+// Tag of the block dots a GEMV phase shares between CTAs: unique per (launch, phase) over 2^32 - 1 phases and
+// never 0, so a zeroed `part` or an earlier phase's words never pass for this phase's.
+__device__ __forceinline__ unsigned dots_tag(unsigned epoch, int n_layers, int phase) {
+  const unsigned long long k = (unsigned long long)epoch * (unsigned)(5 * n_layers + 1) + (unsigned)phase;
+  return 1u + (unsigned)(k % 0xFFFFFFFFull);
 }
 __device__ __forceinline__ void red_add_relaxed(int* p, int v) {
   asm volatile("red.relaxed.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -329,6 +349,7 @@ struct GemvPhase {
   int row_offset = 0; // ARGMAX: global id of row 0 (vocabulary shard)
   int xbuf = 0;       // TP_PARTIAL: exchange buffer (k % 2)
   unsigned xtag = 0;  // TP_PARTIAL: the exchange's tag
+  unsigned dtag = 0;  // tag of this phase's shared block dots (set by gemv_phase)
 };
 constexpr int EPI_TP_PARTIAL = 10;   // fp32 row partial into every rank's TpArea (row-parallel shard)
 
@@ -341,6 +362,9 @@ struct Consumer {
   int best_i;
   long long wait_cycles, fold_cycles;
   int tl_phase = 0;   // timeline phase index of the phase being run
+  long long relwait_cycles = 0;   // waiting for the slowest warp to release a stage this warp folds
+  unsigned epoch = 0;             // launches completed before this one (the block-dot tags)
+  int tail_n = 0;     // GEMV phases so far with a split unit folded here (the tail buffers' use count)
 
   __device__ __forceinline__ bool wait_stage(int s) { return wait_abs(n); }
   // wait for the load of the consumer's stage number `m` (counted over the whole launch)
@@ -360,7 +384,10 @@ struct Consumer {
     return released_wait(m);
   }
   __device__ __forceinline__ bool released_wait(int m) {
-    return __all_sync(0xffffffffu, mbar_wait(&sm->empty[m % ST_NSTAGE], (uint32_t)((m / ST_NSTAGE) & 1)));
+    const long long t0 = clock64();
+    const bool ok = __all_sync(0xffffffffu, mbar_wait(&sm->empty[m % ST_NSTAGE], (uint32_t)((m / ST_NSTAGE) & 1)));
+    relwait_cycles += clock64() - t0;
+    return ok;
   }
   __device__ __forceinline__ void release_stage(int s) {
     __syncwarp();
@@ -390,34 +417,78 @@ __device__ __forceinline__ FoldPre fold_prefetch(const Consumer& c, const GemvPh
   return f;
 }
 
-// Copy the block dots of unit u's slices [hi, end of unit), published by the following CTA(s) in `part`, into
-// the unit's slot behind this CTA's own (cp.async through L2; the caller waits).
-template <int KB, int NG>
-__device__ __forceinline__ void fetch_unit_tail(const Consumer& c, const float* part, float* slot, int u, int hi) {
-  constexpr int RPU = 16 * NG, spu = KB * NG;
-  constexpr int MAXV = (spu * 4 + 31) / 32;                   // 16-byte vectors per lane for a whole unit
-  const int off4 = (hi - u * spu) * 4, n4 = spu * 4;          // in 16-byte vectors
-  const uint4* gsrc = reinterpret_cast<const uint4*>(part + (size_t)u * KB * RPU);
+// Copy n tagged block dots (u64 words: the fp32 value in the low half, the phase's tag in the high half) from
+// `src` into `dst` (shared memory), each once it carries `tag`: a warp loads 128 words at a time and reloads only
+// those not yet written. Bounded; returns false (error word set) on a timeout.
+__device__ __forceinline__ bool copy_tagged_dots(const unsigned long long* src, float* dst, int n, unsigned tag, int lane) {
+  const unsigned long long t0 = globaltimer();
+  for (int b0 = 0; b0 < n; b0 += 128) {
+    unsigned long long w[4];
 #pragma unroll
-  for (int j = 0; j < MAXV; ++j) {
-    const int i4 = off4 + c.lane + 32 * j;
-    if (i4 < n4) cp_async16_cg(reinterpret_cast<uint4*>(slot) + i4, gsrc + i4);
+    for (int k = 0; k < 4; ++k) {
+      const int i = b0 + 32 * k + lane;
+      w[k] = i < n ? ld_relaxed_gpu_u64(src + i) : ((unsigned long long)tag << 32);
+    }
+    while (true) {
+      bool all = true;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int i = b0 + 32 * k + lane;
+        if ((unsigned)(w[k] >> 32) != tag) {
+          all = false;
+          w[k] = ld_relaxed_gpu_u64(src + i);
+        }
+      }
+      if (__all_sync(0xffffffffu, all)) break;
+      if (wait_failed()) return false;
+      if (globaltimer() - t0 > WAIT_LIMIT_NS) {
+        if (lane == 0) atomicOr(&g_dev_error, DEVERR_GRID_TIMEOUT);
+        return false;
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int i = b0 + 32 * k + lane;
+      if (i < n) dst[i] = __uint_as_float((unsigned)w[k]);
+    }
   }
+  return true;
 }
 
-// Issue the copy of unit u's block dots of slices [hi, end of unit), published by the following CTA(s), into
-// sm.tail (cp.async through L2; the folding warp waits for it when it folds the unit).
+// The split unit of a GEMV phase that this CTA folds: its last unit u when it ends past this CTA's range and
+// starts inside it. `need` slices of it come from the following CTA(s), which publish them early in the phase.
+struct TailUnit {
+  int u, hi, need;
+  bool any;
+};
 template <int KB, int NG>
-__device__ __forceinline__ void prefetch_unit_tail(const Consumer& c, const float* part, float* tail, int u, int hi) {
+__device__ __forceinline__ TailUnit tail_unit(int N) {
+  constexpr int spu = KB * NG;
+  const SliceRange r = slice_range(N / (16 * NG) * spu);
+  const int u_lo = r.s0 / spu, u_hi = r.s1 > r.s0 ? (r.s1 - 1) / spu : u_lo - 1;
+  TailUnit t{u_hi, r.s1, (u_hi + 1) * spu - r.s1, false};
+  t.any = u_hi >= u_lo && t.need > 0 && u_hi * spu >= r.s0;
+  return t;
+}
+
+// Tail-fetcher warp, one GEMV phase (timeline phase index `phase`; n counts the phases with a split unit,
+// identically on the consumer side): copy the following CTA's share of the split unit, tagged words published
+// early in that CTA's phase, into tail[n % 2] and signal tail_full[n % 2] (one arrival per lane). It first
+// waits until the folding warp has used the buffer two phases back. Every wait is bounded; on a timeout the
+// error word is set and the fetch is skipped (the folding warp's own bounded wait then gives up).
+template <int KB, int NG>
+__device__ __forceinline__ void tail_fetch(StepSmem& sm, const StepParams& p, int N, int phase, unsigned epoch,
+                                           int& n, int lane) {
   constexpr int spu = KB * NG, RPU = 16 * NG;
-  constexpr int MAXV = (spu * 4 + 31) / 32;
-  const int off4 = (hi - u * spu) * 4, n4 = spu * 4 - off4;    // 16-byte vectors to copy
-  const uint4* gsrc = reinterpret_cast<const uint4*>(part + (size_t)u * KB * RPU) + off4;
-#pragma unroll
-  for (int j = 0; j < MAXV; ++j) {
-    const int i4 = c.lane + 32 * j;
-    if (i4 < n4) cp_async16_cg(reinterpret_cast<uint4*>(tail) + i4, gsrc + i4);
-  }
+  const TailUnit tu = tail_unit<KB, NG>(N);
+  if (!tu.any) return;
+  const int b = n & 1, use = n >> 1;
+  ++n;
+  if (use >= 1 && !__all_sync(0xffffffffu, mbar_wait(&sm.tail_empty[b], (uint32_t)((use - 1) & 1)))) return;
+  const unsigned long long* src =
+      reinterpret_cast<const unsigned long long*>(p.part) + (size_t)tu.u * KB * RPU + (tu.hi - tu.u * spu) * 16;
+  if (copy_tagged_dots(src, sm.tail[b], tu.need * 16, dots_tag(epoch, p.n_layers, phase), lane))
+    mbar_arrive(&sm.tail_full[b]);
 }
 
 // Fold of one 16-row unit (32 rows for gate|up) once this CTA's block dots of it are complete: the per-op
@@ -426,53 +497,31 @@ __device__ __forceinline__ void prefetch_unit_tail(const Consumer& c, const floa
 // from the global scratch. The block dots are read 16 at a time (independent loads), then summed in order.
 template <int KB, int EPI, int SCALE, int NG>
 __device__ __forceinline__ void fold_unit(Consumer& c, const GemvPhase<EPI, SCALE, NG>& ph, const SliceRange& r,
-                                          int u, const FoldPre& pre, bool tail_fetched = false) {
+                                          int u, const FoldPre& pre, int tail_use = -1) {
   StepSmem& sm = *c.sm;
   constexpr int RPU = 16 * NG, spu = KB * NG, slot_floats = KB * RPU, nslots = ST_BD_FLOATS / slot_floats;
   constexpr int FB = KB % 16 == 0 ? 16 : (KB % 8 == 0 ? 8 : 4);   // block dots read per batch
   static_assert(KB % FB == 0, "fold batches");
   const int lo = max(u * spu, r.s0), hi = min((u + 1) * spu, r.s1);
-  if (u * spu < r.s0) {
-    // The unit started in an earlier CTA, which folds it: publish this CTA's share (already in ph.part). Its
-    // dots were stored by several warps, each of which released them to this warp through the stage's `empty`
-    // barrier; the fence is cumulative over them, so the folding CTA sees all of them after its acquire.
-    if (c.lane == 0) {
-      fence_acq_rel_gpu();
-      red_add_relaxed(&ph.counters[u], hi - lo);
-    }
-    return;
-  }
+  if (u * spu < r.s0) return;   // started in an earlier CTA, which folds it (this CTA's dots are in `part`, tagged)
   float* slot = &sm.u.bd[(u % nslots) * slot_floats];
   if (hi < (u + 1) * spu) {
-    // The unit continues in the following CTA(s), which publish their shares early in the phase (their ranges
-    // start with it): wait for them, then copy their block dots behind this CTA's own in the slot. A slice is
-    // 16 consecutive floats of the unit's [KB][NG][16] layout, so the rest is one contiguous run.
-    const int need = (u + 1) * spu - hi;
-    bool ok = true;
-    if (tail_fetched) {   // already copied into sm.tail during the phase: move it behind this CTA's dots
-      cp_async_wait_all();
+    // The unit continues in the following CTA(s), whose share the tail-fetcher warp has copied into tail[use % 2]:
+    // a slice is 16 consecutive floats of the unit's [KB][NG][16] layout, so that share goes behind this CTA's.
+    const int off = (hi - u * spu) * 16, nf = ((u + 1) * spu - hi) * 16;
+    if (tail_use >= 0) {
+      const int b = tail_use & 1;
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(&sm.tail_full[b], (uint32_t)((tail_use >> 1) & 1)));
+      if (ok)
+        for (int i4 = c.lane; i4 < nf / 4; i4 += 32)
+          reinterpret_cast<uint4*>(slot + off)[i4] = reinterpret_cast<const uint4*>(sm.tail[b])[i4];
       __syncwarp();
-      const int off4 = (hi - u * spu) * 4, n4 = spu * 4 - off4;
-      for (int i4 = c.lane; i4 < n4; i4 += 32)
-        reinterpret_cast<uint4*>(slot)[off4 + i4] = reinterpret_cast<const uint4*>(sm.tail)[i4];
-    } else {
-      const unsigned* ctr = reinterpret_cast<const unsigned*>(ph.counters + u);
-      ok = __all_sync(0xffffffffu, ld_acquire_u32(ctr) >= (unsigned)need);
-      if (!ok) {
-        const unsigned long long t0 = globaltimer();
-        while (!(ok = __all_sync(0xffffffffu, ld_acquire_u32(ctr) >= (unsigned)need))) {
-          if (wait_failed()) break;
-          if (globaltimer() - t0 > WAIT_LIMIT_NS) {
-            if (c.lane == 0) atomicOr(&g_dev_error, DEVERR_GRID_TIMEOUT);
-            break;
-          }
-        }
-      }
-      if (ok) fetch_unit_tail<KB, NG>(c, ph.part, slot, u, hi);
-      cp_async_wait_all();
+      if (c.lane == 0) mbar_arrive(&sm.tail_empty[b]);
+    } else {   // not expected (the fetcher covers every split unit): copy the tagged words here
+      const unsigned long long* src = reinterpret_cast<const unsigned long long*>(ph.part) + (size_t)u * KB * RPU + off;
+      copy_tagged_dots(src, slot + off, nf, ph.dtag, c.lane);
     }
     __syncwarp();
-    if (c.lane == 0 && ok) ph.counters[u] = 0;
   }
   const int rr = c.lane & 15, gi = NG == 2 ? c.lane >> 4 : 0;
   const int row = gi * (ph.N / 2) + u * 16 + rr;            // gate (or only) row; up row on lanes 16-31
@@ -519,8 +568,9 @@ __device__ __forceinline__ void fold_unit(Consumer& c, const GemvPhase<EPI, SCAL
 }
 
 template <int KB, int EPI, int SCALE, int NG>      // KB = K / 128 (compile time: slice indexing divides by it)
-__device__ void gemv_phase(Consumer& c, const GemvPhase<EPI, SCALE, NG>& ph) {
+__device__ void gemv_phase(Consumer& c, GemvPhase<EPI, SCALE, NG> ph) {
   StepSmem& sm = *c.sm;
+  ph.dtag = dots_tag(c.epoch, c.p->n_layers, c.tl_phase);
   constexpr int RPU = 16 * NG;                      // rows per unit
   constexpr int spu = KB * NG;                      // slices per unit
   constexpr int slot_floats = KB * RPU;
@@ -542,21 +592,11 @@ __device__ void gemv_phase(Consumer& c, const GemvPhase<EPI, SCALE, NG>& ph) {
   int fu = u_lo + c.warp;                                       // next unit this warp folds
   auto last_stage = [&](int u) { return (min((u + 1) * spu, r.s1) - 1 - r.s0) / ST_SLICES; };
   FoldPre pre = fold_prefetch(c, ph, fu, fu <= u_hi);
-  // The last unit continues in the next CTA when it ends past this range; the CTA holding its first block
-  // folds it. The next CTA publishes its share early in the phase, so the folding warp copies it into sm.tail
-  // as soon as the counter shows it (polled once per iteration) instead of fetching it at the end.
-  const int tail_need = (u_hi + 1) * spu - r.s1;
-  int tail_state = (u_hi >= u_lo && tail_need > 0 && u_hi * spu >= r.s0 && c.warp == (u_hi - u_lo) % ST_WARPS) ? 1 : 0;
-  auto poll_tail = [&]() {   // 1: not fetched yet, 2: copy issued
-    const unsigned* ctr = reinterpret_cast<const unsigned*>(ph.counters + u_hi);
-    if (__all_sync(0xffffffffu, ld_acquire_u32(ctr) >= (unsigned)tail_need)) {
-      prefetch_unit_tail<KB, NG>(c, ph.part, sm.tail, u_hi, r.s1);
-      tail_state = 2;
-    }
-  };
+  const TailUnit tu = tail_unit<KB, NG>(ph.N);
+  const int tail_use = tu.any ? c.tail_n++ : -1;
   auto fold_next = [&]() {   // fold unit fu, move on to this warp's next unit and prefetch its row inputs
     const long long t0 = clock64();
-    fold_unit<KB>(c, ph, r, fu, pre, fu == u_hi && tail_state == 2);
+    fold_unit<KB>(c, ph, r, fu, pre, fu == u_hi ? tail_use : -1);
     fu += ST_WARPS;
     pre = fold_prefetch(c, ph, fu, fu <= u_hi);
     c.fold_cycles += clock64() - t0;
@@ -608,10 +648,17 @@ __device__ void gemv_phase(Consumer& c, const GemvPhase<EPI, SCALE, NG>& ph) {
         const int u = un[j];
         const bool in = u * spu >= r.s0;                        // this CTA folds u: keep its dots here
         if (c.t == 0) {
-          float* dst = in ? &sm.u.bd[(u % nslots) * slot_floats + kb[j] * RPU + gi * 16 + c.g]
-                          : ph.part + ((size_t)u * KB + kb[j]) * RPU + gi * 16 + c.g;
-          dst[0] = d0[j];
-          dst[8] = d1[j];
+          const int off = kb[j] * RPU + gi * 16 + c.g;
+          if (in) {
+            float* dst = &sm.u.bd[(u % nslots) * slot_floats + off];
+            dst[0] = d0[j];
+            dst[8] = d1[j];
+          } else {   // the earlier CTA folds u: publish the dots tagged (no fence or counter needed)
+            unsigned long long* dst = reinterpret_cast<unsigned long long*>(ph.part) + (size_t)u * KB * RPU + off;
+            const unsigned long long tg = (unsigned long long)ph.dtag << 32;
+            st_relaxed_gpu_u64(dst, tg | __float_as_uint(d0[j]));
+            st_relaxed_gpu_u64(dst + 8, tg | __float_as_uint(d1[j]));
+          }
         }
       }
     }
@@ -626,17 +673,17 @@ __device__ void gemv_phase(Consumer& c, const GemvPhase<EPI, SCALE, NG>& ph) {
     for (int j = 0; j < ST_SPI; ++j)
       if (j < ns) c.release_stage((n0 + i + j) % ST_NSTAGE);
     c.n = n0 + i_hi + 1;
-    if (tail_state == 1) poll_tail();
     while (fu <= u_hi && last_stage(fu) <= i_hi && c.released_test(n0 + last_stage(fu))) {
       fold_next();
     }
   }
-  if (threadIdx.x == 0) step_stamp(*c.p, c.tl_phase, 7);
+  if (c.lane == 0 && c.p->tl) step_stamp(*c.p, c.tl_phase, c.warp == 0 ? 7 : 8 + c.warp);
   // the rest of this warp's units: wait for the slowest warp to release their stages
   while (fu <= u_hi) {
     if (!c.released_wait(n0 + last_stage(fu))) atomicOr(&g_dev_error, DEVERR_MBAR_TIMEOUT);
     fold_next();
   }
+  if (threadIdx.x == 0) step_put(*c.p, c.tl_phase, 8, c.relwait_cycles);
 }
 
 // ---- consumer: activation prologue ---------------------------------------------------------------------------
@@ -908,18 +955,49 @@ __device__ void attention_phase(Consumer& c, const StepLayer& L, int l, int pos)
   }
 }
 
-// Merge of the 64-key splits (after a grid barrier): CTA c < 2 * NQ produces dims 64*(c%2) .. +63 of query
-// head c/2. The head's partials of up to 64 splits are prefetched into shared memory at once, then every output is
-// the reference's in-order sum over splits: sum_s exp(m_s - M) * o_s[d] / sum_s exp(m_s - M) * l_s.
-template <int NQ>    // query heads of this rank
-__device__ void merge_phase(Consumer& c, int pos) {
+// After its attention items, a CTA counts them on the per-KV-head counters (p.attn_counters: monotonic over the
+// layers of a launch, reset by the launch's last CTA) with a release reduction; nothing waits for it here.
+template <int NKV>
+__device__ __forceinline__ void attention_arrive(const StepParams& p, int pos) {
+  const AttnItems it = attn_items(pos, NKV);
+  if (threadIdx.x != 0 || it.i1 <= it.i0) return;   // the consumer barrier before orders the CTA's partials
+  const int g0 = it.i0 / it.n_splits, g1 = (it.i1 - 1) / it.n_splits;
+  for (int g = g0; g <= g1; ++g) {
+    const int mine = min(it.i1, (g + 1) * it.n_splits) - max(it.i0, g * it.n_splits);
+    asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p.attn_counters + g), "r"(mine) : "memory");
+  }
+}
+
+// Merge of the 64-key splits: CTA m < 4 * NQ produces dims 32*(m%4) .. +31 of query head m/4, once every split
+// of that head's KV head is counted (bounded wait on its counter instead of a grid barrier). Warp 0 takes the
+// maximum M of the split maxima and the weights w_s = exp(m_s - M) with their l-weighted sum (lane-strided over
+// the splits, then a butterfly); all warps stage the partial rows in shared memory; threads 0-31 sum
+// w_s * o_s[d] over the splits in order. The arithmetic of the attention op's merge (attn_merge_kernel), so
+// the output is bit-identical to it.
+template <int NQ>
+__device__ void merge_phase(Consumer& c, int l, int pos) {
   StepSmem& sm = *c.sm;
   const StepParams& p = *c.p;
-  if (blockIdx.x >= 2 * NQ) return;
+  if (blockIdx.x >= 4 * NQ) return;
   const int tid = threadIdx.x, lane = c.lane, warp = c.warp;
-  const int qh = blockIdx.x >> 1, d0 = (blockIdx.x & 1) * 64;
+  const int qh = blockIdx.x >> 2, d0 = (blockIdx.x & 3) * 32;
   const int n_splits = (pos + 1 + ST_CHUNK - 1) / ST_CHUNK;
-  float* cw = sm.u.mg.cw;
+  if (tid == 0) {   // every split of the KV head has been counted (this layer: l + 1 rounds of n_splits)
+    const unsigned* ctr = reinterpret_cast<const unsigned*>(p.attn_counters + qh / GQA);
+    const unsigned target = (unsigned)((l + 1) * n_splits);
+    if (ld_acquire_u32(ctr) < target) {
+      const unsigned long long t0 = globaltimer();
+      while (ld_acquire_u32(ctr) < target) {
+        if (wait_failed()) break;
+        if (globaltimer() - t0 > WAIT_LIMIT_NS) {
+          atomicOr(&g_dev_error, DEVERR_GRID_TIMEOUT);
+          break;
+        }
+      }
+    }
+  }
+  consumer_sync();
+  float* cw = sm.u.mg.w;
   if (warp == 0) {
     const float* ml = p.ml_part + (size_t)qh * p.max_splits * 2;
     float mloc = -INFINITY;
@@ -927,29 +1005,28 @@ __device__ void merge_phase(Consumer& c, int pos) {
     const float M = warp_max(mloc);
     float lsum = 0.f;
     for (int s = lane; s < n_splits; s += 32) {
-      const float wgt = expf(__ldcg(ml + 2 * s) - M);
-      cw[s] = wgt;
-      lsum += wgt * __ldcg(ml + 2 * s + 1);
+      const float wt = expf(__ldcg(ml + 2 * s) - M);
+      cw[s] = wt;
+      lsum += wt * __ldcg(ml + 2 * s + 1);
     }
     lsum = warp_sum(lsum);
     if (lane == 0) sm.u.mg.cl = lsum;
   }
   float o = 0.f;
   const float* op = p.o_part + (size_t)qh * p.max_splits * HEAD_DIM + d0;
-  for (int s0 = 0; s0 < n_splits; s0 += ST_MERGE_SPLITS) {
-    const int ns = min(ST_MERGE_SPLITS, n_splits - s0);
-    // rows s0..s0+ns-1, 64 floats each = 16 float4; 256 threads load ns*16 float4
-    for (int i = tid; i < ns * 16; i += ST_WARPS * 32) {
-      const int s = i >> 4, f = i & 15;
-      reinterpret_cast<uint4*>(sm.u.mg.o)[i] = ldcg_u4(op + (size_t)(s0 + s) * HEAD_DIM + f * 4);
+  for (int s0 = 0; s0 < n_splits; s0 += ST_MERGE_ROUND) {
+    const int ns = min(ST_MERGE_ROUND, n_splits - s0);
+    for (int i = tid; i < ns * 8; i += ST_WARPS * 32) {   // 8 x 16 bytes per split row of 32 dims
+      const int sr = i >> 3, f = i & 7;
+      reinterpret_cast<uint4*>(sm.u.mg.o)[i] = ldcg_u4(op + (size_t)(s0 + sr) * HEAD_DIM + f * 4);
     }
     consumer_sync();
-    if (tid < 64) {
-      for (int s = 0; s < ns; ++s) o += cw[s0 + s] * sm.u.mg.o[s * 64 + tid];
+    if (tid < 32) {
+      for (int sr = 0; sr < ns; ++sr) o += cw[s0 + sr] * sm.u.mg.o[sr * 32 + tid];
     }
     consumer_sync();
   }
-  if (tid < 64) p.attn[qh * HEAD_DIM + d0 + tid] = __float2bfloat16_rn(o / sm.u.mg.cl);
+  if (tid < 32) p.attn[qh * HEAD_DIM + d0 + tid] = __float2bfloat16_rn(o / sm.u.mg.cl);
 }
 
 // ---- tensor-parallel exchange -------------------------------------------------------------------------------------
@@ -1008,6 +1085,10 @@ __global__ void __launch_bounds__(ST_THREADS, 1) decode_step_kernel(const __grid
       mbar_init(&sm.full[s], 1);
       mbar_init(&sm.empty[s], ST_WARPS);
     }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sm.tail_full[b], 32);   // the fetcher's 32 lanes, each after its words are in shared memory
+      mbar_init(&sm.tail_empty[b], 1);
+    }
     fence_mbar_init();
   }
   __syncthreads();
@@ -1041,12 +1122,23 @@ __global__ void __launch_bounds__(ST_THREADS, 1) decode_step_kernel(const __grid
       step_stamp(p, 5 * p.n_layers, 3);
       step_put(p, 5 * p.n_layers, 6, pr.wait_cycles);
       pr.gemv(p.w_head, (p.vocab / 16) * (H / QB));
+    } else if (warp == ST_WARPS + 1) {   // tail fetcher: the split units' remote block dots, phase by phase
+      const unsigned epoch = __ldcg(p.sync + 2);
+      int n = 0;
+      for (int l = 0; l < p.n_layers; ++l) {
+        tail_fetch<H / QB, 1>(sm, p, QKV_N, 5 * l + 0, epoch, n, lane);
+        tail_fetch<KO / QB, 1>(sm, p, H, 5 * l + 2, epoch, n, lane);
+        tail_fetch<H / QB, 2>(sm, p, 2 * I, 5 * l + 3, epoch, n, lane);
+        tail_fetch<I / QB, 1>(sm, p, H, 5 * l + 4, epoch, n, lane);
+      }
+      tail_fetch<H / QB, 1>(sm, p, p.vocab, 5 * p.n_layers, epoch, n, lane);
     }
     return;
   }
   // ---------------- consumers ----------------
   asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(ST_CONSUMER_REGS) : "memory");
   Consumer c{&sm, &p, 0, lane, warp, lane >> 2, lane & 3, -INFINITY, 0x7FFFFFFF, 0, 0};
+  c.epoch = __ldcg(p.sync + 2);
   unsigned nbar = 0;
   const int tok = p.token[0];
   const bool tok_ok = tok >= 0 && tok < p.vocab * TP;
@@ -1073,9 +1165,9 @@ __global__ void __launch_bounds__(ST_THREADS, 1) decode_step_kernel(const __grid
     if (tl) step_stamp(p, ph + 1, 0);
     attention_phase<NKV>(c, L, l, pos);
     if (tl) step_stamp(p, ph + 1, 7);
-    grid_barrier(p.sync, nbar++);
+    attention_arrive<NKV>(p, pos);
+    merge_phase<NQ>(c, l, pos);
     if (tl) step_stamp(p, ph + 1, 1);
-    merge_phase<NQ>(c, pos);
     if (tl) { step_put(p, ph + 1, 4, c.wait_cycles); step_put(p, ph + 1, 5, c.fold_cycles); }
     grid_barrier(p.sync, nbar++, step_word(p, ph + 1, 2));
     // O: resid += W_o . quant(attn)   (TP: this rank's fp32 partial, exchanged)
@@ -1168,6 +1260,8 @@ __global__ void __launch_bounds__(ST_THREADS, 1) decode_step_kernel(const __grid
         p.state[0] = pos + 1;
         p.state[1] = step + 1;
         *p.best = 0ull;
+        for (int g = 0; g < NKV; ++g) p.attn_counters[g] = 0;
+        p.sync[2] = c.epoch + 1;   // the next launch's block-dot tags
         p.sync[0] = 0;
         p.sync[1] = 0;
         __threadfence();

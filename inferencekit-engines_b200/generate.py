@@ -62,7 +62,7 @@ class Engine:
         self.lm_head_ctas = lm_head_ctas
         self.graph = None
         self.fused = fused
-        self.step_timeline = None     # fused step only: int64 [#SMs, 5*layers+1, 4] %globaltimer stamps
+        self.step_timeline = None     # fused step only: int64 [#SMs, 5*layers+1, 16] stamps (include/qwen3_b200.h)
         if fused:
             if not isinstance(m.lm_head, Linear) or attn_chunk != 64 or m.batch != 1:
                 raise ValueError("the fused step needs an FP8 lm_head, 64-key attention splits and batch 1")
@@ -74,9 +74,10 @@ class Engine:
                              L.q_norm.data_ptr(), L.k_norm.data_ptr()])
             self.layer_table = torch.tensor(ptrs, dtype=torch.int64, device=dev)
             lib = self.k.lib
-            self.part = torch.empty(lib.qk_decode_step_part_floats(cfg.vocab), dtype=torch.float32, device=dev)
+            # the shared block dots carry (launch, phase) tags: part starts zeroed, sync[2] counts the launches
+            self.part = torch.zeros(lib.qk_decode_step_part_floats(cfg.vocab), dtype=torch.float32, device=dev)
             self.gemv_counters = torch.zeros(lib.qk_decode_step_counters(cfg.vocab), dtype=torch.int32, device=dev)
-            self.sync = torch.zeros(2, dtype=torch.int32, device=dev)
+            self.sync = torch.zeros(4, dtype=torch.int32, device=dev)
             self.scale_mode = 1 if m.scale_mode == "channel" else 0
 
     def settings(self) -> dict:
@@ -177,7 +178,7 @@ class Engine:
         the fused step's grid-barrier, GEMV-unit and attention counters and the argmax key, or the op path's
         counters. Call it between steps, with no launch in flight; clears the device error word."""
         torch.cuda.synchronize()
-        for t in (self.counters, self.best) + ((self.sync, self.gemv_counters) if self.fused else ()):
+        for t in (self.counters, self.best) + ((self.sync, self.gemv_counters, self.part) if self.fused else ()):
             t.zero_()
         if not self.fused:
             for _, cnt in self.k._scratch.values():

@@ -312,9 +312,9 @@ class FusedTPEngine:
         self.ml_part = torch.zeros(cfg.n_heads, self.max_splits, 2, dtype=torch.float32, device=dev)
         self.counters = torch.zeros(cfg.n_kv_heads, dtype=torch.int32, device=dev)
         lib = k.lib
-        self.scratch = torch.empty(lib.qk_decode_step_part_floats(cfg.vocab), dtype=torch.float32, device=dev)
+        self.scratch = torch.zeros(lib.qk_decode_step_part_floats(cfg.vocab), dtype=torch.float32, device=dev)
         self.gemv_counters = torch.zeros(lib.qk_decode_step_counters(cfg.vocab), dtype=torch.int32, device=dev)
-        self.sync = torch.zeros(2, dtype=torch.int32, device=dev)
+        self.sync = torch.zeros(4, dtype=torch.int32, device=dev)
         self.layer_table = torch.tensor([[L.qkv.packed.data_ptr(), L.o.packed.data_ptr(), L.gu.packed.data_ptr(),
                                           L.down.packed.data_ptr(), L.qkv.scale.data_ptr(), L.o.scale.data_ptr(),
                                           L.gu.scale.data_ptr(), L.down.scale.data_ptr(), L.ln1.data_ptr(),
@@ -384,7 +384,7 @@ class FusedTPEngine:
         torch.cuda.synchronize()
         self.dist.barrier(group=self.group)
         self.k.tp_area_reset(self.area)
-        for t in (self.gemv_counters, self.counters, self.sync, self.best):
+        for t in (self.gemv_counters, self.counters, self.sync, self.best, self.scratch):
             t.zero_()
         torch.cuda.synchronize()
         self.k.device_error()

@@ -71,9 +71,9 @@ def test_ops_refuses_to_run_without_cuda():
 
 def test_fused_step_scratch_sizes(lib):
     """The fused step's boundary-unit scratch covers the largest GEMV of a layer even for a small vocabulary."""
-    assert lib.qk_decode_step_part_floats(4096) == 24576 * 4096 // 128
+    assert lib.qk_decode_step_part_floats(4096) == 2 * 24576 * 4096 // 128   # u64 tagged words
     assert lib.qk_decode_step_counters(4096) == 768
-    assert lib.qk_decode_step_part_floats(151936) == 151936 * 32
+    assert lib.qk_decode_step_part_floats(151936) == 2 * 151936 * 32
     assert lib.qk_decode_step_counters(151936) == 151936 // 16
 
 
@@ -85,7 +85,7 @@ def test_tp_entry_points_check_arguments_without_a_gpu(lib):
         _fields_ = [("tp", ctypes.c_int), ("rank", ctypes.c_int), ("areas", ctypes.c_void_p)]
 
     args = [p, 1, p, p, ctypes.c_longlong(8 * 4096 * 256), p, p, p, p, 151936, p, p, p, p, p, 4096, p, p, p, p, p,
-            p, p, ctypes.c_longlong(151936 * 32), p, 151936 // 16, p, p, p, p, 4096, 128, ctypes.c_float(1e-6),
+            p, p, ctypes.c_longlong(2 * 151936 * 32), p, 151936 // 16, p, p, p, p, 4096, 128, ctypes.c_float(1e-6),
             None, p]
     for tp, rank, off, msg in ((3, 0, 0, b"tp must be"), (2, 2, 0, b"bad rank"), (2, 0, 8, b"vocab_offset")):
         comm = Comm(tp, rank, 16)
