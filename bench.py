@@ -501,13 +501,14 @@ PHASES = ("qkv", "attn", "o_proj", "gate_up", "down")
 
 
 def timeline_summary(tl, n_layers: int, clock_ghz: float = 1.965) -> dict:
-    """Per-phase breakdown of one fused-step launch from its timeline (int64 [CTAs, 5*layers+1, 16], words as in
+    """Per-phase breakdown of one fused-step launch from its timeline (int64 [CTAs, 5*layers+1, 24], words as in
     csrc/step.cuh: 0 consumers start the phase, 1 prologue done (attention: arrival counted and, on the CTA
     that completed a KV head, its merge done), 2 the whole CTA done (stamped inside the grid barrier), 3
     producer's first load of the phase, 4-6 cumulative clock64 cycles (consumer warp 0 waiting for ring
     stages, folding units; producer waiting for free slots), 7 consumer warp 0 leaves the stage loop
     (attention: partials done), 8 cumulative cycles warp 0 waited for the slowest warp to release a stage it
-    folds, 9-15 warps 1-7 leave the stage loop). Times in us: medians over CTAs, then over layers 1..n-1 (layer 0 includes the
+    folds, 9-15 warps 1-7 leave the stage loop, 16-18 warp 0's cycles computing slice pairs, taking and
+    counting them, and the pairs it took). Times in us: medians over CTAs, then over layers 1..n-1 (layer 0 includes the
     launch ramp). `barrier` is the time from a CTA's end of the phase to its start of the next one; `tail` from
     warp 0 leaving the stage loop to the whole CTA being done; `ring_wait` the consumer's stage waits inside
     the phase; `producer_wait` the producer's waits for free slots while issuing the phase. For every grid
@@ -521,7 +522,7 @@ def timeline_summary(tl, n_layers: int, clock_ghz: float = 1.965) -> dict:
     pw = np.diff(np.concatenate([t[:, :, 6], t[:, -1:, 6]], axis=1), axis=1)                 # phase -> next phase
     names = {0: "qkv", 2: "o_proj", 3: "gate_up", 4: "down"}
     per = {k: [] for k in ("qkv", "attn", "o_proj", "gate_up", "down")}
-    layer_us, bar_stats = [], []
+    layer_us, bar_stats, lags = [], [], {}
     for l in (range(1, n_layers) if n_layers > 1 else range(n_layers)):
         b = 5 * l
         for j, name in names.items():
@@ -535,7 +536,10 @@ def timeline_summary(tl, n_layers: int, clock_ghz: float = 1.965) -> dict:
                                   last_warp_to_done=us(ph[:, 2] - exits.max(1)),
                                   fold=cyc(np.diff(np.concatenate([np.zeros((G, 1), np.int64), t[:, :, 5]], axis=1),
                                                    axis=1)[:, b + j]),
-                                  slowest_warp_wait=cyc(rw[:, b + j])))
+                                  slowest_warp_wait=cyc(rw[:, b + j]),
+                                  warp0_compute=cyc(ph[:, 16]), warp0_take_and_count=cyc(ph[:, 17]),
+                                  warp0_pairs=ph[:, 18].astype(np.float64)))
+            lags.setdefault(name, []).append(us(exits - exits.min(1, keepdims=True)))
         a = t[:, b + 1]
         merged = us(a[:, 1] - a[:, 7])
         per["attn"].append(dict(partials=us(a[:, 7] - a[:, 0]), arrive=merged,
@@ -552,6 +556,9 @@ def timeline_summary(tl, n_layers: int, clock_ghz: float = 1.965) -> dict:
                        for i, n in enumerate(["qkv->attn", "attn->o", "o->gu", "gu->down", "down->qkv"])}
     for k, v in per.items():
         out[k] = {f: round(float(np.median([np.median(d[f]) for d in v])), 3) for f in v[0]}
+    # per consumer warp: how long after the CTA's first warp it left the stage loop (median over CTAs, layers)
+    out["warp_exit_lag_us"] = {k: [round(float(np.median(np.stack(v)[:, :, w])), 3) for w in range(8)]
+                               for k, v in lags.items()}
     h = t[:, 5 * n_layers]
     out["head"] = {"prologue": float(np.median(us(h[:, 1] - h[:, 0]))),
                    "stage_loop": float(np.median(us(h[:, 7] - h[:, 1]))),
@@ -576,7 +583,7 @@ def run_timeline(args):
     eng = Engine(m, fused=True)
     n = len(m.layers)
     sms = torch.cuda.get_device_properties(0).multi_processor_count
-    eng.step_timeline = torch.zeros(sms, 5 * n + 1, 16, dtype=torch.int64, device="cuda")
+    eng.step_timeline = torch.zeros(sms, 5 * n + 1, 24, dtype=torch.int64, device="cuda")
     eng.token.fill_(1)
     eng.state.copy_(torch.tensor([start, 0], dtype=torch.int32))
     for _ in range(args.launches):

@@ -161,13 +161,14 @@ typedef struct {
  *   sync        unsigned [4] zeroed once before the first launch: [0], [1] barrier counters (left zero), [2] the
  *               launches completed (tags of the shared block dots; zero it only together with `part`)
  *   max_splits  >= ceil(max_seq/64), <= 1024
- *   timeline    NULL, or a device buffer of (#SMs) x (5*n_layers + 1) x 16 u64: per CTA and phase (layer l:
+ *   timeline    NULL, or a device buffer of (#SMs) x (5*n_layers + 1) x 24 u64: per CTA and phase (layer l:
  *               qkv, attn, o, gu, down = 5l+0..4; lm_head = 5*n_layers) the %globaltimer of 0 consumers start,
  *               1 prologue done (attention: arrivals counted and, on merging CTAs, the merge done), 2 the whole
  *               CTA done (inside the grid barrier), 3 producer issues the phase's first load, 7 consumer warp 0
  *               leaves the stage loop (attention: partials done), 9-15 consumer warps 1-7 leave it; cumulative
  *               clock64 cycles: 4 consumer warp 0 waiting for data, 5 consumer warp 0 folding units, 6 producer
- *               waiting for free ring stages, 8 consumer warp 0 waiting for the slowest warp to release a stage.
+ *               waiting for free ring stages, 8 consumer warp 0 waiting for other warps' slices of a unit it
+ *               folds, 16 consumer warp 0 computing slice pairs, 17 taking and counting them; 18 pairs it took.
  */
 int qk_decode_step(const qk_layer_t* layers, int n_layers, void* k_cache, void* v_cache, long long kv_layer_stride,
                    const void* embed, const void* final_norm, const void* w_head, const float* s_head, int vocab,

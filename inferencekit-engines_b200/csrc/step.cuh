@@ -43,7 +43,10 @@ static_assert(4 * 32 * ST_PRODUCER_REGS + ST_WARPS * 32 * ST_CONSUMER_REGS <= ST
 constexpr int ST_STAGE = 32768;
 constexpr int ST_SLICE = 2048;                     // 16 rows x 128 k of fp8
 constexpr int ST_SLICES = ST_STAGE / ST_SLICE;     // 16 slices per stage
-constexpr int ST_SPW = ST_SLICES / ST_WARPS;       // 2 slices per consumer warp per stage
+constexpr int ST_SPW = ST_SLICES / ST_WARPS;       // 2 slices per consumer warp per stage (attention: stage share)
+#ifndef ST_QUAD
+#define ST_QUAD 4                                  // GEMV slices a consumer warp takes at a time
+#endif
 constexpr int ST_NSTAGE = 5;
 constexpr int ST_MAX_K = 12288;
 constexpr int ST_CHUNK = 64;                       // attention keys per item
@@ -54,9 +57,6 @@ constexpr int ST_BD_FLOATS = 6144;
 constexpr int ST_MERGE_ROUND = 128;                // splits staged per round of the attention merge
 constexpr int ST_TAIL_FLOATS = 96 * 16;            // StepSmem::tail: the remote block dots of a split unit
 constexpr int ST_ABATCH = 4;                       // attention items processed together (<= ST_NSTAGE)
-#ifndef ST_SPI
-#define ST_SPI 1                                   // GEMV stages a consumer warp takes per iteration
-#endif
 
 struct StepLayer {
   const uint8_t *w_qkv, *w_o, *w_gu, *w_down;      // model.pack_fp8 layout
@@ -124,8 +124,9 @@ struct StepParams {
 // 5 consumer warp 0 folding units, 6 producer waiting for free stages (cumulative at the phase's first load).
 // Word 7: warp 0 leaves a GEMV phase's stage loop (before its last folds); the attention partials are done.
 // Word 8: cumulative clock64 cycles consumer warp 0 spent waiting for the slowest warp to release a stage it
-// must fold. Words 9-15: GEMV phases: consumer warps 1-7 leave the stage loop (%globaltimer).
-constexpr int ST_TL_WORDS = 16;
+// must fold. Words 9-15: GEMV phases: consumer warps 1-7 leave the stage loop (%globaltimer). Words 16-18 (GEMV
+// phases, consumer warp 0): cycles computing its slice pairs, cycles taking pairs and counting them, pairs taken.
+constexpr int ST_TL_WORDS = 24;
 __device__ __forceinline__ void step_put(const StepParams& p, int phase, int i, unsigned long long v) {
   if (p.tl) p.tl[((size_t)blockIdx.x * (5 * p.n_layers + 1) + phase) * ST_TL_WORDS + i] = v;
 }
@@ -155,11 +156,13 @@ struct StepSmem {
     } mg;
   } u;
   // Block dots of the last unit of a GEMV phase when it continues in the next CTA: the tail-fetcher warp copies
-  // them (tagged words in `part`) into tail[n % 2] as soon as that CTA has published them (a unit has KB * NG <= 96 slices of
-  // 16 dots; at most all but one come from the next CTA). tail_full[b]: the copy landed (32 lane arrivals);
-  // tail_empty[b]: the folding warp has used it.
+  // them (tagged words in `part`) into tail[n % 2] as soon as that CTA has published them (a unit has KB * NG
+  // <= 96 slices of 16 dots; at most all but one come from the next CTA). tail_full[b]: the copy landed (the
+  // fetcher's 32 lanes arrive); tail_empty[b]: the folding warp has used it.
   __align__(16) float tail[2][ST_TAIL_FLOATS];
   uint64_t tail_full[2], tail_empty[2];
+  int grab;                                        // GEMV phase: slice pairs handed out so far
+  int done[16];                                    // GEMV phase: finished slices per block-dot slot
   float red[8];
   unsigned long long bestbuf[ST_WARPS];
   uint64_t full[ST_NSTAGE], empty[ST_NSTAGE];
@@ -227,6 +230,9 @@ __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
 }
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_n(uint64_t* bar, uint32_t n) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(n) : "memory");
 }
 __device__ __forceinline__ bf16 ldcg_bf16(const bf16* p) {
   unsigned short v;
@@ -373,15 +379,6 @@ struct Consumer {
     const bool ok = __all_sync(0xffffffffu, mbar_wait(&sm->full[m % ST_NSTAGE], (uint32_t)((m / ST_NSTAGE) & 1)));
     wait_cycles += clock64() - t0;
     return ok;
-  }
-  // Have all consumer warps released stage number `m`? Its `empty` barrier completes phase m / ST_NSTAGE when
-  // the last warp arrives (release); the test acquires, so every warp's writes before its arrive are visible.
-  // Unambiguous only while this warp has not released stage m + ST_NSTAGE (the slot's next phase).
-  // (warp-uniform results: lane 0's test decides; a lane that saw "not yet" waits, which then returns at once)
-  __device__ __forceinline__ bool released_test(int m) {
-    const bool t = mbar_test_wait(&sm->empty[m % ST_NSTAGE], (uint32_t)((m / ST_NSTAGE) & 1));
-    if (!__shfl_sync(0xffffffffu, (int)t, 0)) return false;
-    return released_wait(m);
   }
   __device__ __forceinline__ bool released_wait(int m) {
     const long long t0 = clock64();
@@ -575,52 +572,62 @@ __device__ void gemv_phase(Consumer& c, GemvPhase<EPI, SCALE, NG> ph) {
   constexpr int spu = KB * NG;                      // slices per unit
   constexpr int slot_floats = KB * RPU;
   constexpr int nslots = ST_BD_FLOATS / slot_floats;
-  // A unit's slot is reused by unit u + nslots, whose first slice lies nslots * spu - spu slices past u's last.
-  // u is folded at the latest when its owner reaches stage (u's last) + ST_NSTAGE, and no warp runs more than
-  // ST_NSTAGE stages ahead of the slowest, so writers stay within (2 * ST_NSTAGE + 2) stages of u's last slice.
+  // A unit's slot is next used by unit u + nslots, whose first slice lies (nslots - 1) * spu slices past u's last.
+  // No warp works more than ST_NSTAGE stages past the oldest stage not yet released, and u's owner folds it at
+  // the latest after its next slice pair once u is complete, so no writer of u + nslots can come first.
   static_assert((nslots - 1) * spu > (2 * ST_NSTAGE + 2) * ST_SLICES, "too few block-dot slots");
+  constexpr int NQ = ST_SLICES / ST_QUAD;         // grabs per stage
+  static_assert(ST_SLICES % ST_QUAD == 0 && ST_WARPS % NQ == 0, "a stage's grabs must add up to its ST_WARPS arrivals");
   const int units = ph.N / RPU;
   const SliceRange r = slice_range(units * spu);
   const int nst = (r.s1 - r.s0 + ST_SLICES - 1) / ST_SLICES;   // stages of this phase (as the producer issues)
   const int n0 = c.n;
   const uint8_t* xh = reinterpret_cast<const uint8_t*>(sm.xh);
-  // Warps run through the stages without waiting for each other, ST_SPI stages per iteration (ST_SPW slices of each,
-  // all shared-memory loads issued before the MMAs). A unit is complete for this CTA once every warp has
-  // released the stage holding its last slice, which the ring's `empty` barrier already records; unit u is
-  // folded by warp (u - u_lo) % ST_WARPS as soon as that warp sees its stage released.
+  // Work is handed out in groups of ST_QUAD consecutive slices: grab p is slices ST_QUAD * (p % NQ) .. +ST_QUAD-1
+  // of stage p / NQ, taken by whichever warp asks next (sm.grab), so a warp that is delayed (a fold, a slow wait)
+  // leaves its share to the others; each grab counts ST_WARPS / NQ arrivals on the stage's `empty` barrier. A
+  // finished slice adds 1 to its unit's counter (sm.done, per slot); unit u is folded by warp
+  // (u - u_lo) % ST_WARPS once all its slices in this CTA are done.
   const int u_lo = r.s0 / spu, u_hi = r.s1 > r.s0 ? (r.s1 - 1) / spu : u_lo - 1;
   int fu = u_lo + c.warp;                                       // next unit this warp folds
-  auto last_stage = [&](int u) { return (min((u + 1) * spu, r.s1) - 1 - r.s0) / ST_SLICES; };
+  // slices of unit u that this CTA computes and folds (none for a unit an earlier CTA started, which folds it)
+  auto local_count = [&](int u) { return u * spu < r.s0 ? 0 : min((u + 1) * spu, r.s1) - u * spu; };
   FoldPre pre = fold_prefetch(c, ph, fu, fu <= u_hi);
   const TailUnit tu = tail_unit<KB, NG>(ph.N);
   const int tail_use = tu.any ? c.tail_n++ : -1;
+  auto fold_ready = [&](int u) { return *reinterpret_cast<volatile int*>(&sm.done[u % nslots]) >= local_count(u); };
   auto fold_next = [&]() {   // fold unit fu, move on to this warp's next unit and prefetch its row inputs
     const long long t0 = clock64();
+    __threadfence_block();   // the other warps' block dots, published before their counts
     fold_unit<KB>(c, ph, r, fu, pre, fu == u_hi ? tail_use : -1);
+    __syncwarp();
+    if (c.lane == 0) sm.done[fu % nslots] = 0;
     fu += ST_WARPS;
     pre = fold_prefetch(c, ph, fu, fu <= u_hi);
     c.fold_cycles += clock64() - t0;
   };
-  for (int i = 0; i < nst; i += ST_SPI) {
-    const int ns = min(ST_SPI, nst - i);                        // stages in this iteration
-    bool ok = true;
+  long long cyc_compute = 0, cyc_sync = 0;
+  int pairs = 0;
+  while (true) {
+    const long long tg0 = clock64();
+    int pidx = 0;
+    if (c.lane == 0) pidx = atomicAdd(&sm.grab, 1);
+    pidx = __shfl_sync(0xffffffffu, pidx, 0);
+    if (pidx >= NQ * nst) break;
+    const int i = pidx / NQ, k0 = (pidx - i * NQ) * ST_QUAD;
+    const long long tg1 = clock64();
+    if (!c.wait_abs(n0 + i)) atomicOr(&g_dev_error, DEVERR_MBAR_TIMEOUT);
+    const long long tc0 = clock64();
+    // slice coordinates (also computed for slices past the range: kb stays in [0, KB), nothing is stored)
+    int q[ST_QUAD], tl[ST_QUAD], un[ST_QUAD], kb[ST_QUAD];
+    uint4 W[ST_QUAD][4], X[ST_QUAD][4];
 #pragma unroll
-    for (int j = 0; j < ST_SPI; ++j)
-      if (j < ns) ok = c.wait_abs(n0 + i + j) && ok;
-    if (!ok) atomicOr(&g_dev_error, DEVERR_MBAR_TIMEOUT);
-    // slice coordinates (also computed for slices past the range: kb stays in [0, KB), nothing is stored);
-    // slice j of the iteration is slice (j % ST_SPW) * ST_WARPS + warp of stage i + j / ST_SPW
-    constexpr int NSL = ST_SPI * ST_SPW;
-    int q[NSL], tl[NSL], un[NSL], kb[NSL];
-    uint4 W[NSL][4], X[NSL][4];
-#pragma unroll
-    for (int j = 0; j < NSL; ++j) {
-      const int st = j / ST_SPW, k = j % ST_SPW;
-      q[j] = r.s0 + (i + st) * ST_SLICES + k * ST_WARPS + c.warp;
+    for (int j = 0; j < ST_QUAD; ++j) {
+      q[j] = r.s0 + i * ST_SLICES + k0 + j;
       tl[j] = q[j] / NG;
       un[j] = tl[j] / KB;
       kb[j] = tl[j] - un[j] * KB;
-      const uint8_t* w = sm.ring[(n0 + i + st) % ST_NSTAGE] + (k * ST_WARPS + c.warp) * ST_SLICE + c.lane * 16;
+      const uint8_t* w = sm.ring[(n0 + i) % ST_NSTAGE] + (k0 + j) * ST_SLICE + c.lane * 16;
       const uint8_t* x = xh + kb[j] * 256 + c.t * 16;
 #pragma unroll
       for (int ch = 0; ch < 4; ++ch) {
@@ -628,13 +635,13 @@ __device__ void gemv_phase(Consumer& c, GemvPhase<EPI, SCALE, NG> ph) {
         X[j][ch] = *reinterpret_cast<const uint4*>(x + ch * 64);
       }
     }
-    float d0[NSL], d1[NSL];
+    float d0[ST_QUAD], d1[ST_QUAD];
 #pragma unroll
-    for (int j = 0; j < NSL; ++j) d0[j] = d1[j] = 0.f;
+    for (int j = 0; j < ST_QUAD; ++j) d0[j] = d1[j] = 0.f;
 #pragma unroll
     for (int ch = 0; ch < 4; ++ch) {
 #pragma unroll
-      for (int j = 0; j < NSL; ++j) {
+      for (int j = 0; j < ST_QUAD; ++j) {
         float e[4];
         fp8_chunk_dot(W[j][ch], X[j][ch], e);
         d0[j] += e[0];
@@ -642,8 +649,8 @@ __device__ void gemv_phase(Consumer& c, GemvPhase<EPI, SCALE, NG> ph) {
       }
     }
 #pragma unroll
-    for (int j = 0; j < NSL; ++j) {
-      if (j / ST_SPW < ns && q[j] < r.s1) {
+    for (int j = 0; j < ST_QUAD; ++j) {
+      if (q[j] < r.s1) {
         const int gi = q[j] - tl[j] * NG;                       // sub-matrix of the slice (0 for NG == 1)
         const int u = un[j];
         const bool in = u * spu >= r.s0;                        // this CTA folds u: keep its dots here
@@ -662,28 +669,56 @@ __device__ void gemv_phase(Consumer& c, GemvPhase<EPI, SCALE, NG> ph) {
         }
       }
     }
-    // A unit whose last stage is ST_NSTAGE or more behind the newest stage this warp now holds must be folded
-    // before this warp releases that stage (afterwards the slot's barrier could complete its next phase).
-    const int i_hi = i + ns - 1;
-    while (fu <= u_hi && last_stage(fu) + ST_NSTAGE <= i_hi) {
-      if (!c.released_wait(n0 + last_stage(fu))) atomicOr(&g_dev_error, DEVERR_MBAR_TIMEOUT);
-      fold_next();
-    }
+    const long long tc1 = clock64();
+    __syncwarp();
+    if (c.lane == 0) {
+      __threadfence_block();   // this pair's block dots before its counts
+      // the group's slices by unit (consecutive slices: at most two units), one count per unit
+      int cu = -1, cn = 0;
 #pragma unroll
-    for (int j = 0; j < ST_SPI; ++j)
-      if (j < ns) c.release_stage((n0 + i + j) % ST_NSTAGE);
-    c.n = n0 + i_hi + 1;
-    while (fu <= u_hi && last_stage(fu) <= i_hi && c.released_test(n0 + last_stage(fu))) {
-      fold_next();
+      for (int j = 0; j < ST_QUAD; ++j) {
+        if (q[j] < r.s1 && un[j] * spu >= r.s0) {
+          if (un[j] != cu) {
+            if (cn) atomicAdd(&sm.done[cu % nslots], cn);
+            cu = un[j];
+            cn = 0;
+          }
+          ++cn;
+        }
+      }
+      if (cn) atomicAdd(&sm.done[cu % nslots], cn);
+      mbar_arrive_n(&sm.empty[(n0 + i) % ST_NSTAGE], ST_WARPS / NQ);
     }
+    __syncwarp();
+    cyc_compute += tc1 - tc0;
+    cyc_sync += (tg1 - tg0) + (clock64() - tc1);
+    ++pairs;
+    while (fu <= u_hi && fold_ready(fu)) fold_next();
   }
   if (c.lane == 0 && c.p->tl) step_stamp(*c.p, c.tl_phase, c.warp == 0 ? 7 : 8 + c.warp);
-  // the rest of this warp's units: wait for the slowest warp to release their stages
+  // the rest of this warp's units: wait (bounded) until the other warps have finished their slices
   while (fu <= u_hi) {
-    if (!c.released_wait(n0 + last_stage(fu))) atomicOr(&g_dev_error, DEVERR_MBAR_TIMEOUT);
+    if (!fold_ready(fu)) {
+      const long long t0 = clock64();
+      const unsigned long long g0 = globaltimer();
+      while (!fold_ready(fu)) {
+        if (wait_failed()) break;
+        if (globaltimer() - g0 > WAIT_LIMIT_NS) {
+          if (c.lane == 0) atomicOr(&g_dev_error, DEVERR_MBAR_TIMEOUT);
+          break;
+        }
+      }
+      c.relwait_cycles += clock64() - t0;
+    }
     fold_next();
   }
-  if (threadIdx.x == 0) step_put(*c.p, c.tl_phase, 8, c.relwait_cycles);
+  c.n = n0 + nst;
+  if (threadIdx.x == 0) {
+    step_put(*c.p, c.tl_phase, 8, c.relwait_cycles);
+    step_put(*c.p, c.tl_phase, 16, cyc_compute);
+    step_put(*c.p, c.tl_phase, 17, cyc_sync);
+    step_put(*c.p, c.tl_phase, 18, pairs);
+  }
 }
 
 // ---- consumer: activation prologue ---------------------------------------------------------------------------
@@ -695,6 +730,7 @@ __device__ void step_prologue(Consumer& c, const bf16* x, const bf16* norm_w, in
   StepSmem& sm = *c.sm;
   const int tid = threadIdx.x;
   const int KB = K / QB;
+  if (tid == 0) sm.grab = 0;   // every warp left the previous GEMV phase (a grid barrier lies between)
   constexpr int MAXG = ST_MAX_K / QB / ST_WARPS;   // 128-groups per warp at most (12)
   // Issue every global load of the prologue at once (one L2 round trip instead of one per group).
   uint2 raw[MAXG], nraw[NORM ? MAXG : 1];
@@ -1085,6 +1121,8 @@ __global__ void __launch_bounds__(ST_THREADS, 1) decode_step_kernel(const __grid
       mbar_init(&sm.full[s], 1);
       mbar_init(&sm.empty[s], ST_WARPS);
     }
+    sm.grab = 0;
+    for (int i = 0; i < 16; ++i) sm.done[i] = 0;
     for (int b = 0; b < 2; ++b) {
       mbar_init(&sm.tail_full[b], 32);   // the fetcher's 32 lanes, each after its words are in shared memory
       mbar_init(&sm.tail_empty[b], 1);

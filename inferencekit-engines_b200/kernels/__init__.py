@@ -216,7 +216,7 @@ class DecodeOps:
         """The fused decode step (qk_decode_step): one launch per token. layer_table: int64 CUDA tensor
         [n_layers, 12] of device pointers in qk_layer_t order; k_cache/v_cache: bf16 [n_layers, 1, 8, max_seq, 128]
         (a layer stride of any multiple of 16 bytes); timeline: optional int64 CUDA tensor of
-        #SMs * (5*n_layers + 1) * 16 words (layout in include/qwen3_b200.h)."""
+        #SMs * (5*n_layers + 1) * 24 words (layout in include/qwen3_b200.h)."""
         if k_cache.stride() != v_cache.stride() or k_cache.shape[-2] != max_seq or k_cache.shape[-1] != 128:
             raise ValueError("k_cache/v_cache must be [layers, 1, 8, max_seq, 128] with equal strides")
         stride = k_cache.stride(0) * k_cache.element_size()
