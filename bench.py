@@ -162,6 +162,102 @@ def step_traffic(bytes_tok):
     return t["dram_bytes_per_launch"] * bytes_tok / t["algorithmic_bytes_per_launch"]
 
 
+def time_replays(replay, reset, K: int, W: int) -> float:
+    """Seconds for K replays after W untimed ones (reset() before each group), CUDA events on the current stream."""
+    reset()
+    for _ in range(W):
+        replay()
+    torch.cuda.synchronize()
+    reset()
+    torch.cuda.synchronize()
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(K):
+        replay()
+    e1.record(s)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) * 1e-3
+
+
+def ref_format_step(K: int, W: int, peak: float):
+    """Our fused step in the reference checkpoint's format (block-128 scales, bf16 lm_head; the only format the
+    reference's own kernels run), at the bench's 36-layer 4k-context workload: tokens/s and HBM fraction."""
+    import model as M
+    from generate import Engine
+    cfg = M.Config()
+    max_seq, start = 4096, 4096 - K
+    m = M.Qwen3FP8Decode.synthetic(cfg, max_seq=max_seq, device="cuda", seed=0, scale_mode="block", head_dtype="bf16",
+                                   norm_init="ones")
+    m.fill_cache_random(start, seed=1234)
+    eng = Engine(m, fused=True)
+    eng.token.fill_(1)
+    eng.state.copy_(torch.tensor([start, 0], dtype=torch.int32))
+    eng.capture()
+
+    def reset():
+        eng.token.fill_(1)
+        eng.state.copy_(torch.tensor([start, 0], dtype=torch.int32, device="cuda"))
+
+    t = time_replays(eng.graph.replay, reset, K, W)
+    eng.check()
+    bytes_tok, _ = step_bytes(m, start, max_seq - 1)
+    out = {"format": "block-128 scales, bf16 lm_head (the reference checkpoint's)", "engine": "fused step",
+           "tok_s": K / t, "ms_per_step": t / K * 1e3, "bytes_per_token": bytes_tok,
+           "frac": bytes_tok * K / t / 1e9 / peak}
+    del eng, m
+    torch.cuda.empty_cache()
+    return out
+
+
+def ref_gpu_step(K: int, W: int, peak: float):
+    """The reference's own decode kernels (its kernels/decode.cu built for sm_100a, oracle/_ref) driven as its
+    engine drives them (Q/generate.py:102-137: one CUDA graph per step, the shipped launch knobs, chunk-64
+    attention, lm_head on every SM), at the same 36-layer 4k-context workload in its checkpoint format."""
+    import model as M
+    from oracle import ref_gpu as R
+    if not R.available():
+        return {"unavailable": "oracle/_ref/ref_decode.so was not built (no reference checkout where the tree was built)"}
+    cfg = M.Config()
+    max_seq, start = 4096, 4096 - K
+    m = M.Qwen3FP8Decode.synthetic(cfg, max_seq=max_seq, device="cuda", seed=0, scale_mode="block", head_dtype="bf16",
+                                   norm_init="ones", keep_rowmajor=True)
+    bytes_tok, _ = step_bytes(m, start, max_seq - 1)
+    layers = []
+    for L in m.layers:
+        layers.append(dict(ln1=L.ln1, ln2=L.ln2, q_norm=L.q_norm, k_norm=L.k_norm,
+                           qkv=(L.rowmajor["qkv"], L.qkv.scale), o_proj=(L.rowmajor["o_proj"], L.o.scale),
+                           gate_up=(L.rowmajor["gate_up"], L.gu.scale), down_proj=(L.rowmajor["down_proj"], L.down.scale)))
+        L.qkv = L.o = L.gu = L.down = None
+        L.rowmajor = {}
+    ref = R.RefEngine(layers, m.embed, m.norm, m.lm_head, m.cos, m.sin, max_seq)
+    del layers
+    m.k_cache = m.v_cache = None
+    torch.cuda.empty_cache()
+    g = torch.Generator(device="cuda")
+    g.manual_seed(1234)
+    for c in (ref.k_cache, ref.v_cache):
+        for li in range(c.shape[0]):
+            t = c[li, :, :start]
+            t.copy_(torch.randn(t.shape, generator=g, device="cuda", dtype=torch.float32))
+    ref.token.fill_(1)
+    ref.state.copy_(torch.tensor([start, 0], dtype=torch.int32))
+    ref.capture()
+
+    def reset():
+        ref.token.fill_(1)
+        ref.state.copy_(torch.tensor([start, 0], dtype=torch.int32, device="cuda"))
+        ref.best.zero_()
+
+    t = time_replays(ref.graph.replay, reset, K, W)
+    out = {"kernels": "reference kernels/decode.cu, sm_100a build (oracle/_ref), 183 launches per step in one graph",
+           "format": "block-128 scales, bf16 lm_head", "tok_s": K / t, "ms_per_step": t / K * 1e3,
+           "bytes_per_token": bytes_tok, "frac": bytes_tok * K / t / 1e9 / peak}
+    del ref, m
+    torch.cuda.empty_cache()
+    return out
+
+
 def cpu_model() -> str:
     try:
         with open("/proc/cpuinfo") as f:
@@ -285,6 +381,12 @@ def run_reference(args):
                       "seq_len": 4096, "parallelism": "cpu"},
            "cpu_baseline": base,
            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if torch.cuda.is_available() and not args.no_ref_gpu:
+        # the reference's GPU kernels on this box (not the arm's value: the reference arm is its CPU path)
+        try:
+            out["ref_gpu"] = ref_gpu_step(min(args.steps, 64), args.warmup, peaks()[0])
+        except Exception as e:   # report, do not fail the CPU arm
+            out["ref_gpu"] = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
     print(json.dumps(out), flush=True)
 
 
@@ -430,6 +532,10 @@ def run_ours(args):
         }
         if not args.no_cpu_baseline and ws == 1:
             out["cpu_baseline"] = cpu_baseline(start)
+        if ws == 1 and fused and not args.no_ref_format:
+            del eng, m
+            torch.cuda.empty_cache()
+            out["ref_format"] = ref_format_step(K, W, peak)
         print(json.dumps(out), flush=True)
     if ws > 1:
         import torch.distributed as dist
@@ -613,6 +719,10 @@ def main():
     ap.add_argument("--path", default="fused", choices=["fused", "ops"],
                     help="fused: one persistent kernel per token; ops: the reference's 183 per-op launches")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-ref-format", action="store_true",
+                    help="skip the extra measurement of the fused step in the reference checkpoint's format")
+    ap.add_argument("--no-ref-gpu", action="store_true",
+                    help="reference arm: skip timing the reference's own decode kernels on the GPU")
     ap.add_argument("--timeline", action="store_true",
                     help="one fused-step launch with per-phase timeline stamps, summarised (36 layers unless --layers)")
     args = ap.parse_args()

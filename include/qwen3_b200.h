@@ -146,10 +146,12 @@ typedef struct {
 
 /*
  * The whole batch-1 decode step in one launch: embed -> n_layers x (qkv GEMV, attention with KV append,
- * o_proj, gate_up, down) -> FP8 per-channel lm_head + greedy argmax -> token/state update. Replaces the
- * reference's 183-launch `Engine.decode_step` (generate.py:102-119) with bit-identical results; the ops it
- * fuses are the entry points above. Cooperative launch of one CTA per SM (graph-capturable).
+ * o_proj, gate_up, down) -> lm_head + greedy argmax -> token/state update. Replaces the reference's 183-launch
+ * `Engine.decode_step` (generate.py:102-119) with bit-identical results; the ops it fuses are the entry points
+ * above. Cooperative launch of one CTA per SM (graph-capturable).
  *   layers      DEVICE array of n_layers qk_layer_t
+ *   w_head/s_head  FP8 per-channel head: packed fp8 [vocab x 4096] and fp32 scales [vocab]; or, with s_head
+ *               NULL, the reference checkpoint's bf16 head, row-major [vocab][4096] (tp = 1 only)
  *   k_cache/v_cache  bf16 KV caches of all layers: layer l at byte offset l * kv_layer_stride, each
  *               [8][max_seq][128] (16-byte aligned, stride a multiple of 16); read through TMA tensor maps
  *   state       [pos, step]; token [1]; out_tokens [out_len]; best u64 [1] zero before the first launch

@@ -413,7 +413,7 @@ int launch_decode_step(const qk_layer_t* layers, int n_layers, void* k_cache, vo
                        float* ml_part, int* attn_counters, unsigned* sync, int max_seq, int max_splits, float eps,
                        int scale_mode, uint64_t* timeline, int tp, int rank, void* resid_alt, int vocab_offset,
                        void* const* areas, cudaStream_t stream) {
-  if (!layers || n_layers < 1 || !k_cache || !v_cache || !embed || !final_norm || !w_head || !s_head || !cos_tab ||
+  if (!layers || n_layers < 1 || !k_cache || !v_cache || !embed || !final_norm || !w_head || !cos_tab ||
       !sin_tab || !token || !state || !out_tokens || !best || !resid || !qkv || !attn || !h || !logits || !part ||
       !counters || !o_part || !ml_part || !attn_counters || !sync)
     return fail(QK_EINVAL, "null pointer argument");
@@ -430,6 +430,9 @@ int launch_decode_step(const qk_layer_t* layers, int n_layers, void* k_cache, vo
   if (max_splits < (max_seq + ST_CHUNK - 1) / ST_CHUNK || max_splits > ST_MAX_SPLITS)
     return fail(QK_EINVAL, "max_splits must cover max_seq/64 and be at most %d", ST_MAX_SPLITS);
   if (scale_mode != QK_SCALE_BLOCK128 && scale_mode != QK_SCALE_CHANNEL) return fail(QK_EINVAL, "bad scale_mode");
+  const bool head_bf16 = s_head == nullptr;   // the reference checkpoint's bf16 lm_head
+  if (head_bf16 && tp != 1) return fail(QK_EINVAL, "the tensor-parallel step needs the FP8 head (s_head)");
+  if (!aligned(w_head, 16)) return fail(QK_EINVAL, "w_head must be 16-byte aligned");
   StepParams p = {};
   if (int r = encode_kv_map(&p.tm_k, k_cache, max_seq, n_kv, n_layers, kv_layer_stride)) return r;
   if (int r = encode_kv_map(&p.tm_v, v_cache, max_seq, n_kv, n_layers, kv_layer_stride)) return r;
@@ -472,10 +475,14 @@ int launch_decode_step(const qk_layer_t* layers, int n_layers, void* k_cache, vo
   p.resid_alt = static_cast<bf16*>(resid_alt);
   p.areas = reinterpret_cast<TpArea* const*>(areas);
   void (*kernel)(const StepParams) = nullptr;
-  if (tp == 1) kernel = scale_mode == QK_SCALE_CHANNEL ? decode_step_kernel<SCALE_CHANNEL, 1> : decode_step_kernel<SCALE_BLOCK, 1>;
-  else if (tp == 2) kernel = decode_step_kernel<SCALE_CHANNEL, 2>;
-  else if (tp == 4) kernel = decode_step_kernel<SCALE_CHANNEL, 4>;
-  else if (tp == 8) kernel = decode_step_kernel<SCALE_CHANNEL, 8>;
+  if (tp == 1) {
+    if (scale_mode == QK_SCALE_CHANNEL)
+      kernel = head_bf16 ? decode_step_kernel<SCALE_CHANNEL, 1, 1> : decode_step_kernel<SCALE_CHANNEL, 1, 0>;
+    else
+      kernel = head_bf16 ? decode_step_kernel<SCALE_BLOCK, 1, 1> : decode_step_kernel<SCALE_BLOCK, 1, 0>;
+  } else if (tp == 2) kernel = decode_step_kernel<SCALE_CHANNEL, 2, 0>;
+  else if (tp == 4) kernel = decode_step_kernel<SCALE_CHANNEL, 4, 0>;
+  else if (tp == 8) kernel = decode_step_kernel<SCALE_CHANNEL, 8, 0>;
   const int smem = (int)sizeof(StepSmem);
   if (int r = ensure_smem((const void*)kernel, smem)) return r;
   cudaLaunchConfig_t cfg = {};

@@ -92,8 +92,8 @@ struct StepParams {
   int n_layers;
   const bf16* embed;                               // [vocab][4096]
   const bf16* final_norm;                          // [4096]
-  const uint8_t* w_head;                           // packed fp8 [vocab x 4096]
-  const float* s_head;                             // [vocab] per-channel
+  const uint8_t* w_head;                           // packed fp8 [vocab x 4096], or bf16 row-major [vocab][4096]
+  const float* s_head;                             // [vocab] per-channel (fp8 head only)
   int vocab;
   const bf16 *cos_tab, *sin_tab;                   // [max_seq][128]
   int* token;                                      // [1]
@@ -1102,11 +1102,79 @@ __device__ __forceinline__ void tp_reduce(const StepParams& p, const bf16* resid
   resid_next[row] = __float2bfloat16_rn(__bfloat162float(ldcg_bf16(resid + row)) + bf16r(sum));
 }
 
+// ---- bf16 lm_head (the reference checkpoint's format) -----------------------------------------------------------
+// The CTA's rows [r0, r1) stream through the ring 4 rows (32 KiB) per stage; consumer warp w computes row w % 4 of
+// every other stage (warps 0-3 the even stages, 4-7 the odd ones) and counts 2 of the stage's 8 releases. The
+// arithmetic is the bf16 lm_head kernel's (csrc/gemv.cuh, lm_head_bf16_kernel): the final RMSNorm with the
+// 256-thread strided sum of squares, and per row lane l summing elements (32 j + l) * 8 .. +7 for j = 0..15 in
+// order, then a butterfly; so logits and the chosen token are bit-identical to it.
+constexpr int ST_HEAD_ROWS = ST_STAGE / (HIDDEN * 2);   // bf16 rows per ring stage (4)
+__device__ __forceinline__ SliceRange head_rows(int vocab) {
+  const long long G = gridDim.x, c = blockIdx.x;
+  return SliceRange{(int)(c * vocab / G), (int)((c + 1) * vocab / G)};
+}
+__device__ void head_bf16_phase(Consumer& c, const bf16* x, int row_offset) {
+  StepSmem& sm = *c.sm;
+  const StepParams& p = *c.p;
+  const int tid = threadIdx.x, lane = c.lane, warp = c.warp;
+  constexpr int K = HIDDEN;
+  float* xn = reinterpret_cast<float*>(sm.xh);   // the normalised input, fp32 (16 KiB)
+  float ss = 0.f;
+  for (int i = tid; i < K; i += ST_WARPS * 32) {
+    const float f = __bfloat162float(ldcg_bf16(x + i));
+    xn[i] = f;
+    ss += f * f;
+  }
+  ss = warp_sum(ss);
+  if (lane == 0) sm.red[warp] = ss;
+  consumer_sync();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < ST_WARPS; ++i) tot += sm.red[i];
+  const float rstd = rsqrtf(tot / (float)K + p.eps);
+  for (int i = tid; i < K; i += ST_WARPS * 32) xn[i] = bf16r(__bfloat162float(p.final_norm[i]) * bf16r(xn[i] * rstd));
+  consumer_sync();
+  const SliceRange r = head_rows(p.vocab);
+  const int nst = (r.s1 - r.s0 + ST_HEAD_ROWS - 1) / ST_HEAD_ROWS;
+  const int n0 = c.n;
+  for (int s = warp / ST_HEAD_ROWS; s < nst; s += ST_WARPS / ST_HEAD_ROWS) {
+    if (!c.wait_abs(n0 + s)) atomicOr(&g_dev_error, DEVERR_MBAR_TIMEOUT);
+    const int row = r.s0 + s * ST_HEAD_ROWS + warp % ST_HEAD_ROWS;
+    if (row < r.s1) {
+      const uint8_t* wrow = sm.ring[(n0 + s) % ST_NSTAGE] + (warp % ST_HEAD_ROWS) * (K * 2);
+      float acc = 0.f;
+#pragma unroll
+      for (int j = 0; j < K / 8 / 32; ++j) {
+        const int k0 = (j * 32 + lane) * 8;
+        const uint4 wv = lds128(wrow + (size_t)(j * 32 + lane) * 16);
+        const uint32_t* q = reinterpret_cast<const uint32_t*>(&wv);
+        const float4 x0 = *reinterpret_cast<const float4*>(&xn[k0]);
+        const float4 x1 = *reinterpret_cast<const float4*>(&xn[k0 + 4]);
+        acc += __uint_as_float(q[0] << 16) * x0.x + __uint_as_float(q[0] & 0xFFFF0000u) * x0.y;
+        acc += __uint_as_float(q[1] << 16) * x0.z + __uint_as_float(q[1] & 0xFFFF0000u) * x0.w;
+        acc += __uint_as_float(q[2] << 16) * x1.x + __uint_as_float(q[2] & 0xFFFF0000u) * x1.y;
+        acc += __uint_as_float(q[3] << 16) * x1.z + __uint_as_float(q[3] & 0xFFFF0000u) * x1.w;
+      }
+      acc = warp_sum(acc);
+      if (lane == 0) p.logits[row] = __float2bfloat16_rn(acc);
+      const float lv = bf16r(acc);
+      const int gid = row + row_offset;
+      if (lv > c.best_v || (lv == c.best_v && gid < c.best_i)) {
+        c.best_v = lv;
+        c.best_i = gid;
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive_n(&sm.empty[(n0 + s) % ST_NSTAGE], ST_WARPS / ST_HEAD_ROWS);
+  }
+  c.n = n0 + nst;
+}
+
 // ---- the kernel -------------------------------------------------------------------------------------------------
 // TP = 1: the whole model on one GPU. TP > 1: this rank's shard (query heads 32/TP, KV heads 8/TP, intermediate
 // 12288/TP, vocabulary rows p.vocab from p.vocab_offset); o_proj and down produce fp32 partials that are
 // exchanged (tp_reduce) and added to the residual, in rank order on every rank.
-template <int SCALE, int TP>
+template <int SCALE, int TP, int HEAD_BF16>
 __global__ void __launch_bounds__(ST_THREADS, 1) decode_step_kernel(const __grid_constant__ StepParams p) {
   extern __shared__ __align__(1024) uint8_t smem_step[];
   StepSmem& sm = *reinterpret_cast<StepSmem*>(smem_step);
@@ -1159,7 +1227,13 @@ __global__ void __launch_bounds__(ST_THREADS, 1) decode_step_kernel(const __grid
       }
       step_stamp(p, 5 * p.n_layers, 3);
       step_put(p, 5 * p.n_layers, 6, pr.wait_cycles);
-      pr.gemv(p.w_head, (p.vocab / 16) * (H / QB));
+      if (HEAD_BF16) {   // 4 bf16 rows per stage
+        const SliceRange hr = head_rows(p.vocab);
+        for (int row = hr.s0; row < hr.s1; row += ST_HEAD_ROWS)
+          pr.push(p.w_head + (size_t)row * HIDDEN * 2, (uint32_t)(min(ST_HEAD_ROWS, hr.s1 - row) * HIDDEN * 2));
+      } else {
+        pr.gemv(p.w_head, (p.vocab / 16) * (H / QB));
+      }
     } else if (warp == ST_WARPS + 1) {   // tail fetcher: the split units' remote block dots, phase by phase
       const unsigned epoch = __ldcg(p.sync + 2);
       int n = 0;
@@ -1169,7 +1243,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) decode_step_kernel(const __grid
         tail_fetch<H / QB, 2>(sm, p, 2 * I, 5 * l + 3, epoch, n, lane);
         tail_fetch<I / QB, 1>(sm, p, H, 5 * l + 4, epoch, n, lane);
       }
-      tail_fetch<H / QB, 1>(sm, p, p.vocab, 5 * p.n_layers, epoch, n, lane);
+      if (!HEAD_BF16) tail_fetch<H / QB, 1>(sm, p, p.vocab, 5 * p.n_layers, epoch, n, lane);
     }
     return;
   }
@@ -1252,12 +1326,17 @@ __global__ void __launch_bounds__(ST_THREADS, 1) decode_step_kernel(const __grid
     grid_barrier(p.sync, nbar++, step_word(p, ph + 4, 2));
   }
   if (tl) step_stamp(p, 5 * p.n_layers, 0);
-  // HEAD: logits + greedy argmax (FP8 per-channel head; TP: this rank's vocabulary rows)
-  step_prologue<true>(c, rbuf(xk), p.final_norm, H, p.eps, nullptr);
-  if (tl) step_stamp(p, 5 * p.n_layers, 1);
+  // HEAD: logits + greedy argmax (FP8 per-channel head, or the bf16 head; TP: this rank's vocabulary rows)
   c.tl_phase = 5 * p.n_layers;
-  gemv_phase<32>(c, GemvPhase<EPI_ARGMAX, SCALE_CHANNEL, 1>{p.s_head, p.vocab, H, p.logits, p.part, p.counters,
-                                                            p.vocab_offset});
+  if (HEAD_BF16) {
+    if (tl) step_stamp(p, 5 * p.n_layers, 1);
+    head_bf16_phase(c, rbuf(xk), p.vocab_offset);
+  } else {
+    step_prologue<true>(c, rbuf(xk), p.final_norm, H, p.eps, nullptr);
+    if (tl) step_stamp(p, 5 * p.n_layers, 1);
+    gemv_phase<32>(c, GemvPhase<EPI_ARGMAX, SCALE_CHANNEL, 1>{p.s_head, p.vocab, H, p.logits, p.part, p.counters,
+                                                              p.vocab_offset});
+  }
   if (tl) { step_stamp(p, 5 * p.n_layers, 2); step_put(p, 5 * p.n_layers, 4, c.wait_cycles); step_put(p, 5 * p.n_layers, 5, c.fold_cycles); }
   {
     unsigned long long key = (c.best_i == 0x7FFFFFFF) ? 0ull : argmax_key(c.best_v, c.best_i);

@@ -28,8 +28,9 @@ DEFAULT_GEMV_SHAPE = {
 
 class Engine:
     """fused=True runs each token as ONE persistent kernel (qk_decode_step, csrc/step.cuh) instead of the
-    reference's 183 launches; results are bit-identical. It needs the FP8 per-channel lm_head and 64-key
-    attention splits; fused=False is the op-by-op path with the reference's drop-in ops."""
+    reference's 183 launches; results are bit-identical. It takes either head format (FP8 per-channel or the
+    reference's bf16 head) and needs 64-key attention splits; fused=False is the op-by-op path with the
+    reference's drop-in ops."""
 
     def __init__(self, model: Qwen3FP8Decode, pdl: bool = True, attn_chunk: int = 64, lm_head_ctas: int = 0,
                  gemv_shape: dict | None = None, fused: bool = False):
@@ -64,8 +65,8 @@ class Engine:
         self.fused = fused
         self.step_timeline = None     # fused step only: int64 [#SMs, 5*layers+1, 24] stamps (include/qwen3_b200.h)
         if fused:
-            if not isinstance(m.lm_head, Linear) or attn_chunk != 64 or m.batch != 1:
-                raise ValueError("the fused step needs an FP8 lm_head, 64-key attention splits and batch 1")
+            if attn_chunk != 64 or m.batch != 1:
+                raise ValueError("the fused step needs 64-key attention splits and batch 1")
             ptrs = []
             for li, L in enumerate(m.layers):
                 ptrs.append([L.qkv.packed.data_ptr(), L.o.packed.data_ptr(), L.gu.packed.data_ptr(),
@@ -95,8 +96,9 @@ class Engine:
         """Launch one decode step (eager). Also what gets captured into the graph."""
         m, k, cfg = self.m, self.k, self.m.cfg
         if self.fused:
-            k.decode_step(self.layer_table, len(m.layers), m.k_cache, m.v_cache, m.embed, m.norm, m.lm_head.packed,
-                          m.lm_head.scale, m.cos, m.sin, self.token, self.state, self.out_tokens, self.best,
+            fp8_head = isinstance(m.lm_head, Linear)
+            k.decode_step(self.layer_table, len(m.layers), m.k_cache, m.v_cache, m.embed, m.norm,
+                          m.lm_head.packed if fp8_head else m.lm_head, m.lm_head.scale if fp8_head else None, m.cos, m.sin, self.token, self.state, self.out_tokens, self.best,
                           self.resid, self.qkv, self.attn, self.h, self.logits, self.part, self.gemv_counters,
                           self.o_part, self.ml_part, self.counters, self.sync, m.max_seq, cfg.eps, self.scale_mode,
                           self.step_timeline)

@@ -219,6 +219,10 @@ class DecodeOps:
         #SMs * (5*n_layers + 1) * 24 words (layout in include/qwen3_b200.h)."""
         if k_cache.stride() != v_cache.stride() or k_cache.shape[-2] != max_seq or k_cache.shape[-1] != 128:
             raise ValueError("k_cache/v_cache must be [layers, 1, 8, max_seq, 128] with equal strides")
+        if s_head is not None:
+            check_packed(w_head, False, "decode_step")
+        elif w_head.dtype != torch.bfloat16:
+            raise RuntimeError("decode_step: without s_head the head must be bf16 [vocab, 4096]")
         stride = k_cache.stride(0) * k_cache.element_size()
         st = self.lib.qk_decode_step(_p(layer_table), int(n_layers), _p(k_cache), _p(v_cache), stride, _p(embed),
                                      _p(final_norm), _p(w_head),

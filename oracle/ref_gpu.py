@@ -110,6 +110,25 @@ class RefEngine:
         k.lm_head_argmax(self.lm_head, self.resid, self.norm, self.logits, self.best, eps, self.lm_head_ctas)
         k.finalize(self.best, self.token, self.out_tokens, self.state)
 
+    def capture(self):
+        """One decode step into a CUDA graph, as the reference engine does (Q/generate.py:121-137): two eager
+        warm-up steps on a side stream (token and state restored after each), then the capture."""
+        token, state = self.token.clone(), self.state.clone()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                self.token.copy_(token)
+                self.state.copy_(state)
+                self.decode_step()
+        torch.cuda.current_stream().wait_stream(s)
+        self.token.copy_(token)
+        self.state.copy_(state)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.decode_step()
+        torch.cuda.synchronize()
+
     @torch.no_grad()
     def generate(self, prompt, gen_len):
         """Prompt through the decode step (teacher forcing, as the B200 engine does), then greedy."""

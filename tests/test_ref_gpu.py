@@ -97,9 +97,11 @@ def test_lm_head_bf16_bitwise_vs_reference_kernel():
     assert int(bm.item()) == int(br.item())
 
 
-def test_greedy_256_identical_to_reference_engine():
+@pytest.mark.parametrize("fused", [False, True], ids=["ops", "fused"])
+def test_greedy_256_identical_to_reference_engine(fused):
     """Full 36-layer model, block-128 scales + bf16 lm_head (the reference's format): 256 greedy tokens from
-    the B200 engine (CUDA graph) == the reference engine's decode step run on its own kernels."""
+    the B200 engine (CUDA graph; the op path or the fused one-launch step) == the reference engine's decode
+    step run on its own kernels, and the KV caches equal."""
     from generate import Engine
     cfg = M.Config()
     m = M.Qwen3FP8Decode.synthetic(cfg, max_seq=512, device="cuda", seed=0, scale_mode="block", head_dtype="bf16",
@@ -118,7 +120,7 @@ def test_greedy_256_identical_to_reference_engine():
     ref_k = ref.k_cache.clone()
     del ref
     torch.cuda.empty_cache()
-    eng = Engine(m)
+    eng = Engine(m, fused=fused)
     tokens = eng.generate(prompt, 256)
     assert tokens == ref_tokens, next(i for i, (a, b) in enumerate(zip(tokens, ref_tokens)) if a != b)
     assert torch.equal(m.k_cache[:, 0, :, : len(prompt) + 255], ref_k[:, :, : len(prompt) + 255])

@@ -8,10 +8,10 @@ import model as M
 pytestmark = pytest.mark.gpu
 
 
-def build(n_layers, scale_mode, vocab=4096, max_seq=512, seed=3):
+def build(n_layers, scale_mode, vocab=4096, max_seq=512, seed=3, head="fp8"):
     cfg = M.Config(layers=n_layers, vocab=vocab)
     m = M.Qwen3FP8Decode.synthetic(cfg, max_seq=max_seq, device="cuda", seed=seed, scale_mode=scale_mode,
-                                   head_dtype="fp8", norm_init="random")
+                                   head_dtype=head, norm_init="random")
     return m
 
 
@@ -51,6 +51,15 @@ def test_fused_step_matches_op_by_op_small(scale_mode):
     m = build(2, scale_mode)
     ref = run_steps(m, fused=False, start_pos=0, steps=6, use_graph=False)
     got = run_steps(m, fused=True, start_pos=0, steps=6, use_graph=False)
+    assert_same(got, ref)
+
+
+def test_fused_step_bf16_head_matches_op_by_op():
+    """The reference checkpoint's format: block-128 scales and the bf16 lm_head (vocabulary not a multiple of
+    the 4-row ring stage per CTA), bit for bit against the op path."""
+    m = build(2, "block", vocab=4112, head="bf16")
+    ref = run_steps(m, fused=False, start_pos=40, steps=5, use_graph=True, fill=40)
+    got = run_steps(m, fused=True, start_pos=40, steps=5, use_graph=True, fill=40)
     assert_same(got, ref)
 
 
