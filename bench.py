@@ -701,6 +701,84 @@ def run_timeline(args):
     print(json.dumps({"timeline": summ}), flush=True)
 
 
+def run_attention_sweep(args):
+    """BASELINE config 4 through the drop-in attention op (the two kernels of qk_attention: partials, merge):
+    contexts L in {1k, 4k, 8k, 16k, 32k}, batch 1 (length L) and batch 8 (lengths ~ U[L/2, L], seeded), KV
+    N(0,1) bf16, the new token at position len. Per point: time per call (CUDA events around one replay of a
+    graph of K calls, after W eager ones; the caches of as many independent layers as keep the working set
+    above the 126 MB L2, cycled), the KV bytes
+    it must read (K and V of len + 1 keys, 8 heads, plus the appended row), and GB/s against the measured HBM
+    peak. One JSON line per point."""
+    from kernels import ops
+    import model as M
+    k = ops()
+    peak, _ = peaks()
+    K, W = max(args.steps, 8), max(args.warmup, 3)
+    out = []
+    for L in (1024, 4096, 8192, 16384, 32768):
+        for batch in (1, 8):
+            if batch == 1:
+                lengths = [L]
+            else:
+                g = torch.Generator().manual_seed(L)
+                lengths = [int(x) for x in torch.randint(L // 2, L + 1, (batch,), generator=g)]
+            max_seq = L + 1
+            kv_bytes = sum((p + 1) * 8 * 128 * 2 * 2 for p in lengths)
+            per_layer = 2 * batch * 8 * max_seq * 128 * 2
+            n_layers = max(1, -(-256 * 2 ** 20 // per_layer))           # > 2 x L2 of caches, cycled
+            g = torch.Generator(device="cuda").manual_seed(L + batch)
+            caches = []
+            for _ in range(n_layers):
+                kc = torch.randn(batch, 8, max_seq, 128, generator=g, device="cuda").to(torch.bfloat16)
+                vc = torch.randn(batch, 8, max_seq, 128, generator=g, device="cuda").to(torch.bfloat16)
+                caches.append((kc, vc))
+            qkv = (torch.randn(batch, 6144, generator=g, device="cuda") * 2).to(torch.bfloat16)
+            qn = torch.ones(128, dtype=torch.bfloat16, device="cuda")
+            cos, sin = M.rope_tables(max_seq, 128, 1e6, "cuda")
+            max_splits = (max_seq + 63) // 64
+            o_part = torch.zeros(batch, 32, max_splits, 128, device="cuda")
+            ml_part = torch.zeros(batch, 32, max_splits, 2, device="cuda")
+            counters = torch.zeros(batch, 8, dtype=torch.int32, device="cuda")
+            state = torch.tensor([[p, 0] for p in lengths], dtype=torch.int32, device="cuda").view(-1)
+            att = torch.empty(batch, 4096, dtype=torch.bfloat16, device="cuda")
+
+            def call(i):
+                kc, vc = caches[i % n_layers]
+                k.attention(qkv, qn, qn, cos, sin, state, kc, vc, o_part, ml_part, counters, att, 128 ** -0.5,
+                            1e-6, 0, 64, batch=batch)
+
+            for i in range(W):
+                call(i)
+            torch.cuda.synchronize()
+            # the timed calls replay from one CUDA graph (as the engine runs them), so host launch cost is out
+            graph = torch.cuda.CUDAGraph()
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                with torch.cuda.graph(graph, stream=side):
+                    for i in range(K):
+                        call(i)
+            torch.cuda.current_stream().wait_stream(side)
+            graph.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            graph.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) / K * 1e3
+            del graph
+            gbs = kv_bytes / (us * 1e-6) / 1e9
+            rec = {"sweep": "attention", "ctx": L, "batch": batch, "lengths": lengths, "us_per_call": us,
+                   "kv_bytes": kv_bytes, "gbs": gbs, "frac_of_peak": gbs / peak, "layers_cycled": n_layers}
+            print(json.dumps(rec), flush=True)
+            out.append(rec)
+            del caches
+            torch.cuda.empty_cache()
+    assert k.device_error() == 0
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--profile-kernel", choices=["qkv", "o_proj", "gate_up", "down", "lm_head", "attention", "decode_step"],
@@ -723,11 +801,14 @@ def main():
                     help="skip the extra measurement of the fused step in the reference checkpoint's format")
     ap.add_argument("--no-ref-gpu", action="store_true",
                     help="reference arm: skip timing the reference's own decode kernels on the GPU")
+    ap.add_argument("--sweep", choices=["attention"], help="BASELINE config 4: the attention op over contexts and batches")
     ap.add_argument("--timeline", action="store_true",
                     help="one fused-step launch with per-phase timeline stamps, summarised (36 layers unless --layers)")
     args = ap.parse_args()
     if args.timeline:
         return run_timeline(args)
+    if args.sweep == "attention":
+        return run_attention_sweep(args)
     if args.profile_kernel:
         return run_profile_kernel(args)
     if args.warmup < 3:

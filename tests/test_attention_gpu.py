@@ -117,3 +117,48 @@ def test_attention_long_context_32k():
     e = ((out[0].float() - ref).norm() / ref.norm()).item()
     assert e < 5e-3, e
     assert int(counters.abs().sum()) == 0
+
+
+def sweep_lengths(L: int, batch: int, seed: int = 0):
+    """BASELINE config 4's sequence lengths: batch 1 holds L keys; batch 8 holds lengths ~ U[L/2, L], seeded.
+    The new token goes at position len (so the attention covers len + 1 keys)."""
+    if batch == 1:
+        return [L]
+    g = torch.Generator().manual_seed(seed + L)
+    return [int(x) for x in torch.randint(L // 2, L + 1, (batch,), generator=g)]
+
+
+@pytest.mark.parametrize("L", [1024, 4096, 8192, 16384, 32768])
+@pytest.mark.parametrize("batch", [1, 8])
+def test_attention_sweep_point(L, batch):
+    """Every point of the attention sweep (bench.py --sweep attention): the drop-in op on the GPU against fp32
+    attention in torch on the GPU from the same normalised, rotated q (the oracle's norm_rope), with the new
+    K/V rows appended at each sequence's position: within 5e-3 rel-L2 (the reference's bar), V rows exact."""
+    from kernels import ops
+    lengths = sweep_lengths(L, batch)
+    max_seq = L + 1
+    g = torch.Generator(device="cuda").manual_seed(L * 10 + batch)
+    kc = torch.randn(batch, 8, max_seq, 128, generator=g, device="cuda").to(torch.bfloat16)
+    vc = torch.randn(batch, 8, max_seq, 128, generator=g, device="cuda").to(torch.bfloat16)
+    qkv = (torch.randn(batch, 6144, generator=g, device="cuda") * 2).to(torch.bfloat16)
+    qn = torch.ones(128, dtype=torch.bfloat16, device="cuda")
+    k = ops()
+    cos, sin = M.rope_tables(max_seq, 128, 1e6, "cuda")
+    max_splits = (max_seq + 63) // 64
+    o_part = torch.zeros(batch, 32, max_splits, 128, device="cuda")
+    ml_part = torch.zeros(batch, 32, max_splits, 2, device="cuda")
+    counters = torch.zeros(batch, 8, dtype=torch.int32, device="cuda")
+    state = torch.tensor([[p, 0] for p in lengths], dtype=torch.int32, device="cuda").view(-1)
+    out = torch.empty(batch, 4096, dtype=torch.bfloat16, device="cuda")
+    k.attention(qkv, qn, qn, cos, sin, state, kc, vc, o_part, ml_part, counters, out, 128 ** -0.5, EPS, 0, 64,
+                batch=batch)
+    torch.cuda.synchronize()
+    assert k.device_error() == 0
+    for b, pos in enumerate(lengths):
+        q, _, v = qkv[b].split([4096, 1024, 1024])
+        assert torch.equal(vc[b, :, pos], v.view(8, 128))
+        qr = O.norm_rope(q.view(32, 128), qn, cos[pos], sin[pos], EPS).float().view(8, 4, 128)
+        s = torch.einsum("ghd,gjd->ghj", qr, kc[b, :, : pos + 1].float()) * 128 ** -0.5
+        ref = torch.einsum("ghj,gjd->ghd", torch.softmax(s, -1), vc[b, :, : pos + 1].float()).reshape(-1)
+        e = ((out[b].float() - ref).norm() / ref.norm()).item()
+        assert e < 5e-3, (b, pos, e)
