@@ -569,6 +569,15 @@ def run_profile_kernel(args):
         print(f"profiled decode_step ({args.layers} layers, vocab 16384) x{args.launches}; algorithmic bytes per "
               f"launch {alg:.0f}")
         return
+    if args.profile_kernel == "gemm_rows":   # the tcgen05 batched linear, gate_up shape, 64 rows
+        w, s = M.synth_linear(0, "prof.gemm", 24576, 4096, "channel", device=dev)
+        x = torch.randn(64, 4096, device=dev).to(torch.bfloat16)
+        out = torch.empty(64, 24576, dtype=torch.bfloat16, device=dev)
+        for _ in range(args.launches):
+            k.fp8_gemm_rows(x, w, s, out)
+        torch.cuda.synchronize()
+        print(f"profiled gemm_rows x{args.launches}")
+        return
     if args.profile_kernel == "attention":
         max_seq = 4096
         kc = torch.randn(8, max_seq, 128, device=dev).to(torch.bfloat16)
@@ -701,6 +710,74 @@ def run_timeline(args):
     print(json.dumps({"timeline": summ}), flush=True)
 
 
+def run_gemv_sweep(args):
+    """the FP8 linear of each decode GEMV shape K -> N in {4096->6144, 4096->4096,
+    4096->24576, 12288->4096, 4096->151936} for rows in {1, 4, 16, 64}, x ~ N(0,1) bf16, per-channel scales.
+    rows 1: the batch-1 GEMV (qk_fp8_gemv, the decode step's kernel; kind 5 = W8A8 dot to fp32); every row
+    count also through the tcgen05 batched linear (qk_fp8_gemm_rows: activation quantization + the tensor-core
+    GEMM). Per point: time per call (one replay of a CUDA graph of K calls after W eager ones; enough weight
+    copies are cycled that the weights come from HBM), algorithmic bytes N*K + scales + rows*K*2 + output, and
+    GB/s against the measured HBM peak. One JSON line per point."""
+    from kernels import ops
+    import model as M
+    k = ops()
+    peak, _ = peaks()
+    K_calls, W = max(args.steps, 8), max(args.warmup, 3)
+    shapes = ((4096, 6144), (4096, 4096), (4096, 24576), (12288, 4096), (4096, 151936))
+    if args.shapes:
+        shapes = [tuple(int(v) for v in sh.split("x")) for sh in args.shapes.split(",")]
+    for (Kd, N) in shapes:
+        copies = max(1, -(-256 * 2 ** 20 // (N * Kd)))
+        ws = [M.synth_linear(c, f"sweep.{N}.{Kd}", N, Kd, "channel", device="cuda") for c in range(copies)]
+        packed = [M.pack_fp8(w) for w, _ in ws]
+        for rows in ([int(r) for r in args.rows.split(",")] if args.rows else (1, 4, 16, 64)):
+            x = torch.randn(rows, Kd, device="cuda").to(torch.bfloat16)
+            impls = [("tcgen05", None)] if rows > 1 else [("gemv", None), ("tcgen05", None)]
+            for impl, _ in impls:
+                if impl == "gemv":
+                    out = torch.empty(N, dtype=torch.float32, device="cuda")
+
+                    def call(i):
+                        w, s = ws[i % copies]
+                        k.fp8_gemv(5, packed[i % copies], s, x[0], None, out, N, 1e-6)
+                    out_bytes = N * 4
+                else:
+                    out = torch.empty(rows, N, dtype=torch.bfloat16, device="cuda")
+
+                    def call(i):
+                        w, s = ws[i % copies]
+                        k.fp8_gemm_rows(x, w, s, out)
+                    out_bytes = rows * N * 2
+                for i in range(W):
+                    call(i)
+                torch.cuda.synchronize()
+                graph = torch.cuda.CUDAGraph()
+                side = torch.cuda.Stream()
+                side.wait_stream(torch.cuda.current_stream())
+                with torch.cuda.stream(side):
+                    with torch.cuda.graph(graph, stream=side):
+                        for i in range(K_calls):
+                            call(i)
+                torch.cuda.current_stream().wait_stream(side)
+                graph.replay()
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                graph.replay()
+                e1.record()
+                torch.cuda.synchronize()
+                us = e0.elapsed_time(e1) / K_calls * 1e3
+                nbytes = N * Kd + N * 4 + rows * Kd * 2 + out_bytes
+                gbs = nbytes / (us * 1e-6) / 1e9
+                print(json.dumps({"sweep": "gemv", "K": Kd, "N": N, "rows": rows, "impl": impl, "us_per_call": us,
+                                  "bytes": nbytes, "gbs": gbs, "frac_of_peak": gbs / peak,
+                                  "flops": 2 * rows * N * Kd}), flush=True)
+                del graph
+        del ws, packed
+        torch.cuda.empty_cache()
+    assert k.device_error() == 0
+
+
 def run_attention_sweep(args):
     """BASELINE config 4 through the drop-in attention op (the two kernels of qk_attention: partials, merge):
     contexts L in {1k, 4k, 8k, 16k, 32k}, batch 1 (length L) and batch 8 (lengths ~ U[L/2, L], seeded), KV
@@ -781,7 +858,8 @@ def run_attention_sweep(args):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--profile-kernel", choices=["qkv", "o_proj", "gate_up", "down", "lm_head", "attention", "decode_step"],
+    ap.add_argument("--profile-kernel", choices=["qkv", "o_proj", "gate_up", "down", "lm_head", "attention", "decode_step",
+                                                 "gemm_rows"],
                     help="launch one kernel --launches times on synthetic inputs and exit (for ncu)")
     ap.add_argument("--launches", type=int, default=3)
     ap.add_argument("--layers", type=int, default=2, help="decoder layers of the --profile-kernel decode_step model")
@@ -801,7 +879,10 @@ def main():
                     help="skip the extra measurement of the fused step in the reference checkpoint's format")
     ap.add_argument("--no-ref-gpu", action="store_true",
                     help="reference arm: skip timing the reference's own decode kernels on the GPU")
-    ap.add_argument("--sweep", choices=["attention"], help="BASELINE config 4: the attention op over contexts and batches")
+    ap.add_argument("--sweep", choices=["attention", "gemv"],
+                    help="attention: BASELINE config 4 (contexts x batches); gemv: config 3 (shapes x rows)")
+    ap.add_argument("--shapes", default="", help="--sweep gemv: comma-separated KxN shapes instead of the five")
+    ap.add_argument("--rows", default="", help="--sweep gemv: comma-separated row counts instead of 1,4,16,64")
     ap.add_argument("--timeline", action="store_true",
                     help="one fused-step launch with per-phase timeline stamps, summarised (36 layers unless --layers)")
     args = ap.parse_args()
@@ -809,6 +890,8 @@ def main():
         return run_timeline(args)
     if args.sweep == "attention":
         return run_attention_sweep(args)
+    if args.sweep == "gemv":
+        return run_gemv_sweep(args)
     if args.profile_kernel:
         return run_profile_kernel(args)
     if args.warmup < 3:

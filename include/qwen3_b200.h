@@ -235,6 +235,20 @@ int qk_embed(const int* token, const void* table, void* resid, int vocab, int ba
 int qk_finalize(unsigned long long* best, int* token, int* out_tokens, int* state, int out_len, int batch,
                 qk_stream_t stream);
 
+/* Batched FP8 W8A8 linear on the tcgen05 tensor cores (BASELINE's batched GEMV rows; the reference's batched
+ * path is its Triton fp8_matmul, prefill.py:121-156, with act_quant :23-41): out[m][n] = bf16(sum over K blocks
+ * kb of dot_kb(q(x[m]), w[n]) * s_x[m][kb] * s_w[n][kb]) for M = 1..64 rows, where q() is the per-128-group e4m3
+ * quantizer of the GEMV (optionally after RMSNorm with norm_w). x bf16 [M][K]; w fp8 row-major [N][K] (plain
+ * matrix, TMA boxes; not the GEMV's packed layout); w_scale fp32 [N] (QK_SCALE_CHANNEL) or [N/128][K/128];
+ * out bf16 [M][N]; N and K multiples of 128, N <= 1,048,576, K <= 16384. scratch: at least
+ * qk_fp8_gemm_rows_scratch_bytes(M, N, K) bytes, 256-byte aligned, zeroed once before the first call (its first
+ * 32 KiB hold the tile counters, which every call leaves zero, so one buffer serves calls of any shape). Results match the oracle's
+ * recipe to rounding (split-K boundaries reorder the fp32 sum), not bit for bit. */
+long long qk_fp8_gemm_rows_scratch_bytes(int M, int N, int K);
+int qk_fp8_gemm_rows(const void* x, const void* norm_w, int M, int K, const void* w, const float* w_scale,
+                     int scale_mode, int N, float eps, void* out, void* scratch, long long scratch_bytes,
+                     qk_stream_t stream);
+
 /* Tensor-parallel helpers (no counterpart in the single-GPU reference; the TP plan of its decode step):
  * resid[i] = bf16(resid[i] + bf16(sum[i])) for the fp32 all-reduced partial of a row-parallel GEMV (the
  * rounding of the reference's residual epilogue, decode.cu:320-323); and the top-bit flip of packed argmax

@@ -10,6 +10,7 @@
 #include "../../include/qwen3_b200.h"
 #include "attention.cuh"
 #include "common.cuh"
+#include "gemm_tc.cuh"
 #include "gemv.cuh"
 #include "step.cuh"
 
@@ -70,6 +71,22 @@ int encode_cache_map(CUtensorMap* map, void* base, int max_seq, int n_kv, int n_
 }
 int encode_kv_map(CUtensorMap* map, void* base, int max_seq, int n_kv, int n_layers, long long layer_stride_bytes) {
   return encode_cache_map(map, base, max_seq, n_kv, n_layers, layer_stride_bytes, 64);
+}
+
+// TMA map of a row-major fp8 matrix [rows][cols] (cols bytes per row), box {128 bytes, box_rows}, 128-byte
+// swizzle, rows past the end zero-filled.
+int encode_fp8_rows_map(CUtensorMap* map, const void* base, long long rows, long long cols, int box_rows) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return fail(QK_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)cols};
+  const cuuint32_t box[2] = {128, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(QK_EINVAL, "cuTensorMapEncodeTiled failed for an fp8 matrix (CUresult %d)", (int)r);
+  return QK_OK;
 }
 
 int device_sms() {
@@ -608,6 +625,76 @@ int qk_argmax_key_flip(unsigned long long* keys, int n, qk_stream_t stream) {
 }
 
 }  // extern "C"
+
+// ---- batched FP8 linear on the tcgen05 tensor cores ----------------------------------------------------------
+namespace {
+int gemm_rows_pad(int M) { return M <= 16 ? 16 : (M <= 32 ? 32 : 64); }
+struct GemmScratch { size_t qx, sx, part, counters, total; };
+// The tile counters come first, in a region of fixed size, so that they stay zero from call to call whatever
+// the shapes (every call leaves them zero); the quantized activations, their scales and the split-tile partials
+// follow and need no initial value.
+GemmScratch gemm_scratch_layout(int M, int N, int K, int grid) {
+  auto up = [](size_t v) { return (v + 255) / 256 * 256; };
+  GemmScratch L;
+  (void)N;
+  L.counters = 0;
+  L.qx = up((size_t)TC_MAX_TILES * 4);
+  L.sx = L.qx + up((size_t)M * K);
+  L.part = L.sx + up((size_t)M * (K / QB) * 4);
+  L.total = L.part + up((size_t)grid * 2 * TC_TILE * gemm_rows_pad(M) * 4);
+  return L;
+}
+}  // namespace
+
+extern "C" long long qk_fp8_gemm_rows_scratch_bytes(int M, int N, int K) {
+  if (M < 1 || M > TC_MAX_ROWS || N < TC_TILE || N % TC_TILE || N / TC_TILE > TC_MAX_TILES || K < TC_BK ||
+      K % TC_BK || K > 16384)
+    return -1;
+  return (long long)gemm_scratch_layout(M, N, K, device_sms()).total;
+}
+
+extern "C" int qk_fp8_gemm_rows(const void* x, const void* norm_w, int M, int K, const void* w, const float* w_scale,
+                                int scale_mode, int N, float eps, void* out, void* scratch, long long scratch_bytes,
+                                qk_stream_t stream) {
+  if (!x || !w || !w_scale || !out || !scratch) return fail(QK_EINVAL, "null pointer argument");
+  if (M < 1 || M > TC_MAX_ROWS) return fail(QK_EINVAL, "M=%d rows: 1..%d per call", M, TC_MAX_ROWS);
+  if (N < TC_TILE || N % TC_TILE || N / TC_TILE > TC_MAX_TILES || K < TC_BK || K % TC_BK || K > 16384)
+    return fail(QK_EINVAL, "N=%d, K=%d: both multiples of 128 (N at most %d, K at most 16384)", N, K, TC_MAX_TILES * TC_TILE);
+  if (scale_mode != QK_SCALE_BLOCK128 && scale_mode != QK_SCALE_CHANNEL) return fail(QK_EINVAL, "bad scale_mode %d", scale_mode);
+  if (!aligned(x, 16) || !aligned(w, 16) || !aligned(out, 16) || !aligned(scratch, 256) || (norm_w && !aligned(norm_w, 16)))
+    return fail(QK_EINVAL, "x, w and out must be 16-byte aligned, scratch 256-byte aligned");
+  const int sms = device_sms();
+  const long long pairs = (long long)(N / TC_TILE) * (K / TC_BK);
+  const int grid = (int)(pairs < sms ? pairs : sms);
+  const GemmScratch L = gemm_scratch_layout(M, N, K, sms);
+  if (scratch_bytes < (long long)L.total)
+    return fail(QK_EINVAL, "scratch too small: %lld bytes, need qk_fp8_gemm_rows_scratch_bytes = %zu", scratch_bytes, L.total);
+  unsigned char* sc = static_cast<unsigned char*>(scratch);
+  TcGemmParams p = {};
+  if (int r = encode_fp8_rows_map(&p.tm_w, w, N, K, TC_TILE)) return r;
+  const int mp = gemm_rows_pad(M);
+  if (int r = encode_fp8_rows_map(&p.tm_x, sc + L.qx, M, K, mp)) return r;
+  p.sx = reinterpret_cast<const float*>(sc + L.sx);
+  p.sw = w_scale;
+  p.out = static_cast<bf16*>(out);
+  p.part = reinterpret_cast<float*>(sc + L.part);
+  p.counters = reinterpret_cast<int*>(sc + L.counters);
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.scale_block = scale_mode == QK_SCALE_BLOCK128;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (int r = launch(quantize_rows_kernel, dim3(M), dim3(256), 0, st, static_cast<const bf16*>(x),
+                     static_cast<const bf16*>(norm_w), K, eps, sc + L.qx, reinterpret_cast<float*>(sc + L.sx)))
+    return r;
+  auto run = [&](auto kernel, size_t smem) -> int {
+    if (int r = ensure_smem((const void*)kernel, (int)smem)) return r;
+    return launch(kernel, dim3(grid), dim3(TC_THREADS), smem, st, p);
+  };
+  if (mp == 16) return run(fp8_gemm_tc_kernel<16>, tc_smem_bytes<16>());
+  if (mp == 32) return run(fp8_gemm_tc_kernel<32>, tc_smem_bytes<32>());
+  return run(fp8_gemm_tc_kernel<64>, tc_smem_bytes<64>());
+}
 
 // ---- GEMV without caller-provided scratch --------------------------------------------------------------------
 // qk_fp8_gemv needs two scratch buffers from its caller (the split-K block dots and the per-unit counters).

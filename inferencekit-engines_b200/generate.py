@@ -183,8 +183,9 @@ class Engine:
         for t in (self.counters, self.best) + ((self.sync, self.gemv_counters, self.part) if self.fused else ()):
             t.zero_()
         if not self.fused:
-            for _, cnt in self.k._scratch.values():
-                cnt.zero_()
+            for key, val in self.k._scratch.items():
+                if isinstance(val, tuple):   # the GEMV's (block dots, unit counters)
+                    val[1].zero_()
         torch.cuda.synchronize()
         self.k.device_error()
 

@@ -65,6 +65,8 @@ _SIGS = {
     "qk_decode_step_counters": ([_I], _I),
     "qk_fp8_gemv_noalloc": ([_I, _VP, _VP, _I, _VP, _VP, _VP, _VP, _VP, _I, _I, _F, _VP], _I),
     "qk_finalize": ([_VP, _VP, _VP, _VP, _I, _I, _VP], _I),
+    "qk_fp8_gemm_rows_scratch_bytes": ([_I, _I, _I], ctypes.c_longlong),
+    "qk_fp8_gemm_rows": ([_VP, _VP, _I, _I, _VP, _VP, _I, _I, _F, _VP, _VP, ctypes.c_longlong, _VP], _I),
 }
 
 
@@ -282,6 +284,28 @@ class DecodeOps:
     def embed(self, token, table, resid):
         b = token.numel()
         self._check(self.lib.qk_embed(_p(token), _p(table), _p(resid), table.shape[0], b, _stream()), "embed")
+
+    def fp8_gemm_rows(self, x, w, w_scale, out, norm_w=None, eps=1e-6):
+        """Batched FP8 linear on the tcgen05 tensor cores: out[m] = bf16 W8A8 linear of x[m] (optionally
+        RMS-normalised with norm_w first), for M = 1..64 rows. x bf16 [M, K]; w row-major fp8 [N, K] (this op
+        streams TMA boxes of the plain matrix, not the pack_fp8 layout); w_scale fp32 [N] or [N/128, K/128];
+        out bf16 [M, N]. Scratch is owned by this object (zeroed once per size and device)."""
+        if isinstance(w, PackedFP8) or w.dtype != torch.float8_e4m3fn or w.dim() != 2 or not w.is_contiguous():
+            raise RuntimeError("fp8_gemm_rows: w must be a row-major float8_e4m3fn [N, K] matrix (not pack_fp8)")
+        M, K = x.shape
+        N = w.shape[0]
+        nbytes = self.lib.qk_fp8_gemm_rows_scratch_bytes(M, N, K)
+        if nbytes < 0:
+            raise RuntimeError(f"fp8_gemm_rows: unsupported shape M={M} N={N} K={K}")
+        key = ("gemm", x.device.index if x.device.index is not None else torch.cuda.current_device())
+        sc = self._scratch.get(key)
+        if sc is None or sc.numel() < nbytes:
+            sc = torch.zeros(nbytes, dtype=torch.uint8, device=x.device)
+            self._scratch[key] = sc
+        scale_mode = SCALE_CHANNEL if w_scale.dim() == 1 else SCALE_BLOCK128
+        st = self.lib.qk_fp8_gemm_rows(_p(x), _p(norm_w), M, K, _p(w), _p(w_scale), scale_mode, N, float(eps),
+                                       _p(out), _p(sc), sc.numel(), _stream())
+        self._check(st, "fp8_gemm_rows")
 
     def finalize(self, best, token, out_tokens, state):
         b = token.numel()
