@@ -623,7 +623,8 @@ def timeline_summary(tl, n_layers: int, clock_ghz: float = 1.965) -> dict:
     stages, folding units; producer waiting for free slots), 7 consumer warp 0 leaves the stage loop
     (attention: partials done), 8 cumulative cycles warp 0 waited for the slowest warp to release a stage it
     folds, 9-15 warps 1-7 leave the stage loop, 16-18 warp 0's cycles computing slice pairs, taking and
-    counting them, and the pairs it took). Times in us: medians over CTAs, then over layers 1..n-1 (layer 0 includes the
+    counting them, and the pairs it took; attention: 9-12 K/V landed, setup, scores, softmax done; merge: 13-15
+    entered, KV head counter complete, split weights ready). Times in us: medians over CTAs, then over layers 1..n-1 (layer 0 includes the
     launch ramp). `barrier` is the time from a CTA's end of the phase to its start of the next one; `tail` from
     warp 0 leaving the stage loop to the whole CTA being done; `ring_wait` the consumer's stage waits inside
     the phase; `producer_wait` the producer's waits for free slots while issuing the phase. For every grid
@@ -657,9 +658,15 @@ def timeline_summary(tl, n_layers: int, clock_ghz: float = 1.965) -> dict:
             lags.setdefault(name, []).append(us(exits - exits.min(1, keepdims=True)))
         a = t[:, b + 1]
         merged = us(a[:, 1] - a[:, 7])
+        mg = a[:128]   # the merging CTAs
         per["attn"].append(dict(partials=us(a[:, 7] - a[:, 0]), arrive=merged,
                                 merge_on_merging_ctas=np.sort(merged)[-4:], tail=us(a[:, 2] - a[:, 1]),
-                                barrier=us(t[:, b + 2, 0] - a[:, 2]), producer_wait=cyc(pw[:, b + 1])))
+                                barrier=us(t[:, b + 2, 0] - a[:, 2]), producer_wait=cyc(pw[:, b + 1]),
+                                kv_landed=us(a[:, 9] - a[:, 0]), setup=us(a[:, 10] - a[:, 9]),
+                                scores=us(a[:, 11] - a[:, 10]), softmax=us(a[:, 12] - a[:, 11]),
+                                pv_and_store=us(a[:, 7] - a[:, 12]), merge_counter_wait=us(mg[:, 14] - mg[:, 13]),
+                                merge_weights=us(mg[:, 15] - mg[:, 14]), merge_sum=us(mg[:, 1] - mg[:, 15]),
+                                merge_entry_after_release=us(mg[:, 14] - a[:, 0].min())))
         layer_us.append(np.median(us(t[:, b + 5, 0] - t[:, b, 0])))
         for end_ph in (b, b + 1, b + 2, b + 3, b + 4):
             arrive, leave = t[:, end_ph, 2], t[:, end_ph + 1, 0]
@@ -707,6 +714,8 @@ def run_timeline(args):
     eng.check()
     summ = timeline_summary(eng.step_timeline, n)
     summ["ctx"] = start + args.launches - 1
+    if args.timeline_out:   # the raw stamps [CTA][phase][word], for per-CTA analysis
+        torch.save(eng.step_timeline.cpu(), args.timeline_out)
     print(json.dumps({"timeline": summ}), flush=True)
 
 
@@ -883,6 +892,7 @@ def main():
                     help="attention: BASELINE config 4 (contexts x batches); gemv: config 3 (shapes x rows)")
     ap.add_argument("--shapes", default="", help="--sweep gemv: comma-separated KxN shapes instead of the five")
     ap.add_argument("--rows", default="", help="--sweep gemv: comma-separated row counts instead of 1,4,16,64")
+    ap.add_argument("--timeline-out", default="", help="--timeline: also save the raw stamps (torch.save) here")
     ap.add_argument("--timeline", action="store_true",
                     help="one fused-step launch with per-phase timeline stamps, summarised (36 layers unless --layers)")
     args = ap.parse_args()

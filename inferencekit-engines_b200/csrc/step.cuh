@@ -47,7 +47,10 @@ constexpr int ST_SPW = ST_SLICES / ST_WARPS;       // 2 slices per consumer warp
 #ifndef ST_QUAD
 #define ST_QUAD 4                                  // GEMV slices a consumer warp takes at a time
 #endif
-constexpr int ST_NSTAGE = 5;
+#ifndef ST_NSTAGE_N
+#define ST_NSTAGE_N 5                              // ring stages (a tuning knob: the weight stream's depth per SM)
+#endif
+constexpr int ST_NSTAGE = ST_NSTAGE_N;
 constexpr int ST_MAX_K = 12288;
 constexpr int ST_CHUNK = 64;                       // attention keys per item
 constexpr int ST_MAX_SPLITS = 1024;                // contexts up to 64k
@@ -56,7 +59,7 @@ constexpr int ST_MAX_SPLITS = 1024;                // contexts up to 64k
 constexpr int ST_BD_FLOATS = 6144;
 constexpr int ST_MERGE_ROUND = 128;                // splits staged per round of the attention merge
 constexpr int ST_TAIL_FLOATS = 96 * 16;            // StepSmem::tail: the remote block dots of a split unit
-constexpr int ST_ABATCH = 4;                       // attention items processed together (<= ST_NSTAGE)
+constexpr int ST_ABATCH = ST_NSTAGE < 4 ? ST_NSTAGE : 4;   // attention items processed together (<= ST_NSTAGE)
 
 struct StepLayer {
   const uint8_t *w_qkv, *w_o, *w_gu, *w_down;      // model.pack_fp8 layout
@@ -126,6 +129,10 @@ struct StepParams {
 // Word 8: cumulative clock64 cycles consumer warp 0 spent waiting for the slowest warp to release a stage it
 // must fold. Words 9-15: GEMV phases: consumer warps 1-7 leave the stage loop (%globaltimer). Words 16-18 (GEMV
 // phases, consumer warp 0): cycles computing its slice pairs, cycles taking pairs and counting them, pairs taken.
+// GEMV phases with a split unit: 19 the tail fetcher starts copying its remote block dots, 20 the copy is done,
+// 21 the folding warp starts waiting for the copy, 22 it has it; 23 the prologue's input is in shared memory (and,
+// for an RMSNorm, its scale known). Attention phase, thread 0, last batch of items: 9 its K/V stages have landed, 10 q/k/v setup done, 11 scores
+// done, 12 softmax done; merge: 13 merge entered, 14 the KV head's counter complete, 15 split weights ready.
 constexpr int ST_TL_WORDS = 24;
 __device__ __forceinline__ void step_put(const StepParams& p, int phase, int i, unsigned long long v) {
   if (p.tl) p.tl[((size_t)blockIdx.x * (5 * p.n_layers + 1) + phase) * ST_TL_WORDS + i] = v;
@@ -143,7 +150,7 @@ struct StepSmem {
   float xscale[ST_MAX_K / QB];
   union {
     float bd[ST_BD_FLOATS];                        // block dots of the 16-row units in flight (slots)
-    bf16 xs[HIDDEN];                               // raw x during an RMSNorm prologue
+    bf16 xs[ST_MAX_K];                             // x during a prologue
     struct {
       float qs[ST_ABATCH][GQA][HEAD_DIM + 4];      // q per kv head of the batch; +4: 4 heads read conflict-free
       float sc[ST_ABATCH][GQA][ST_CHUNK];          // scores, then probabilities, per item and query head
@@ -162,7 +169,7 @@ struct StepSmem {
   __align__(16) float tail[2][ST_TAIL_FLOATS];
   uint64_t tail_full[2], tail_empty[2];
   int grab;                                        // GEMV phase: slice pairs handed out so far
-  int done[16];                                    // GEMV phase: finished slices per block-dot slot
+  int done[ST_BD_FLOATS / (4 * 16)];               // GEMV phase: finished slices per block-dot slot (K/128 >= 4)
   float red[8];
   unsigned long long bestbuf[ST_WARPS];
   uint64_t full[ST_NSTAGE], empty[ST_NSTAGE];
@@ -340,19 +347,40 @@ struct Producer {
 };
 
 // ---- consumer: GEMV phase ---------------------------------------------------------------------------------------
-template <int EPI, int SCALE, int NG>
+// ONE code path serves every GEMV phase of the step (qkv, o_proj, gate_up, down, lm_head): the matrix shape, the
+// sub-matrix count, the scale layout and the epilogue are run-time fields of GemvPhase, and the step calls
+// gemv_phase from a single site. A layer then executes one copy of the stage loop and of the fold instead of
+// four specialised ones (~25-30 KB of code each), which keeps a layer's code inside the SM's instruction cache.
+constexpr int EPI_TP_PARTIAL = 10;   // fp32 row partial into every rank's TpArea (row-parallel shard)
+
 struct GemvPhase {
-  const float* ws;
+  const float* ws;    // weight scales: [N] per channel, or [N/128][KB] per 128x128 block
   int N, K;           // N = all rows (gate + up for NG = 2)
+  int KB, NG;         // K / 128; sub-matrices per unit (1, or 2 = gate|up)
+  int epi;            // EPI_STORE | EPI_RESIDUAL | EPI_SWIGLU | EPI_ARGMAX | EPI_TP_PARTIAL
+  int scale_block;    // 1: block-128 scales, 0: per channel
   bf16* out;          // STORE: qkv; RESIDUAL: resid; SWIGLU: h; ARGMAX: logits
   float* part;
-  int* counters;
-  int row_offset = 0; // ARGMAX: global id of row 0 (vocabulary shard)
-  int xbuf = 0;       // TP_PARTIAL: exchange buffer (k % 2)
-  unsigned xtag = 0;  // TP_PARTIAL: the exchange's tag
-  unsigned dtag = 0;  // tag of this phase's shared block dots (set by gemv_phase)
+  int row_offset;     // ARGMAX: global id of row 0 (vocabulary shard)
+  int xbuf;           // TP_PARTIAL: exchange buffer (k % 2)
+  unsigned xtag;      // TP_PARTIAL: the exchange's tag
+  unsigned dtag;      // tag of this phase's shared block dots (set by gemv_phase)
+  int nslots;         // block-dot slots of this shape (set by gemv_phase)
 };
-constexpr int EPI_TP_PARTIAL = 10;   // fp32 row partial into every rank's TpArea (row-parallel shard)
+
+// Block-dot slots: unit u uses slot u % nslots, next reused by unit u + nslots, whose first slice lies
+// (nslots - 1) * spu slices past u's last. No warp works more than ST_NSTAGE stages past the oldest stage not yet
+// released, and u's owner folds it at the latest after its next slice group once u is complete, so no writer of
+// u + nslots can come first when this holds (checked for every shape the step runs, TP 1..8):
+__host__ __device__ constexpr bool gemv_slots_ok(int KB, int NG) {
+  return (ST_BD_FLOATS / (KB * 16 * NG) - 1) * KB * NG > (2 * ST_NSTAGE + 2) * ST_SLICES;
+}
+static_assert(gemv_slots_ok(32, 1) && gemv_slots_ok(32, 2) && gemv_slots_ok(96, 1) && gemv_slots_ok(16, 1) &&
+                  gemv_slots_ok(48, 1) && gemv_slots_ok(8, 1) && gemv_slots_ok(24, 1) && gemv_slots_ok(4, 1) &&
+                  gemv_slots_ok(12, 1),
+              "too few block-dot slots");
+static_assert(96 * 16 <= ST_TAIL_FLOATS, "a split unit's remote block dots must fit a tail buffer");
+static_assert(ST_BD_FLOATS / (4 * 16) == sizeof(StepSmem::done) / sizeof(int), "a done counter per block-dot slot");
 
 struct Consumer {
   StepSmem* sm;
@@ -387,10 +415,9 @@ struct Consumer {
   }
 };
 
-// Weight scale of `row` at K block `kb` (both layouts).
-template <int SCALE>
-__device__ __forceinline__ float row_scale(const float* ws, int row, int kb, int KB) {
-  return SCALE == SCALE_CHANNEL ? __ldg(ws + row) : __ldg(ws + (size_t)(row / QB) * KB + kb);
+// Block-128 weight scale of `row` at K block `kb`.
+__device__ __forceinline__ float block_row_scale(const float* ws, int row, int kb, int KB) {
+  return __ldg(ws + (size_t)(row / QB) * KB + kb);
 }
 
 // Per-row inputs of a unit's epilogue that do not depend on this phase's block dots (the channel scale and,
@@ -398,14 +425,12 @@ __device__ __forceinline__ float row_scale(const float* ws, int row, int kb, int
 struct FoldPre {
   float sw, resid;
 };
-template <int EPI, int SCALE, int NG>
-__device__ __forceinline__ FoldPre fold_prefetch(const Consumer& c, const GemvPhase<EPI, SCALE, NG>& ph, int u,
-                                                 bool valid) {
-  const int row = (NG == 2 ? (c.lane >> 4) * (ph.N / 2) : 0) + u * 16 + (c.lane & 15);
-  const bool active = valid && (NG == 2 || c.lane < 16);
+__device__ __forceinline__ FoldPre fold_prefetch(const Consumer& c, const GemvPhase& ph, int u, bool valid) {
+  const int row = (ph.NG == 2 ? (c.lane >> 4) * (ph.N / 2) : 0) + u * 16 + (c.lane & 15);
+  const bool active = valid && (ph.NG == 2 || c.lane < 16);
   FoldPre f;
-  f.sw = (SCALE == SCALE_CHANNEL && active) ? __ldg(ph.ws + row) : 0.f;
-  f.resid = (EPI == EPI_RESIDUAL && active) ? __bfloat162float(ldcg_bf16(ph.out + row)) : 0.f;
+  f.sw = (!ph.scale_block && active) ? __ldg(ph.ws + row) : 0.f;
+  f.resid = (ph.epi == EPI_RESIDUAL && active) ? __bfloat162float(ldcg_bf16(ph.out + row)) : 0.f;
   return f;
 }
 
@@ -453,9 +478,8 @@ struct TailUnit {
   int u, hi, need;
   bool any;
 };
-template <int KB, int NG>
-__device__ __forceinline__ TailUnit tail_unit(int N) {
-  constexpr int spu = KB * NG;
+__device__ __forceinline__ TailUnit tail_unit(int N, int KB, int NG) {
+  const int spu = KB * NG;
   const SliceRange r = slice_range(N / (16 * NG) * spu);
   const int u_lo = r.s0 / spu, u_hi = r.s1 > r.s0 ? (r.s1 - 1) / spu : u_lo - 1;
   TailUnit t{u_hi, r.s1, (u_hi + 1) * spu - r.s1, false};
@@ -468,42 +492,60 @@ __device__ __forceinline__ TailUnit tail_unit(int N) {
 // early in that CTA's phase, into tail[n % 2] and signal tail_full[n % 2] (one arrival per lane). It first
 // waits until the folding warp has used the buffer two phases back. Every wait is bounded; on a timeout the
 // error word is set and the fetch is skipped (the folding warp's own bounded wait then gives up).
-template <int KB, int NG>
-__device__ __forceinline__ void tail_fetch(StepSmem& sm, const StepParams& p, int N, int phase, unsigned epoch,
-                                           int& n, int lane) {
-  constexpr int spu = KB * NG, RPU = 16 * NG;
-  const TailUnit tu = tail_unit<KB, NG>(N);
+__device__ __forceinline__ void tail_fetch(StepSmem& sm, const StepParams& p, int N, int KB, int NG, int phase,
+                                           unsigned epoch, int& n, int lane) {
+  const int spu = KB * NG, RPU = 16 * NG;
+  const TailUnit tu = tail_unit(N, KB, NG);
   if (!tu.any) return;
   const int b = n & 1, use = n >> 1;
   ++n;
   if (use >= 1 && !__all_sync(0xffffffffu, mbar_wait(&sm.tail_empty[b], (uint32_t)((use - 1) & 1)))) return;
   const unsigned long long* src =
       reinterpret_cast<const unsigned long long*>(p.part) + (size_t)tu.u * KB * RPU + (tu.hi - tu.u * spu) * 16;
-  if (copy_tagged_dots(src, sm.tail[b], tu.need * 16, dots_tag(epoch, p.n_layers, phase), lane))
-    mbar_arrive(&sm.tail_full[b]);
+  if (lane == 0) step_stamp(p, phase, 19);
+  const bool ok = copy_tagged_dots(src, sm.tail[b], tu.need * 16, dots_tag(epoch, p.n_layers, phase), lane);
+  if (lane == 0) step_stamp(p, phase, 20);
+  if (ok) mbar_arrive(&sm.tail_full[b]);
+}
+
+// In-order sum over a unit's K blocks, acc += d * s_x * s_w, reading FB block dots at a time (independent loads).
+template <int FB>
+__device__ __forceinline__ float fold_dots(const float* s, int RPU, int KB, const float* xscale, const float* ws,
+                                           int scale_block, int row, float sw_ch) {
+  float a = 0.f;
+  for (int k0 = 0; k0 < KB; k0 += FB) {
+    float d[FB], sw[FB];
+#pragma unroll
+    for (int j = 0; j < FB; ++j) {
+      d[j] = s[(k0 + j) * RPU];
+      sw[j] = scale_block ? block_row_scale(ws, row, k0 + j, KB) : sw_ch;
+    }
+#pragma unroll
+    for (int j = 0; j < FB; ++j) a += d[j] * xscale[k0 + j] * sw[j];
+  }
+  return a;
 }
 
 // Fold of one 16-row unit (32 rows for gate|up) once this CTA's block dots of it are complete: the per-op
 // kernel's in-order sum acc += d * sx * sw over K blocks, then the epilogue. Gate rows fold on lanes 0-15 and
-// up rows on lanes 16-31. A unit shared with a neighbouring CTA is folded by whichever CTA completes it last,
-// from the global scratch. The block dots are read 16 at a time (independent loads), then summed in order.
-template <int KB, int EPI, int SCALE, int NG>
-__device__ __forceinline__ void fold_unit(Consumer& c, const GemvPhase<EPI, SCALE, NG>& ph, const SliceRange& r,
-                                          int u, const FoldPre& pre, int tail_use = -1) {
+// up rows on lanes 16-31. A unit shared with a neighbouring CTA is folded by the CTA holding its first K block,
+// with the following CTA's block dots (tagged words in `part`, copied by the tail-fetcher warp).
+__device__ __forceinline__ void fold_unit(Consumer& c, const GemvPhase& ph, const SliceRange& r, int u,
+                                          const FoldPre& pre, int tail_use = -1) {
   StepSmem& sm = *c.sm;
-  constexpr int RPU = 16 * NG, spu = KB * NG, slot_floats = KB * RPU, nslots = ST_BD_FLOATS / slot_floats;
-  constexpr int FB = KB % 16 == 0 ? 16 : (KB % 8 == 0 ? 8 : 4);   // block dots read per batch
-  static_assert(KB % FB == 0, "fold batches");
-  const int lo = max(u * spu, r.s0), hi = min((u + 1) * spu, r.s1);
+  const int KB = ph.KB, NG = ph.NG, RPU = 16 * NG, spu = KB * NG, slot_floats = KB * RPU;
+  const int hi = min((u + 1) * spu, r.s1);
   if (u * spu < r.s0) return;   // started in an earlier CTA, which folds it (this CTA's dots are in `part`, tagged)
-  float* slot = &sm.u.bd[(u % nslots) * slot_floats];
+  float* slot = &sm.u.bd[(u % ph.nslots) * slot_floats];
   if (hi < (u + 1) * spu) {
     // The unit continues in the following CTA(s), whose share the tail-fetcher warp has copied into tail[use % 2]:
     // a slice is 16 consecutive floats of the unit's [KB][NG][16] layout, so that share goes behind this CTA's.
     const int off = (hi - u * spu) * 16, nf = ((u + 1) * spu - hi) * 16;
     if (tail_use >= 0) {
       const int b = tail_use & 1;
+      if (c.lane == 0) step_stamp(*c.p, c.tl_phase, 21);
       const bool ok = __all_sync(0xffffffffu, mbar_wait(&sm.tail_full[b], (uint32_t)((tail_use >> 1) & 1)));
+      if (c.lane == 0) step_stamp(*c.p, c.tl_phase, 22);
       if (ok)
         for (int i4 = c.lane; i4 < nf / 4; i4 += 32)
           reinterpret_cast<uint4*>(slot + off)[i4] = reinterpret_cast<const uint4*>(sm.tail[b])[i4];
@@ -521,19 +563,12 @@ __device__ __forceinline__ void fold_unit(Consumer& c, const GemvPhase<EPI, SCAL
   float a = 0.f;
   if (active) {
     const float* s = slot + gi * 16 + rr;
-    for (int k0 = 0; k0 < KB; k0 += FB) {
-      float d[FB], sw[FB];
-#pragma unroll
-      for (int j = 0; j < FB; ++j) {
-        d[j] = s[(k0 + j) * RPU];
-        sw[j] = SCALE == SCALE_CHANNEL ? pre.sw : row_scale<SCALE>(ph.ws, row, k0 + j, KB);
-      }
-#pragma unroll
-      for (int j = 0; j < FB; ++j) a += d[j] * sm.xscale[k0 + j] * sw[j];
-    }
+    if (KB % 16 == 0) a = fold_dots<16>(s, RPU, KB, sm.xscale, ph.ws, ph.scale_block, row, pre.sw);
+    else if (KB % 8 == 0) a = fold_dots<8>(s, RPU, KB, sm.xscale, ph.ws, ph.scale_block, row, pre.sw);
+    else a = fold_dots<4>(s, RPU, KB, sm.xscale, ph.ws, ph.scale_block, row, pre.sw);
   }
   const float resid_in = pre.resid;
-  if (EPI == EPI_SWIGLU) {
+  if (ph.epi == EPI_SWIGLU) {
     const float a_up = __shfl_down_sync(0xffffffffu, a, 16);
     if (c.lane < 16) {
       const float gt = bf16r(a);
@@ -542,11 +577,11 @@ __device__ __forceinline__ void fold_unit(Consumer& c, const GemvPhase<EPI, SCAL
       ph.out[row] = __float2bfloat16_rn(act * up);
     }
   } else if (c.lane < 16) {
-    if (EPI == EPI_STORE) {
+    if (ph.epi == EPI_STORE) {
       ph.out[row] = __float2bfloat16_rn(a);
-    } else if (EPI == EPI_RESIDUAL) {
+    } else if (ph.epi == EPI_RESIDUAL) {
       ph.out[row] = __float2bfloat16_rn(resid_in + bf16r(a));
-    } else if (EPI == EPI_TP_PARTIAL) {   // this rank's fp32 partial of the row, to every rank (NVLink stores)
+    } else if (ph.epi == EPI_TP_PARTIAL) {   // this rank's fp32 partial of the row, to every rank (NVLink stores)
       const StepParams& p = *c.p;
       const unsigned long long w = ((unsigned long long)ph.xtag << 32) | __float_as_uint(a);
       for (int r2 = 0; r2 < p.tp; ++r2) st_relaxed_sys_u64(&p.areas[r2]->recv[ph.xbuf][p.tp_rank][row], w);
@@ -559,20 +594,18 @@ __device__ __forceinline__ void fold_unit(Consumer& c, const GemvPhase<EPI, SCAL
   }
 }
 
-template <int KB, int EPI, int SCALE, int NG>      // KB = K / 128 (compile time: slice indexing divides by it)
-__device__ void gemv_phase(Consumer& c, GemvPhase<EPI, SCALE, NG> ph) {
+__device__ void gemv_phase(Consumer& c, GemvPhase ph) {
   StepSmem& sm = *c.sm;
   ph.dtag = dots_tag(c.epoch, c.p->n_layers, c.tl_phase);
-  constexpr int RPU = 16 * NG;                      // rows per unit
-  constexpr int spu = KB * NG;                      // slices per unit
-  constexpr int slot_floats = KB * RPU;
-  constexpr int nslots = ST_BD_FLOATS / slot_floats;
-  // A unit's slot is next used by unit u + nslots, whose first slice lies (nslots - 1) * spu slices past u's last.
-  // No warp works more than ST_NSTAGE stages past the oldest stage not yet released, and u's owner folds it at
-  // the latest after its next slice pair once u is complete, so no writer of u + nslots can come first.
-  static_assert((nslots - 1) * spu > (2 * ST_NSTAGE + 2) * ST_SLICES, "too few block-dot slots");
+  const int KB = ph.KB, NG = ph.NG, ngs = NG - 1;   // NG is 1 or 2: slice q is tile q >> ngs, sub-matrix q & ngs
+  const int RPU = 16 * NG;                          // rows per unit
+  const int spu = KB * NG;                          // slices per unit
+  const int slot_floats = KB * RPU;
+  const int nslots = ST_BD_FLOATS / slot_floats;
+  ph.nslots = nslots;
   constexpr int NQ = ST_SLICES / ST_QUAD;         // grabs per stage
   static_assert(ST_SLICES % ST_QUAD == 0 && ST_WARPS % NQ == 0, "a stage's grabs must add up to its ST_WARPS arrivals");
+  static_assert(ST_QUAD <= 4, "a group of slices spans at most two units (4 <= every K / 128)");
   const int units = ph.N / RPU;
   const SliceRange r = slice_range(units * spu);
   const int nst = (r.s1 - r.s0 + ST_SLICES - 1) / ST_SLICES;   // stages of this phase (as the producer issues)
@@ -588,13 +621,13 @@ __device__ void gemv_phase(Consumer& c, GemvPhase<EPI, SCALE, NG> ph) {
   // slices of unit u that this CTA computes and folds (none for a unit an earlier CTA started, which folds it)
   auto local_count = [&](int u) { return u * spu < r.s0 ? 0 : min((u + 1) * spu, r.s1) - u * spu; };
   FoldPre pre = fold_prefetch(c, ph, fu, fu <= u_hi);
-  const TailUnit tu = tail_unit<KB, NG>(ph.N);
+  const TailUnit tu = tail_unit(ph.N, KB, NG);
   const int tail_use = tu.any ? c.tail_n++ : -1;
   auto fold_ready = [&](int u) { return *reinterpret_cast<volatile int*>(&sm.done[u % nslots]) >= local_count(u); };
   auto fold_next = [&]() {   // fold unit fu, move on to this warp's next unit and prefetch its row inputs
     const long long t0 = clock64();
     __threadfence_block();   // the other warps' block dots, published before their counts
-    fold_unit<KB>(c, ph, r, fu, pre, fu == u_hi ? tail_use : -1);
+    fold_unit(c, ph, r, fu, pre, fu == u_hi ? tail_use : -1);
     __syncwarp();
     if (c.lane == 0) sm.done[fu % nslots] = 0;
     fu += ST_WARPS;
@@ -613,32 +646,39 @@ __device__ void gemv_phase(Consumer& c, GemvPhase<EPI, SCALE, NG> ph) {
     const long long tg1 = clock64();
     if (!c.wait_abs(n0 + i)) atomicOr(&g_dev_error, DEVERR_MBAR_TIMEOUT);
     const long long tc0 = clock64();
-    // slice coordinates (also computed for slices past the range: kb stays in [0, KB), nothing is stored)
-    int q[ST_QUAD], tl[ST_QUAD], un[ST_QUAD], kb[ST_QUAD];
-    uint4 W[ST_QUAD][4], X[ST_QUAD][4];
+    // slice coordinates (also computed for slices past the range: kb stays in [0, KB), nothing is stored): one
+    // division for the group, then steps (the group's tiles are consecutive and KB >= 4 > the step)
+    const int qa = r.s0 + i * ST_SLICES + k0;
+    const int tla = qa >> ngs;
+    const int una = tla / KB, kba = tla - una * KB;
+    const int sla = una % nslots, slb = sla + 1 == nslots ? 0 : sla + 1;   // slots of units una, una + 1
+    int q[ST_QUAD], un[ST_QUAD], kb[ST_QUAD];
+    const uint8_t* wp[ST_QUAD];
+    const uint8_t* xp[ST_QUAD];
 #pragma unroll
     for (int j = 0; j < ST_QUAD; ++j) {
-      q[j] = r.s0 + i * ST_SLICES + k0 + j;
-      tl[j] = q[j] / NG;
-      un[j] = tl[j] / KB;
-      kb[j] = tl[j] - un[j] * KB;
-      const uint8_t* w = sm.ring[(n0 + i) % ST_NSTAGE] + (k0 + j) * ST_SLICE + c.lane * 16;
-      const uint8_t* x = xh + kb[j] * 256 + c.t * 16;
-#pragma unroll
-      for (int ch = 0; ch < 4; ++ch) {
-        W[j][ch] = *reinterpret_cast<const uint4*>(w + ch * 512);
-        X[j][ch] = *reinterpret_cast<const uint4*>(x + ch * 64);
-      }
+      q[j] = qa + j;
+      const int kk = kba + ((q[j] >> ngs) - tla);
+      un[j] = kk >= KB ? una + 1 : una;
+      kb[j] = kk >= KB ? kk - KB : kk;
+      wp[j] = sm.ring[(n0 + i) % ST_NSTAGE] + (k0 + j) * ST_SLICE + c.lane * 16;
+      xp[j] = xh + kb[j] * 256 + c.t * 16;
     }
     float d0[ST_QUAD], d1[ST_QUAD];
 #pragma unroll
     for (int j = 0; j < ST_QUAD; ++j) d0[j] = d1[j] = 0.f;
 #pragma unroll
-    for (int ch = 0; ch < 4; ++ch) {
+    for (int ch = 0; ch < 4; ++ch) {   // 32-k chunk ch of the group's slices (16-byte fragments per lane)
+      uint4 W[ST_QUAD], X[ST_QUAD];
+#pragma unroll
+      for (int j = 0; j < ST_QUAD; ++j) {
+        W[j] = *reinterpret_cast<const uint4*>(wp[j] + ch * 512);
+        X[j] = *reinterpret_cast<const uint4*>(xp[j] + ch * 64);
+      }
 #pragma unroll
       for (int j = 0; j < ST_QUAD; ++j) {
         float e[4];
-        fp8_chunk_dot(W[j][ch], X[j][ch], e);
+        fp8_chunk_dot(W[j], X[j], e);
         d0[j] += e[0];
         d1[j] += e[2];
       }
@@ -646,13 +686,13 @@ __device__ void gemv_phase(Consumer& c, GemvPhase<EPI, SCALE, NG> ph) {
 #pragma unroll
     for (int j = 0; j < ST_QUAD; ++j) {
       if (q[j] < r.s1) {
-        const int gi = q[j] - tl[j] * NG;                       // sub-matrix of the slice (0 for NG == 1)
+        const int gi = q[j] & ngs;                              // sub-matrix of the slice (0 for NG == 1)
         const int u = un[j];
         const bool in = u * spu >= r.s0;                        // this CTA folds u: keep its dots here
         if (c.t == 0) {
           const int off = kb[j] * RPU + gi * 16 + c.g;
           if (in) {
-            float* dst = &sm.u.bd[(u % nslots) * slot_floats + off];
+            float* dst = &sm.u.bd[(u == una ? sla : slb) * slot_floats + off];
             dst[0] = d0[j];
             dst[8] = d1[j];
           } else {   // the earlier CTA folds u: publish the dots tagged (no fence or counter needed)
@@ -667,21 +707,18 @@ __device__ void gemv_phase(Consumer& c, GemvPhase<EPI, SCALE, NG> ph) {
     const long long tc1 = clock64();
     __syncwarp();
     if (c.lane == 0) {
-      __threadfence_block();   // this pair's block dots before its counts
+      __threadfence_block();   // this group's block dots before its counts
       // the group's slices by unit (consecutive slices: at most two units), one count per unit
-      int cu = -1, cn = 0;
+      int na = 0, nb = 0;
 #pragma unroll
       for (int j = 0; j < ST_QUAD; ++j) {
         if (q[j] < r.s1 && un[j] * spu >= r.s0) {
-          if (un[j] != cu) {
-            if (cn) atomicAdd(&sm.done[cu % nslots], cn);
-            cu = un[j];
-            cn = 0;
-          }
-          ++cn;
+          if (un[j] == una) ++na;
+          else ++nb;
         }
       }
-      if (cn) atomicAdd(&sm.done[cu % nslots], cn);
+      if (na) atomicAdd(&sm.done[sla], na);
+      if (nb) atomicAdd(&sm.done[slb], nb);
       mbar_arrive_n(&sm.empty[(n0 + i) % ST_NSTAGE], ST_WARPS / NQ);
     }
     __syncwarp();
@@ -717,45 +754,39 @@ __device__ void gemv_phase(Consumer& c, GemvPhase<EPI, SCALE, NG> ph) {
 }
 
 // ---- consumer: activation prologue ---------------------------------------------------------------------------
-// x (global, K values) -> optional RMSNorm (reference 128-thread reduction order) -> e4m3 per 128-group ->
-// f16 fragments in sm.xh + scales in sm.xscale. `embed_row` (layer 0): x is that row of the embedding table
-// and this CTA also writes its slice of it into the residual stream.
-template <bool NORM>
+// x (global, K values) -> RMSNorm when norm_w is given (K == 4096; the reference's 128-thread reduction order) ->
+// e4m3 per 128-group -> f16 fragments in sm.xh + scales in sm.xscale. x is read through L2 (other CTAs wrote it),
+// every load in flight at once, and staged in shared memory: by the whole CTA for an RMSNorm (every thread needs
+// the sum of squares), else by each warp for its own groups, so that only the warp waits. `resid_slice_dst`
+// (layer 0): x is the token's embedding row and this CTA also writes its slice of it into the residual stream.
 __device__ void step_prologue(Consumer& c, const bf16* x, const bf16* norm_w, int K, float eps, bf16* resid_slice_dst) {
   StepSmem& sm = *c.sm;
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = c.lane, warp = c.warp;
   const int KB = K / QB;
+  constexpr int NT = ST_WARPS * 32;
   if (tid == 0) sm.grab = 0;   // every warp left the previous GEMV phase (a grid barrier lies between)
-  constexpr int MAXG = ST_MAX_K / QB / ST_WARPS;   // 128-groups per warp at most (12)
-  // Issue every global load of the prologue at once (one L2 round trip instead of one per group).
-  uint2 raw[MAXG], nraw[NORM ? MAXG : 1];
-#pragma unroll
-  for (int i = 0; i < MAXG; ++i) {
-    const int gq = c.warp + i * ST_WARPS;
-    if (gq < KB) {
-      const int k0 = gq * QB + c.lane * 4;
-      if (NORM) nraw[i] = *reinterpret_cast<const uint2*>(norm_w + k0);
-      else raw[i] = ldcg_u2(x + k0);
-    }
-  }
+  uint4* xs4 = reinterpret_cast<uint4*>(sm.u.xs);
+  const uint4* x4 = reinterpret_cast<const uint4*>(x);
   float rstd = 0.f;
-  if (NORM) {   // K == 4096: stage x in shared memory
+  uint2 nraw[4];   // RMSNorm: the norm weights of this lane's 4 values in each of the warp's 4 groups
+  if (norm_w) {   // every thread loads two 8-value chunks (K == 4096), all loads in flight at once
     uint4 xv[2];
 #pragma unroll
-    for (int i = 0; i < 2; ++i) xv[i] = ldcg_u4(x + (tid + i * ST_WARPS * 32) * 8);
+    for (int i = 0; i < 2; ++i) xv[i] = ldcg_u4(x4 + tid + i * NT);
 #pragma unroll
-    for (int i = 0; i < 2; ++i) reinterpret_cast<uint4*>(sm.u.xs)[tid + i * ST_WARPS * 32] = xv[i];
+    for (int i = 0; i < 4; ++i) nraw[i] = __ldg(reinterpret_cast<const uint2*>(norm_w + (warp + i * ST_WARPS) * QB) + lane);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) xs4[tid + i * NT] = xv[i];
     consumer_sync();
     if (resid_slice_dst) {
       const int per = (K / 8 + gridDim.x - 1) / gridDim.x;
       const int lo = blockIdx.x * per, hi = min(lo + per, K / 8);
-      for (int i = lo + tid; i < hi; i += ST_WARPS * 32)
-        reinterpret_cast<uint4*>(resid_slice_dst)[i] = reinterpret_cast<const uint4*>(sm.u.xs)[i];
+      for (int i = lo + tid; i < hi; i += NT) reinterpret_cast<uint4*>(resid_slice_dst)[i] = xs4[i];
     }
     if (tid < 128) {
       float ss = 0.f;
       for (int i = tid; i < K / 8; i += 128) {
-        const uint4 v = reinterpret_cast<const uint4*>(sm.u.xs)[i];
+        const uint4 v = xs4[i];
         const bf16* e = reinterpret_cast<const bf16*>(&v);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
@@ -764,39 +795,59 @@ __device__ void step_prologue(Consumer& c, const bf16* x, const bf16* norm_w, in
         }
       }
       ss = warp_sum(ss);
-      if (c.lane == 0) sm.red[c.warp] = ss;
+      if (lane == 0) sm.red[warp] = ss;
     }
     consumer_sync();
     float tot = 0.f;
 #pragma unroll
     for (int i = 0; i < 4; ++i) tot += sm.red[i];
     rstd = rsqrtf(tot / (float)K + eps);
-  }
-  const int ch = c.lane >> 3, hi = (c.lane >> 2) & 1, t = c.lane & 3;
+  } else {   // each warp loads its own groups gq = warp + 8 i (up to 12), all at once, into its part of xs
+    constexpr int MAXG = ST_MAX_K / QB / ST_WARPS;
+    uint2 raw[MAXG];
 #pragma unroll
-  for (int i = 0; i < MAXG; ++i) {
-    const int gq = c.warp + i * ST_WARPS;
-    if (gq >= KB) break;
-    const int k0 = gq * QB + c.lane * 4;
-    if (NORM) raw[i] = *reinterpret_cast<const uint2*>(sm.u.xs + k0);
-    const bf16* e = reinterpret_cast<const bf16*>(&raw[i]);
-    float v[4];
-    if (NORM) {
-      const bf16* we = reinterpret_cast<const bf16*>(&nraw[i]);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) v[j] = bf16r(__bfloat162float(we[j]) * bf16r(__bfloat162float(e[j]) * rstd));
-    } else {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) v[j] = __bfloat162float(e[j]);
+    for (int i = 0; i < MAXG; ++i) {
+      const int gq = warp + i * ST_WARPS;
+      if (gq < KB) raw[i] = ldcg_u2(x + gq * QB + lane * 4);
     }
-    float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
-    amax = warp_max(amax);
-    const float sc = div_full(amax, 448.0f);
-    const uint32_t qv = quant4(v[0], v[1], v[2], v[3], sc);
-    uint32_t* dst = sm.xh + ((gq * 4 + ch) * 4 + t) * 4;
-    dst[hi] = e4m3x2_to_f16x2(qv);
-    dst[2 + hi] = e4m3x2_to_f16x2(qv >> 16);
-    if (c.lane == 0) sm.xscale[gq] = sc;
+#pragma unroll
+    for (int i = 0; i < MAXG; ++i) {
+      const int gq = warp + i * ST_WARPS;
+      if (gq < KB) *reinterpret_cast<uint2*>(sm.u.xs + gq * QB + lane * 4) = raw[i];
+    }
+    __syncwarp();
+  }
+  if (tid == 0 && c.p->tl) step_stamp(*c.p, c.tl_phase, 23);
+  const int ch = lane >> 3, hi = (lane >> 2) & 1, t = lane & 3;
+  for (int g0 = warp; g0 < KB; g0 += 4 * ST_WARPS) {   // 4 groups at a time (independent chains)
+    float v[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int gq = g0 + i * ST_WARPS;
+      const uint2 raw = gq < KB ? *reinterpret_cast<const uint2*>(sm.u.xs + gq * QB + lane * 4) : make_uint2(0, 0);
+      v[i][0] = bf16lo(raw.x);
+      v[i][1] = bf16hi(raw.x);
+      v[i][2] = bf16lo(raw.y);
+      v[i][3] = bf16hi(raw.y);
+      if (norm_w) {   // K == 4096: a single batch, so nraw[i] is group gq's
+        const float w[4] = {bf16lo(nraw[i].x), bf16hi(nraw[i].x), bf16lo(nraw[i].y), bf16hi(nraw[i].y)};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[i][j] = bf16r(w[j] * bf16r(v[i][j] * rstd));
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int gq = g0 + i * ST_WARPS;
+      if (gq >= KB) break;
+      float amax = fmaxf(fmaxf(fabsf(v[i][0]), fabsf(v[i][1])), fmaxf(fabsf(v[i][2]), fabsf(v[i][3])));
+      amax = warp_max(amax);
+      const float sc = div_full(amax, 448.0f);
+      const uint32_t qv = quant4(v[i][0], v[i][1], v[i][2], v[i][3], sc);
+      uint32_t* dst = sm.xh + ((gq * 4 + ch) * 4 + t) * 4;
+      dst[hi] = e4m3x2_to_f16x2(qv);
+      dst[2 + hi] = e4m3x2_to_f16x2(qv >> 16);
+      if (lane == 0) sm.xscale[gq] = sc;
+    }
   }
   consumer_sync();
 }
@@ -826,48 +877,46 @@ __device__ void attention_phase(Consumer& c, const StepLayer& L, int l, int pos)
     bool ok = true;
     for (int k = 0; k < nb; ++k) ok = c.wait_abs(c.n + k) && ok;
     if (!ok) atomicOr(&g_dev_error, DEVERR_MBAR_TIMEOUT);
+    const bool tl = p.tl != nullptr && tid == 0;
+    if (tl) step_stamp(p, c.tl_phase, 9);
     auto stage = [&](int k) { return sm.ring[(c.n + k) % ST_NSTAGE]; };
     // setup tasks, one warp each: q of every query head of the batch's kv heads (RMSNorm + RoPE), and the new
     // K row (RMSNorm + RoPE) and V row of every kv head whose last split is in the batch
     const int n_tasks = 4 * nkv + 2 * nkv;
     for (int t = warp; t < n_tasks; t += ST_WARPS) {
-      if (t < 4 * nkv) {
-        const int slot = t >> 2, qh = t & 3;
-        const uint2 raw = ldcg_u2(p.qkv + ((kv0 + slot) * GQA + qh) * HEAD_DIM + lane * 4);
-        const bf16* e = reinterpret_cast<const bf16*>(&raw);
-        float v[4] = {__bfloat162float(e[0]), __bfloat162float(e[1]), __bfloat162float(e[2]), __bfloat162float(e[3])};
-        float o[4];
-        head_norm_rope(v, L.q_norm, cos_row, sin_row, lane, p.eps, o);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) sm.u.at.qs[slot][qh][lane * 4 + j] = bf16r(o[j]);
-      } else {
-        const int kvh = kv0 + ((t - 4 * nkv) >> 1), is_v = (t - 4 * nkv) & 1;
-        const int k = kvh * it.n_splits + last_split - b0;     // batch index of the item owning pos
-        if (k < 0 || k >= nb) continue;
-        const int jn = pos - last_split * ST_CHUNK;
-        uint8_t* st = stage(k) + (is_v ? ST_STAGE / 2 : 0);
-        if (!is_v) {
-          const uint2 raw = ldcg_u2(p.qkv + (NQ + kvh) * HEAD_DIM + lane * 4);
-          const bf16* e = reinterpret_cast<const bf16*>(&raw);
-          float v[4] = {__bfloat162float(e[0]), __bfloat162float(e[1]), __bfloat162float(e[2]), __bfloat162float(e[3])};
-          float o[4];
-          head_norm_rope(v, L.k_norm, cos_row, sin_row, lane, p.eps, o);
-          bf16* dst = k_cache + ((size_t)kvh * p.max_seq + pos) * HEAD_DIM + lane * 4;
-          bf16* sdst = reinterpret_cast<bf16*>(st + kv_swz(jn, lane * 4));
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            dst[j] = __float2bfloat16_rn(o[j]);
-            sdst[j] = __float2bfloat16_rn(o[j]);
-          }
-        } else {
-          const uint2 raw = ldcg_u2(p.qkv + (NQ + NKV + kvh) * HEAD_DIM + lane * 4);
-          *reinterpret_cast<uint2*>(v_cache + ((size_t)kvh * p.max_seq + pos) * HEAD_DIM + lane * 4) = raw;
-          *reinterpret_cast<uint2*>(st + kv_swz(jn, lane * 4)) = raw;
-        }
+      const bool is_q = t < 4 * nkv;
+      const int kvh = kv0 + ((t - 4 * nkv) >> 1), is_v = is_q ? 0 : (t - 4 * nkv) & 1;
+      const int k = kvh * it.n_splits + last_split - b0;     // K/V tasks: batch index of the item owning pos
+      if (!is_q && (k < 0 || k >= nb)) continue;
+      const int row = is_q ? (kv0 + (t >> 2)) * GQA + (t & 3) : (is_v ? NQ + NKV : NQ) + kvh;   // qkv head row
+      const uint2 raw = ldcg_u2(p.qkv + row * HEAD_DIM + lane * 4);
+      const int jn = pos - last_split * ST_CHUNK;
+      uint8_t* st = is_q ? nullptr : stage(k) + (is_v ? ST_STAGE / 2 : 0);
+      if (is_v) {
+        *reinterpret_cast<uint2*>(v_cache + ((size_t)kvh * p.max_seq + pos) * HEAD_DIM + lane * 4) = raw;
+        *reinterpret_cast<uint2*>(st + kv_swz(jn, lane * 4)) = raw;
         fence_proxy_async_smem();   // this stage is refilled by TMA (async proxy) after its release
+        continue;
+      }
+      float v[4] = {bf16lo(raw.x), bf16hi(raw.x), bf16lo(raw.y), bf16hi(raw.y)};
+      float o[4];
+      head_norm_rope(v, is_q ? L.q_norm : L.k_norm, cos_row, sin_row, lane, p.eps, o);
+      if (is_q) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) sm.u.at.qs[t >> 2][t & 3][lane * 4 + j] = bf16r(o[j]);
+      } else {
+        bf16* dst = k_cache + ((size_t)kvh * p.max_seq + pos) * HEAD_DIM + lane * 4;
+        bf16* sdst = reinterpret_cast<bf16*>(st + kv_swz(jn, lane * 4));
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          dst[j] = __float2bfloat16_rn(o[j]);
+          sdst[j] = __float2bfloat16_rn(o[j]);
+        }
+        fence_proxy_async_smem();
       }
     }
     consumer_sync();
+    if (tl) step_stamp(p, c.tl_phase, 10);
     // scores: thread (item k = tid / 64, key j = tid % 64), all 4 query heads: dims 0..63 and 64..127 each
     // summed in order, then added. Each K chunk is loaded and converted once for the 4 heads; the q values
     // are the same for the whole warp (broadcast reads).
@@ -913,6 +962,7 @@ __device__ void attention_phase(Consumer& c, const StepLayer& L, int l, int pos)
       }
     }
     consumer_sync();
+    if (tl) step_stamp(p, c.tl_phase, 11);
     // softmax over each (item, head) row, one warp per row
     for (int r = warp; r < nb * GQA; r += ST_WARPS) {
       float* row = sm.u.at.sc[r >> 2][r & 3];
@@ -928,6 +978,7 @@ __device__ void attention_phase(Consumer& c, const StepLayer& L, int l, int pos)
       if (lane == 0) { sm.u.at.m_s[r >> 2][r & 3] = m; sm.u.at.l_s[r >> 2][r & 3] = lsum; }
     }
     consumer_sync();
+    if (tl) step_stamp(p, c.tl_phase, 12);
     // P @ V: warps 2k, 2k+1 take item k; thread = dims d, d + 1 of all 4 heads; each output sums over the keys
     // in order (the reference's sequential loop). Keys go in groups of 8, for which the swizzled offsets of
     // this thread's dims are fixed (they depend on key & 7 only).
@@ -1013,6 +1064,8 @@ __device__ void merge_phase(Consumer& c, int l, int pos) {
   const int tid = threadIdx.x, lane = c.lane, warp = c.warp;
   const int qh = blockIdx.x >> 2, d0 = (blockIdx.x & 3) * 32;
   const int n_splits = (pos + 1 + ST_CHUNK - 1) / ST_CHUNK;
+  const bool tl = p.tl != nullptr && tid == 0;
+  if (tl) step_stamp(p, c.tl_phase, 13);
   if (tid == 0) {   // every split of the KV head has been counted (this layer: l + 1 rounds of n_splits)
     const unsigned* ctr = reinterpret_cast<const unsigned*>(p.attn_counters + qh / GQA);
     const unsigned target = (unsigned)((l + 1) * n_splits);
@@ -1028,6 +1081,7 @@ __device__ void merge_phase(Consumer& c, int l, int pos) {
     }
   }
   consumer_sync();
+  if (tl) step_stamp(p, c.tl_phase, 14);
   float* cw = sm.u.mg.w;
   if (warp == 0) {
     const float* ml = p.ml_part + (size_t)qh * p.max_splits * 2;
@@ -1043,6 +1097,7 @@ __device__ void merge_phase(Consumer& c, int l, int pos) {
     lsum = warp_sum(lsum);
     if (lane == 0) sm.u.mg.cl = lsum;
   }
+  if (tl) step_stamp(p, c.tl_phase, 15);
   float o = 0.f;
   const float* op = p.o_part + (size_t)qh * p.max_splits * HEAD_DIM + d0;
   for (int s0 = 0; s0 < n_splits; s0 += ST_MERGE_ROUND) {
@@ -1185,7 +1240,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) decode_step_kernel(const __grid
       mbar_init(&sm.empty[s], ST_WARPS);
     }
     sm.grab = 0;
-    for (int i = 0; i < 16; ++i) sm.done[i] = 0;
+    for (int i = 0; i < ST_BD_FLOATS / (4 * 16); ++i) sm.done[i] = 0;
     for (int b = 0; b < 2; ++b) {
       mbar_init(&sm.tail_full[b], 32);   // the fetcher's 32 lanes, each after its words are in shared memory
       mbar_init(&sm.tail_empty[b], 1);
@@ -1194,51 +1249,55 @@ __global__ void __launch_bounds__(ST_THREADS, 1) decode_step_kernel(const __grid
   }
   __syncthreads();
   constexpr int H = HIDDEN, I = 12288 / TP, QKV_N = 6144 / TP, NKV = 8 / TP, NQ = 32 / TP, KO = HIDDEN / TP;
+  // The step's GEMV phases in order: g = 4 l + k for layer l (k: 0 qkv, 1 o_proj, 2 gate_up, 3 down), then the
+  // FP8 lm_head as g = 4 n_layers. Producer, tail fetcher and consumers walk this list with one call site each.
+  const int n_gemv = 4 * p.n_layers + (HEAD_BF16 ? 0 : 1);
+  auto gemv_timeline_phase = [&](int g) { return (g >> 2) == p.n_layers ? 5 * p.n_layers : 5 * (g >> 2) + ((g & 3) == 0 ? 0 : (g & 3) + 1); };
   if (warp >= ST_WARPS) {   // ---------------- producer ----------------
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(ST_PRODUCER_REGS) : "memory");
     if (warp == ST_WARPS && lane == 0) {
       Producer pr{&sm, 0, policy_evict_first(), true, 0};
       const AttnItems it = attn_items(pos, NKV);
-      for (int l = 0; l < p.n_layers; ++l) {
-        const StepLayer& L = p.layers[l];
-        step_stamp(p, 5 * l + 0, 3);
-        step_put(p, 5 * l + 0, 6, pr.wait_cycles);
-        pr.gemv(L.w_qkv, (QKV_N / 16) * (H / QB));
-        step_stamp(p, 5 * l + 1, 3);
-        step_put(p, 5 * l + 1, 6, pr.wait_cycles);
-        for (int item = it.i0; item < it.i1; ++item) {
-          const int kvh = item / it.n_splits, split = item - kvh * it.n_splits;
-          pr.push_kv(p, l, kvh, split * ST_CHUNK);
+      for (int g = 0; g < n_gemv; ++g) {
+        const int l = g >> 2, k = g & 3, ph = gemv_timeline_phase(g);
+        step_stamp(p, ph, 3);
+        step_put(p, ph, 6, pr.wait_cycles);
+        if (l == p.n_layers) {
+          pr.gemv(p.w_head, (p.vocab / 16) * (H / QB));
+          break;
         }
-        step_stamp(p, 5 * l + 2, 3);
-        step_put(p, 5 * l + 2, 6, pr.wait_cycles);
-        pr.gemv(L.w_o, (H / 16) * (KO / QB));
-        step_stamp(p, 5 * l + 3, 3);
-        step_put(p, 5 * l + 3, 6, pr.wait_cycles);
-        pr.gemv(L.w_gu, (2 * I / 16) * (H / QB));
-        step_stamp(p, 5 * l + 4, 3);
-        step_put(p, 5 * l + 4, 6, pr.wait_cycles);
-        pr.gemv(L.w_down, (H / 16) * (I / QB));
+        const StepLayer& L = p.layers[l];
+        const uint8_t* w = k == 0 ? L.w_qkv : k == 1 ? L.w_o : k == 2 ? L.w_gu : L.w_down;
+        const int n_slices = k == 0 ? (QKV_N / 16) * (H / QB)
+                             : k == 1 ? (H / 16) * (KO / QB)
+                             : k == 2 ? (2 * I / 16) * (H / QB)
+                                      : (H / 16) * (I / QB);
+        pr.gemv(w, n_slices);
+        if (k == 0) {   // the layer's attention items follow its qkv
+          step_stamp(p, 5 * l + 1, 3);
+          step_put(p, 5 * l + 1, 6, pr.wait_cycles);
+          for (int item = it.i0; item < it.i1; ++item) {
+            const int kvh = item / it.n_splits, split = item - kvh * it.n_splits;
+            pr.push_kv(p, l, kvh, split * ST_CHUNK);
+          }
+        }
       }
-      step_stamp(p, 5 * p.n_layers, 3);
-      step_put(p, 5 * p.n_layers, 6, pr.wait_cycles);
       if (HEAD_BF16) {   // 4 bf16 rows per stage
+        step_stamp(p, 5 * p.n_layers, 3);
+        step_put(p, 5 * p.n_layers, 6, pr.wait_cycles);
         const SliceRange hr = head_rows(p.vocab);
         for (int row = hr.s0; row < hr.s1; row += ST_HEAD_ROWS)
           pr.push(p.w_head + (size_t)row * HIDDEN * 2, (uint32_t)(min(ST_HEAD_ROWS, hr.s1 - row) * HIDDEN * 2));
-      } else {
-        pr.gemv(p.w_head, (p.vocab / 16) * (H / QB));
       }
     } else if (warp == ST_WARPS + 1) {   // tail fetcher: the split units' remote block dots, phase by phase
       const unsigned epoch = __ldcg(p.sync + 2);
       int n = 0;
-      for (int l = 0; l < p.n_layers; ++l) {
-        tail_fetch<H / QB, 1>(sm, p, QKV_N, 5 * l + 0, epoch, n, lane);
-        tail_fetch<KO / QB, 1>(sm, p, H, 5 * l + 2, epoch, n, lane);
-        tail_fetch<H / QB, 2>(sm, p, 2 * I, 5 * l + 3, epoch, n, lane);
-        tail_fetch<I / QB, 1>(sm, p, H, 5 * l + 4, epoch, n, lane);
+      for (int g = 0; g < n_gemv; ++g) {
+        const int k = (g >> 2) == p.n_layers ? 0 : g & 3;
+        const int N = (g >> 2) == p.n_layers ? p.vocab : k == 0 ? QKV_N : k == 2 ? 2 * I : H;
+        const int KB = k == 1 ? KO / QB : k == 3 ? I / QB : H / QB;
+        tail_fetch(sm, p, N, KB, k == 2 ? 2 : 1, gemv_timeline_phase(g), epoch, n, lane);
       }
-      if (!HEAD_BF16) tail_fetch<H / QB, 1>(sm, p, p.vocab, 5 * p.n_layers, epoch, n, lane);
     }
     return;
   }
@@ -1256,83 +1315,65 @@ __global__ void __launch_bounds__(ST_THREADS, 1) decode_step_kernel(const __grid
   unsigned xk = 0;                                  // exchange index within this launch
   // residual buffer k: exchange k reads rbuf(k) and writes rbuf(k + 1) (TP = 1: one buffer, updated in place)
   auto rbuf = [&](unsigned k) -> bf16* { return (TP > 1 && (k & 1)) ? p.resid_alt : p.resid; };
-  for (int l = 0; l < p.n_layers; ++l) {
-    const StepLayer& L = p.layers[l];
-    const int ph = 5 * l;
-    // QKV (TP: after the previous layer's down exchange, the residual update happens here)
+  for (int g = 0; g < n_gemv; ++g) {
+    const int l = g >> 2, k = g & 3, ph = gemv_timeline_phase(g);
+    const bool head = l == p.n_layers;
+    const StepLayer& L = p.layers[head ? 0 : l];
+    // the phase's input: QKV RMSNorm(resid) (layer 0: the token's embedding row, also copied into resid); O the
+    // attention output; GU RMSNorm(resid); DOWN the SwiGLU output; HEAD the final RMSNorm of resid. TP: after a
+    // row-parallel phase's exchange the residual lives in the other buffer.
+    const bf16* x = k == 1 ? p.attn : k == 3 ? p.h : rbuf(xk);
+    const bf16* nw = head ? p.final_norm : k == 0 ? L.ln1 : k == 2 ? L.ln2 : nullptr;
+    bf16* embed_dst = nullptr;
+    if (g == 0) {
+      x = p.embed + (size_t)(tok_ok ? tok : 0) * H;
+      embed_dst = p.resid;
+    }
+    const bool row_par = !head && (k == 1 || k == 3);   // o_proj, down: residual add (TP: fp32 partials)
+    GemvPhase d{};
+    d.K = k == 1 ? KO : k == 3 ? I : H;
+    d.KB = d.K / QB;
+    d.NG = !head && k == 2 ? 2 : 1;
+    d.N = head ? p.vocab : k == 0 ? QKV_N : k == 2 ? 2 * I : H;
+    d.ws = head ? p.s_head : k == 0 ? L.s_qkv : k == 1 ? L.s_o : k == 2 ? L.s_gu : L.s_down;
+    d.scale_block = !head && SCALE == SCALE_BLOCK;
+    d.epi = head ? EPI_ARGMAX : k == 0 ? EPI_STORE : k == 2 ? EPI_SWIGLU : (TP == 1 ? EPI_RESIDUAL : EPI_TP_PARTIAL);
+    d.out = head ? p.logits : k == 0 ? p.qkv : k == 2 ? p.h : (TP == 1 ? p.resid : nullptr);
+    d.part = p.part;
+    d.row_offset = head ? p.vocab_offset : 0;
+    d.xbuf = (int)(xk % 2);
+    d.xtag = (unsigned)(x_base + xk + 1);
     if (tl) step_stamp(p, ph, 0);
-    if (l == 0) step_prologue<true>(c, p.embed + (size_t)(tok_ok ? tok : 0) * H, L.ln1, H, p.eps, p.resid);
-    else step_prologue<true>(c, rbuf(xk), L.ln1, H, p.eps, nullptr);
-    if (tl) step_stamp(p, ph, 1);
     c.tl_phase = ph;
-    gemv_phase<32>(c, GemvPhase<EPI_STORE, SCALE, 1>{L.s_qkv, QKV_N, H, p.qkv, p.part, p.counters});
+    step_prologue(c, x, nw, d.K, p.eps, embed_dst);
+    if (tl) step_stamp(p, ph, 1);
+    gemv_phase(c, d);
     if (tl) { step_put(p, ph, 4, c.wait_cycles); step_put(p, ph, 5, c.fold_cycles); }
+    if (head) break;
+    if (TP > 1 && row_par) {   // the tags tell a reducer when every rank's partial of its row has arrived
+      tp_reduce(p, rbuf(xk), rbuf(xk + 1), (int)(xk % 2), (unsigned)(x_base + xk + 1));
+      ++xk;
+    }
     grid_barrier(p.sync, nbar++, step_word(p, ph, 2));
-    // ATTN: split partials (and the K/V rows at pos), then the merge into the attention output
-    if (tl) step_stamp(p, ph + 1, 0);
-    attention_phase<NKV>(c, L, l, pos);
-    if (tl) step_stamp(p, ph + 1, 7);
-    attention_arrive<NKV>(p, pos);
-    merge_phase<NQ>(c, l, pos);
-    if (tl) step_stamp(p, ph + 1, 1);
-    if (tl) { step_put(p, ph + 1, 4, c.wait_cycles); step_put(p, ph + 1, 5, c.fold_cycles); }
-    grid_barrier(p.sync, nbar++, step_word(p, ph + 1, 2));
-    // O: resid += W_o . quant(attn)   (TP: this rank's fp32 partial, exchanged)
-    if (tl) step_stamp(p, ph + 2, 0);
-    step_prologue<false>(c, p.attn, nullptr, KO, p.eps, nullptr);
-    if (tl) step_stamp(p, ph + 2, 1);
-    c.tl_phase = ph + 2;
-    if (TP == 1) {
-      gemv_phase<KO / QB>(c, GemvPhase<EPI_RESIDUAL, SCALE, 1>{L.s_o, H, KO, p.resid, p.part, p.counters});
-    } else {
-      gemv_phase<KO / QB>(c, GemvPhase<EPI_TP_PARTIAL, SCALE, 1>{L.s_o, H, KO, nullptr, p.part, p.counters, 0,
-                                                                 (int)(xk % 2), (unsigned)(x_base + xk + 1)});
+    if (k == 0) {   // ATTN: split partials (and the K/V rows at pos), then the merge into the attention output
+      if (tl) step_stamp(p, ph + 1, 0);
+      c.tl_phase = ph + 1;
+      attention_phase<NKV>(c, L, l, pos);
+      if (tl) step_stamp(p, ph + 1, 7);
+      attention_arrive<NKV>(p, pos);
+      merge_phase<NQ>(c, l, pos);
+      if (tl) step_stamp(p, ph + 1, 1);
+      if (tl) { step_put(p, ph + 1, 4, c.wait_cycles); step_put(p, ph + 1, 5, c.fold_cycles); }
+      grid_barrier(p.sync, nbar++, step_word(p, ph + 1, 2));
     }
-    if (tl) { step_put(p, ph + 2, 4, c.wait_cycles); step_put(p, ph + 2, 5, c.fold_cycles); }
-    if (TP > 1) {   // the tags tell a reducer when every rank's partial of its row has arrived
-      tp_reduce(p, rbuf(xk), rbuf(xk + 1), (int)(xk % 2), (unsigned)(x_base + xk + 1));
-      ++xk;
-    }
-    grid_barrier(p.sync, nbar++, step_word(p, ph + 2, 2));
-    // GU: h = SwiGLU(W_gu . quant(RMSNorm(resid)))
-    if (tl) step_stamp(p, ph + 3, 0);
-    step_prologue<true>(c, rbuf(xk), L.ln2, H, p.eps, nullptr);
-    if (tl) step_stamp(p, ph + 3, 1);
-    c.tl_phase = ph + 3;
-    gemv_phase<32>(c, GemvPhase<EPI_SWIGLU, SCALE, 2>{L.s_gu, 2 * I, H, p.h, p.part, p.counters});
-    if (tl) { step_put(p, ph + 3, 4, c.wait_cycles); step_put(p, ph + 3, 5, c.fold_cycles); }
-    grid_barrier(p.sync, nbar++, step_word(p, ph + 3, 2));
-    // DOWN: resid += W_down . quant(h)   (TP: partial, exchanged)
-    if (tl) step_stamp(p, ph + 4, 0);
-    step_prologue<false>(c, p.h, nullptr, I, p.eps, nullptr);
-    if (tl) step_stamp(p, ph + 4, 1);
-    c.tl_phase = ph + 4;
-    if (TP == 1) {
-      gemv_phase<I / QB>(c, GemvPhase<EPI_RESIDUAL, SCALE, 1>{L.s_down, H, I, p.resid, p.part, p.counters});
-    } else {
-      gemv_phase<I / QB>(c, GemvPhase<EPI_TP_PARTIAL, SCALE, 1>{L.s_down, H, I, nullptr, p.part, p.counters, 0,
-                                                                (int)(xk % 2), (unsigned)(x_base + xk + 1)});
-    }
-    if (tl) { step_put(p, ph + 4, 4, c.wait_cycles); step_put(p, ph + 4, 5, c.fold_cycles); }
-    if (TP > 1) {
-      tp_reduce(p, rbuf(xk), rbuf(xk + 1), (int)(xk % 2), (unsigned)(x_base + xk + 1));
-      ++xk;
-    }
-    grid_barrier(p.sync, nbar++, step_word(p, ph + 4, 2));
   }
-  if (tl) step_stamp(p, 5 * p.n_layers, 0);
-  // HEAD: logits + greedy argmax (FP8 per-channel head, or the bf16 head; TP: this rank's vocabulary rows)
-  c.tl_phase = 5 * p.n_layers;
-  if (HEAD_BF16) {
-    if (tl) step_stamp(p, 5 * p.n_layers, 1);
+  if (HEAD_BF16) {   // HEAD: the bf16 lm_head (reference checkpoint format) with the final RMSNorm
+    if (tl) { step_stamp(p, 5 * p.n_layers, 0); step_stamp(p, 5 * p.n_layers, 1); }
+    c.tl_phase = 5 * p.n_layers;
     head_bf16_phase(c, rbuf(xk), p.vocab_offset);
-  } else {
-    step_prologue<true>(c, rbuf(xk), p.final_norm, H, p.eps, nullptr);
-    if (tl) step_stamp(p, 5 * p.n_layers, 1);
-    gemv_phase<32>(c, GemvPhase<EPI_ARGMAX, SCALE_CHANNEL, 1>{p.s_head, p.vocab, H, p.logits, p.part, p.counters,
-                                                              p.vocab_offset});
+    if (tl) { step_put(p, 5 * p.n_layers, 4, c.wait_cycles); step_put(p, 5 * p.n_layers, 5, c.fold_cycles); }
   }
-  if (tl) { step_stamp(p, 5 * p.n_layers, 2); step_put(p, 5 * p.n_layers, 4, c.wait_cycles); step_put(p, 5 * p.n_layers, 5, c.fold_cycles); }
+  if (tl) step_stamp(p, 5 * p.n_layers, 2);
   {
     unsigned long long key = (c.best_i == 0x7FFFFFFF) ? 0ull : argmax_key(c.best_v, c.best_i);
 #pragma unroll
