@@ -454,6 +454,8 @@ def run_ours(args):
     t = e0.elapsed_time(e1) * 1e-3
     tokens = eng.out_tokens[:K].tolist()
     err = eng.k.device_error()
+    if err:   # a timed-out wait makes every later wait give up at once: the timing would be of broken steps
+        raise RuntimeError(f"decode steps failed on the device (error word {err:#x}); no valid measurement")
 
     # e2e through the public API: pinned h2d of the step's input token, graph replay, d2h of its output
     reset()
