@@ -753,6 +753,52 @@ __device__ void gemv_phase(Consumer& c, GemvPhase ph) {
   }
 }
 
+// ---- consumer: activation quantization of the staged x (sm.u.xs) -------------------------------------------
+// B groups gq = warp + 8 i per batch, every chain independent: loads (+ the RMSNorm scale when `norm`: K == 4096,
+// one batch, nraw[i] is group gq's weights), the group maxima reduced together by one butterfly, then the e4m3
+// quantization into f16 MMA fragments (sm.xh) and the scales (sm.xscale). Groups past KB are zero and not stored.
+template <int B>
+__device__ __forceinline__ void prologue_quant(Consumer& c, int KB, bool norm, const uint2 (&nraw)[4], float rstd) {
+  StepSmem& sm = *c.sm;
+  const int lane = c.lane, warp = c.warp;
+  const int ch = lane >> 3, hi = (lane >> 2) & 1, t = lane & 3;
+  for (int g0 = warp; g0 < KB; g0 += B * ST_WARPS) {
+    float v[B][4], amax[B];
+#pragma unroll
+    for (int i = 0; i < B; ++i) {
+      const int gq = g0 + i * ST_WARPS;
+      const uint2 raw = gq < KB ? *reinterpret_cast<const uint2*>(sm.u.xs + gq * QB + lane * 4) : make_uint2(0, 0);
+      v[i][0] = bf16lo(raw.x);
+      v[i][1] = bf16hi(raw.x);
+      v[i][2] = bf16lo(raw.y);
+      v[i][3] = bf16hi(raw.y);
+      if (B == 4 && norm) {
+        const float w[4] = {bf16lo(nraw[i & 3].x), bf16hi(nraw[i & 3].x), bf16lo(nraw[i & 3].y), bf16hi(nraw[i & 3].y)};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[i][j] = bf16r(w[j] * bf16r(v[i][j] * rstd));
+      }
+      amax[i] = fmaxf(fmaxf(fabsf(v[i][0]), fabsf(v[i][1])), fmaxf(fabsf(v[i][2]), fabsf(v[i][3])));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+      for (int i = 0; i < B; ++i) amax[i] = fmaxf(amax[i], __shfl_xor_sync(0xffffffffu, amax[i], o));
+    }
+#pragma unroll
+    for (int i = 0; i < B; ++i) {
+      const int gq = g0 + i * ST_WARPS;
+      if (gq < KB) {
+        const float sc = div_full(amax[i], 448.0f);
+        const uint32_t qv = quant4(v[i][0], v[i][1], v[i][2], v[i][3], sc);
+        uint32_t* dst = sm.xh + ((gq * 4 + ch) * 4 + t) * 4;
+        dst[hi] = e4m3x2_to_f16x2(qv);
+        dst[2 + hi] = e4m3x2_to_f16x2(qv >> 16);
+        if (lane == 0) sm.xscale[gq] = sc;
+      }
+    }
+  }
+}
+
 // ---- consumer: activation prologue ---------------------------------------------------------------------------
 // x (global, K values) -> RMSNorm when norm_w is given (K == 4096; the reference's 128-thread reduction order) ->
 // e4m3 per 128-group -> f16 fragments in sm.xh + scales in sm.xscale. x is read through L2 (other CTAs wrote it),
@@ -818,37 +864,8 @@ __device__ void step_prologue(Consumer& c, const bf16* x, const bf16* norm_w, in
     __syncwarp();
   }
   if (tid == 0 && c.p->tl) step_stamp(*c.p, c.tl_phase, 23);
-  const int ch = lane >> 3, hi = (lane >> 2) & 1, t = lane & 3;
-  for (int g0 = warp; g0 < KB; g0 += 4 * ST_WARPS) {   // 4 groups at a time (independent chains)
-    float v[4][4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int gq = g0 + i * ST_WARPS;
-      const uint2 raw = gq < KB ? *reinterpret_cast<const uint2*>(sm.u.xs + gq * QB + lane * 4) : make_uint2(0, 0);
-      v[i][0] = bf16lo(raw.x);
-      v[i][1] = bf16hi(raw.x);
-      v[i][2] = bf16lo(raw.y);
-      v[i][3] = bf16hi(raw.y);
-      if (norm_w) {   // K == 4096: a single batch, so nraw[i] is group gq's
-        const float w[4] = {bf16lo(nraw[i].x), bf16hi(nraw[i].x), bf16lo(nraw[i].y), bf16hi(nraw[i].y)};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) v[i][j] = bf16r(w[j] * bf16r(v[i][j] * rstd));
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int gq = g0 + i * ST_WARPS;
-      if (gq >= KB) break;
-      float amax = fmaxf(fmaxf(fabsf(v[i][0]), fabsf(v[i][1])), fmaxf(fabsf(v[i][2]), fabsf(v[i][3])));
-      amax = warp_max(amax);
-      const float sc = div_full(amax, 448.0f);
-      const uint32_t qv = quant4(v[i][0], v[i][1], v[i][2], v[i][3], sc);
-      uint32_t* dst = sm.xh + ((gq * 4 + ch) * 4 + t) * 4;
-      dst[hi] = e4m3x2_to_f16x2(qv);
-      dst[2 + hi] = e4m3x2_to_f16x2(qv >> 16);
-      if (lane == 0) sm.xscale[gq] = sc;
-    }
-  }
+  if (KB <= 4 * ST_WARPS) prologue_quant<4>(c, KB, norm_w != nullptr, nraw, rstd);
+  else prologue_quant<ST_MAX_K / QB / ST_WARPS>(c, KB, false, nraw, rstd);
   consumer_sync();
 }
 
