@@ -31,7 +31,7 @@
 namespace qk {
 
 constexpr int ST_WARPS = 8;                        // consumer warps (warpgroups 0 and 1)
-constexpr int ST_THREADS = (ST_WARPS + 4) * 32;    // + a producer warpgroup: one warp loads, three exit
+constexpr int ST_THREADS = (ST_WARPS + 4) * 32;    // + a producer warpgroup: one warp loads, three fetch split units
 // Register split (setmaxnreg): the CTA launches with 168 registers a thread (65,536 / 384, rounded down to 8),
 // 384 x 168 = 64,512 in all. The producer warpgroup gives its share back down to ST_PRODUCER_REGS and the two
 // consumer warpgroups grow to ST_CONSUMER_REGS: 128 x 56 + 256 x 216 = 62,464 <= 64,512, so the increase
@@ -59,6 +59,7 @@ constexpr int ST_MAX_SPLITS = 1024;                // contexts up to 64k
 constexpr int ST_BD_FLOATS = 6144;
 constexpr int ST_MERGE_ROUND = 128;                // splits staged per round of the attention merge
 constexpr int ST_TAIL_FLOATS = 96 * 16;            // StepSmem::tail: the remote block dots of a split unit
+constexpr int ST_FETCH_WARPS = 3;                  // warps 9-11 copy split units' remote block dots
 constexpr int ST_ABATCH = ST_NSTAGE < 4 ? ST_NSTAGE : 4;   // attention items processed together (<= ST_NSTAGE)
 
 struct StepLayer {
@@ -158,7 +159,8 @@ struct StepSmem {
     } at;
     struct {
       float o[ST_MERGE_ROUND * 32];                // partial outputs of up to ST_MERGE_ROUND splits, 32 dims each
-      float w[ST_MAX_SPLITS];                      // exp(m_s - M) per split
+      float w[ST_MAX_SPLITS];                      // m_s, then exp(m_s - M), per split
+      float l[ST_MAX_SPLITS];                      // l_s per split
       float cl;                                    // sum_s exp(m_s - M) * l_s
     } mg;
   } u;
@@ -437,9 +439,10 @@ __device__ __forceinline__ FoldPre fold_prefetch(const Consumer& c, const GemvPh
 // Copy n tagged block dots (u64 words: the fp32 value in the low half, the phase's tag in the high half) from
 // `src` into `dst` (shared memory), each once it carries `tag`: a warp loads 128 words at a time and reloads only
 // those not yet written. Bounded; returns false (error word set) on a timeout.
-__device__ __forceinline__ bool copy_tagged_dots(const unsigned long long* src, float* dst, int n, unsigned tag, int lane) {
+__device__ __forceinline__ bool copy_tagged_dots(const unsigned long long* src, float* dst, int n, unsigned tag, int lane,
+                                                 int part = 0, int parts = 1) {
   const unsigned long long t0 = globaltimer();
-  for (int b0 = 0; b0 < n; b0 += 128) {
+  for (int b0 = 128 * part; b0 < n; b0 += 128 * parts) {   // this warp's passes of 128 words
     unsigned long long w[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
@@ -493,7 +496,7 @@ __device__ __forceinline__ TailUnit tail_unit(int N, int KB, int NG) {
 // waits until the folding warp has used the buffer two phases back. Every wait is bounded; on a timeout the
 // error word is set and the fetch is skipped (the folding warp's own bounded wait then gives up).
 __device__ __forceinline__ void tail_fetch(StepSmem& sm, const StepParams& p, int N, int KB, int NG, int phase,
-                                           unsigned epoch, int& n, int lane) {
+                                           unsigned epoch, int& n, int lane, int part) {
   const int spu = KB * NG, RPU = 16 * NG;
   const TailUnit tu = tail_unit(N, KB, NG);
   if (!tu.any) return;
@@ -502,9 +505,10 @@ __device__ __forceinline__ void tail_fetch(StepSmem& sm, const StepParams& p, in
   if (use >= 1 && !__all_sync(0xffffffffu, mbar_wait(&sm.tail_empty[b], (uint32_t)((use - 1) & 1)))) return;
   const unsigned long long* src =
       reinterpret_cast<const unsigned long long*>(p.part) + (size_t)tu.u * KB * RPU + (tu.hi - tu.u * spu) * 16;
-  if (lane == 0) step_stamp(p, phase, 19);
-  const bool ok = copy_tagged_dots(src, sm.tail[b], tu.need * 16, dots_tag(epoch, p.n_layers, phase), lane);
-  if (lane == 0) step_stamp(p, phase, 20);
+  if (lane == 0 && part == 0) step_stamp(p, phase, 19);
+  const bool ok = copy_tagged_dots(src, sm.tail[b], tu.need * 16, dots_tag(epoch, p.n_layers, phase), lane, part,
+                                   ST_FETCH_WARPS);
+  if (lane == 0 && part == 0) step_stamp(p, phase, 20);
   if (ok) mbar_arrive(&sm.tail_full[b]);
 }
 
@@ -1100,16 +1104,21 @@ __device__ void merge_phase(Consumer& c, int l, int pos) {
   consumer_sync();
   if (tl) step_stamp(p, c.tl_phase, 14);
   float* cw = sm.u.mg.w;
-  if (warp == 0) {
-    const float* ml = p.ml_part + (size_t)qh * p.max_splits * 2;
+  if (warp == 0) {   // the split weights: one load of each (m_s, l_s) pair, kept in shared memory
+    const float2* ml = reinterpret_cast<const float2*>(p.ml_part + (size_t)qh * p.max_splits * 2);
     float mloc = -INFINITY;
-    for (int s = lane; s < n_splits; s += 32) mloc = fmaxf(mloc, __ldcg(ml + 2 * s));
+    for (int s = lane; s < n_splits; s += 32) {
+      const float2 v = __ldcg(ml + s);
+      cw[s] = v.x;
+      sm.u.mg.l[s] = v.y;
+      mloc = fmaxf(mloc, v.x);
+    }
     const float M = warp_max(mloc);
     float lsum = 0.f;
-    for (int s = lane; s < n_splits; s += 32) {
-      const float wt = expf(__ldcg(ml + 2 * s) - M);
+    for (int s = lane; s < n_splits; s += 32) {   // each lane rereads only the entries it wrote
+      const float wt = expf(cw[s] - M);
       cw[s] = wt;
-      lsum += wt * __ldcg(ml + 2 * s + 1);
+      lsum += wt * sm.u.mg.l[s];
     }
     lsum = warp_sum(lsum);
     if (lane == 0) sm.u.mg.cl = lsum;
@@ -1119,7 +1128,9 @@ __device__ void merge_phase(Consumer& c, int l, int pos) {
   const float* op = p.o_part + (size_t)qh * p.max_splits * HEAD_DIM + d0;
   for (int s0 = 0; s0 < n_splits; s0 += ST_MERGE_ROUND) {
     const int ns = min(ST_MERGE_ROUND, n_splits - s0);
-    for (int i = tid; i < ns * 8; i += ST_WARPS * 32) {   // 8 x 16 bytes per split row of 32 dims
+    // 8 x 16 bytes per split row of 32 dims; warps 1-7 load the first round while warp 0 computes the weights
+    for (int i = s0 == 0 ? tid - 32 : tid; i < ns * 8; i += s0 == 0 ? ST_WARPS * 32 - 32 : ST_WARPS * 32) {
+      if (i < 0) break;
       const int sr = i >> 3, f = i & 7;
       reinterpret_cast<uint4*>(sm.u.mg.o)[i] = ldcg_u4(op + (size_t)(s0 + sr) * HEAD_DIM + f * 4);
     }
@@ -1259,7 +1270,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) decode_step_kernel(const __grid
     sm.grab = 0;
     for (int i = 0; i < ST_BD_FLOATS / (4 * 16); ++i) sm.done[i] = 0;
     for (int b = 0; b < 2; ++b) {
-      mbar_init(&sm.tail_full[b], 32);   // the fetcher's 32 lanes, each after its words are in shared memory
+      mbar_init(&sm.tail_full[b], 32 * ST_FETCH_WARPS);   // every fetcher lane, after its words are in smem
       mbar_init(&sm.tail_empty[b], 1);
     }
     fence_mbar_init();
@@ -1306,14 +1317,15 @@ __global__ void __launch_bounds__(ST_THREADS, 1) decode_step_kernel(const __grid
         for (int row = hr.s0; row < hr.s1; row += ST_HEAD_ROWS)
           pr.push(p.w_head + (size_t)row * HIDDEN * 2, (uint32_t)(min(ST_HEAD_ROWS, hr.s1 - row) * HIDDEN * 2));
       }
-    } else if (warp == ST_WARPS + 1) {   // tail fetcher: the split units' remote block dots, phase by phase
+    } else if (warp >= ST_WARPS + 1) {   // tail fetchers: the split units' remote block dots, phase by phase
+      const int part = warp - (ST_WARPS + 1);   // this warp copies passes part, part + ST_FETCH_WARPS, ...
       const unsigned epoch = __ldcg(p.sync + 2);
       int n = 0;
       for (int g = 0; g < n_gemv; ++g) {
         const int k = (g >> 2) == p.n_layers ? 0 : g & 3;
         const int N = (g >> 2) == p.n_layers ? p.vocab : k == 0 ? QKV_N : k == 2 ? 2 * I : H;
         const int KB = k == 1 ? KO / QB : k == 3 ? I / QB : H / QB;
-        tail_fetch(sm, p, N, KB, k == 2 ? 2 : 1, gemv_timeline_phase(g), epoch, n, lane);
+        tail_fetch(sm, p, N, KB, k == 2 ? 2 : 1, gemv_timeline_phase(g), epoch, n, lane, part);
       }
     }
     return;
