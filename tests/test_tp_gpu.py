@@ -19,7 +19,6 @@ within its wait limit and report a timed-out exchange, and after `recover()` on 
 clean on both. NVLS is off (NCCL_NVLS_ENABLE=0) and the kernel's exchange is plain peer stores and loads.
 """
 import os
-import socket
 
 import pytest
 import torch
@@ -30,19 +29,19 @@ STEPS = 24
 POS0 = 100
 
 
-def _free_port():
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
+def _rendezvous(out_dir: str) -> str:
+    """A file-based rendezvous in the test's own directory: no TCP port to pick, so no port a previous test's
+    processes still hold can collide with it."""
+    return "file://" + os.path.join(out_dir, "pg_rendezvous")
 
 
-def _rank(rank, world, port, out_dir, fused):
+def _rank(rank, world, out_dir, fused):
     import datetime
     import torch.distributed as dist
     import model as M
     import tp as TP
     torch.cuda.set_device(rank)
-    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+    dist.init_process_group("nccl", init_method=_rendezvous(out_dir), rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", rank))
     eng = None
     try:
@@ -95,7 +94,7 @@ def test_tp2_matches_single_gpu(tmp_path, fused):
     torch.save(torch.tensor(tokens), str(tmp_path / "tokens.pt"))
     del eng, m
     torch.cuda.empty_cache()
-    mp.start_processes(_rank, args=(WORLD, _free_port(), str(tmp_path), fused), nprocs=WORLD,
+    mp.start_processes(_rank, args=(WORLD, str(tmp_path), fused), nprocs=WORLD,
                        start_method="spawn", join=True)
     ref = torch.stack(logits)
     full = torch.zeros_like(ref)
@@ -131,14 +130,14 @@ def test_tp2_matches_single_gpu(tmp_path, fused):
     print(f"TP={WORLD}: tokens agree {agree}/{STEPS}; near-tie flips {unclear}")
 
 
-def _skip_rank(rank, world, port, out_dir):
+def _skip_rank(rank, world, out_dir):
     import datetime
     import time
     import torch.distributed as dist
     import model as M
     import tp as TP
     torch.cuda.set_device(rank)
-    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+    dist.init_process_group("nccl", init_method=_rendezvous(out_dir), rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
     eng = None
     rec = {}
@@ -177,7 +176,7 @@ def _skip_rank(rank, world, port, out_dir):
 def test_fused_tp_recovers_after_a_peer_skips_a_step(tmp_path, monkeypatch):
     import torch.multiprocessing as mp
     monkeypatch.setenv("NCCL_NVLS_ENABLE", "0")
-    mp.start_processes(_skip_rank, args=(2, _free_port(), str(tmp_path)), nprocs=2, start_method="spawn", join=True)
+    mp.start_processes(_skip_rank, args=(2, str(tmp_path)), nprocs=2, start_method="spawn", join=True)
     r0 = torch.load(str(tmp_path / "skip0.pt"))
     r1 = torch.load(str(tmp_path / "skip1.pt"))
     assert r0["clean_error"] == 0 and r1["clean_error"] == 0
