@@ -618,7 +618,7 @@ PHASES = ("qkv", "attn", "o_proj", "gate_up", "down")
 
 
 def timeline_summary(tl, n_layers: int, clock_ghz: float = 1.965) -> dict:
-    """Per-phase breakdown of one fused-step launch from its timeline (int64 [CTAs, 5*layers+1, 24], words as in
+    """Per-phase breakdown of one fused-step launch from its timeline (int64 [CTAs, 5*layers+1, 32], words as in
     csrc/step.cuh: 0 consumers start the phase, 1 prologue done (attention: arrival counted and, on the CTA
     that completed a KV head, its merge done), 2 the whole CTA done (stamped inside the grid barrier), 3
     producer's first load of the phase, 4-6 cumulative clock64 cycles (consumer warp 0 waiting for ring
@@ -707,7 +707,7 @@ def run_timeline(args):
     eng = Engine(m, fused=True)
     n = len(m.layers)
     sms = torch.cuda.get_device_properties(0).multi_processor_count
-    eng.step_timeline = torch.zeros(sms, 5 * n + 1, 24, dtype=torch.int64, device="cuda")
+    eng.step_timeline = torch.zeros(sms, 5 * n + 1, 32, dtype=torch.int64, device="cuda")
     eng.token.fill_(1)
     eng.state.copy_(torch.tensor([start, 0], dtype=torch.int32))
     for _ in range(args.launches):

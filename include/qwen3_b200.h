@@ -163,7 +163,7 @@ typedef struct {
  *   sync        unsigned [4] zeroed once before the first launch: [0], [1] barrier counters (left zero), [2] the
  *               launches completed (tags of the shared block dots; zero it only together with `part`)
  *   max_splits  >= ceil(max_seq/64), <= 1024
- *   timeline    NULL, or a device buffer of (#SMs) x (5*n_layers + 1) x 24 u64: per CTA and phase (layer l:
+ *   timeline    NULL, or a device buffer of (#SMs) x (5*n_layers + 1) x 32 u64: per CTA and phase (layer l:
  *               qkv, attn, o, gu, down = 5l+0..4; lm_head = 5*n_layers) the %globaltimer of 0 consumers start,
  *               1 prologue done (attention: arrivals counted and, on merging CTAs, the merge done), 2 the whole
  *               CTA done (inside the grid barrier), 3 producer issues the phase's first load, 7 consumer warp 0

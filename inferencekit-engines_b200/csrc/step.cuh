@@ -134,7 +134,7 @@ struct StepParams {
 // 21 the folding warp starts waiting for the copy, 22 it has it; 23 the prologue's input is in shared memory (and,
 // for an RMSNorm, its scale known). Attention phase, thread 0, last batch of items: 9 its K/V stages have landed, 10 q/k/v setup done, 11 scores
 // done, 12 softmax done; merge: 13 merge entered, 14 the KV head's counter complete, 15 split weights ready.
-constexpr int ST_TL_WORDS = 24;
+constexpr int ST_TL_WORDS = 32;
 __device__ __forceinline__ void step_put(const StepParams& p, int phase, int i, unsigned long long v) {
   if (p.tl) p.tl[((size_t)blockIdx.x * (5 * p.n_layers + 1) + phase) * ST_TL_WORDS + i] = v;
 }
@@ -144,6 +144,17 @@ __device__ __forceinline__ void step_stamp(const StepParams& p, int phase, int i
 __device__ __forceinline__ unsigned long long* step_word(const StepParams& p, int phase, int i) {
   return p.tl ? p.tl + ((size_t)blockIdx.x * (5 * p.n_layers + 1) + phase) * ST_TL_WORDS + i : nullptr;
 }
+
+// A GEMV phase kind's per-CTA constants (slice range, stages, units, split unit), the same for every layer:
+// computed once per launch (their integer divisions off the phases' critical path).
+struct GemvPlan {
+  int s0, s1;           // the CTA's slices
+  int nst;              // ring stages of the phase
+  int u_lo, u_hi;       // its first and last unit
+  int nslots;           // block-dot slots of the shape
+  int tu_u, tu_hi, tu_need, tu_any;   // the split last unit (TailUnit)
+};
+constexpr int ST_PLANS = 5;                        // qkv, o_proj, gate_up, down, lm_head
 
 struct StepSmem {
   uint8_t ring[ST_NSTAGE][ST_STAGE];
@@ -176,6 +187,7 @@ struct StepSmem {
   unsigned long long bestbuf[ST_WARPS];
   uint64_t full[ST_NSTAGE], empty[ST_NSTAGE];
   int flag;
+  GemvPlan plan[ST_PLANS];
 };
 
 static_assert(sizeof(StepSmem) <= 227 * 1024, "the fused step's shared memory exceeds a CTA's 227 KB");
@@ -395,6 +407,7 @@ struct Consumer {
   int tl_phase = 0;   // timeline phase index of the phase being run
   long long relwait_cycles = 0;   // waiting for the slowest warp to release a stage this warp folds
   unsigned epoch = 0;             // launches completed before this one (the block-dot tags)
+  unsigned long long tag_base = 0;   // tag_base(epoch, n_layers)
   int tail_n = 0;     // GEMV phases so far with a split unit folded here (the tail buffers' use count)
 
   __device__ __forceinline__ bool wait_stage(int s) { return wait_abs(n); }
@@ -490,15 +503,42 @@ __device__ __forceinline__ TailUnit tail_unit(int N, int KB, int NG) {
   return t;
 }
 
+__device__ __forceinline__ GemvPlan make_plan(int N, int KB, int NG) {
+  const int spu = KB * NG;
+  const SliceRange r = slice_range(N / (16 * NG) * spu);
+  const TailUnit tu = tail_unit(N, KB, NG);
+  GemvPlan g;
+  g.s0 = r.s0;
+  g.s1 = r.s1;
+  g.nst = (r.s1 - r.s0 + ST_SLICES - 1) / ST_SLICES;
+  g.u_lo = r.s0 / spu;
+  g.u_hi = r.s1 > r.s0 ? (r.s1 - 1) / spu : g.u_lo - 1;
+  g.nslots = ST_BD_FLOATS / (KB * 16 * NG);
+  g.tu_u = tu.u;
+  g.tu_hi = tu.hi;
+  g.tu_need = tu.need;
+  g.tu_any = tu.any;
+  return g;
+}
+// Tag of launch `epoch`'s phase `phase` (dots_tag), from base = dots_tag's k for phase 0 modulo 2^32 - 1.
+__device__ __forceinline__ unsigned phase_tag(unsigned long long base, int phase) {
+  unsigned long long k = base + (unsigned)phase;
+  if (k >= 0xFFFFFFFFull) k -= 0xFFFFFFFFull;
+  return 1u + (unsigned)k;
+}
+__device__ __forceinline__ unsigned long long tag_base(unsigned epoch, int n_layers) {
+  return ((unsigned long long)epoch * (unsigned)(5 * n_layers + 1)) % 0xFFFFFFFFull;
+}
+
 // Tail-fetcher warp, one GEMV phase (timeline phase index `phase`; n counts the phases with a split unit,
 // identically on the consumer side): copy the following CTA's share of the split unit, tagged words published
 // early in that CTA's phase, into tail[n % 2] and signal tail_full[n % 2] (one arrival per lane). It first
 // waits until the folding warp has used the buffer two phases back. Every wait is bounded; on a timeout the
 // error word is set and the fetch is skipped (the folding warp's own bounded wait then gives up).
-__device__ __forceinline__ void tail_fetch(StepSmem& sm, const StepParams& p, int N, int KB, int NG, int phase,
-                                           unsigned epoch, int& n, int lane, int part) {
+__device__ __forceinline__ void tail_fetch(StepSmem& sm, const StepParams& p, const GemvPlan& pl, int KB, int NG,
+                                           int phase, unsigned tag, int& n, int lane, int part) {
   const int spu = KB * NG, RPU = 16 * NG;
-  const TailUnit tu = tail_unit(N, KB, NG);
+  const TailUnit tu{pl.tu_u, pl.tu_hi, pl.tu_need, pl.tu_any != 0};
   if (!tu.any) return;
   const int b = n & 1, use = n >> 1;
   ++n;
@@ -506,8 +546,7 @@ __device__ __forceinline__ void tail_fetch(StepSmem& sm, const StepParams& p, in
   const unsigned long long* src =
       reinterpret_cast<const unsigned long long*>(p.part) + (size_t)tu.u * KB * RPU + (tu.hi - tu.u * spu) * 16;
   if (lane == 0 && part == 0) step_stamp(p, phase, 19);
-  const bool ok = copy_tagged_dots(src, sm.tail[b], tu.need * 16, dots_tag(epoch, p.n_layers, phase), lane, part,
-                                   ST_FETCH_WARPS);
+  const bool ok = copy_tagged_dots(src, sm.tail[b], tu.need * 16, tag, lane, part, ST_FETCH_WARPS);
   if (lane == 0 && part == 0) step_stamp(p, phase, 20);
   if (ok) mbar_arrive(&sm.tail_full[b]);
 }
@@ -598,21 +637,20 @@ __device__ __forceinline__ void fold_unit(Consumer& c, const GemvPhase& ph, cons
   }
 }
 
-__device__ void gemv_phase(Consumer& c, GemvPhase ph) {
+__device__ void gemv_phase(Consumer& c, GemvPhase ph, const GemvPlan& pl) {
   StepSmem& sm = *c.sm;
-  ph.dtag = dots_tag(c.epoch, c.p->n_layers, c.tl_phase);
+  ph.dtag = phase_tag(c.tag_base, c.tl_phase);
   const int KB = ph.KB, NG = ph.NG, ngs = NG - 1;   // NG is 1 or 2: slice q is tile q >> ngs, sub-matrix q & ngs
   const int RPU = 16 * NG;                          // rows per unit
   const int spu = KB * NG;                          // slices per unit
   const int slot_floats = KB * RPU;
-  const int nslots = ST_BD_FLOATS / slot_floats;
+  const int nslots = pl.nslots;
   ph.nslots = nslots;
   constexpr int NQ = ST_SLICES / ST_QUAD;         // grabs per stage
   static_assert(ST_SLICES % ST_QUAD == 0 && ST_WARPS % NQ == 0, "a stage's grabs must add up to its ST_WARPS arrivals");
   static_assert(ST_QUAD <= 4, "a group of slices spans at most two units (4 <= every K / 128)");
-  const int units = ph.N / RPU;
-  const SliceRange r = slice_range(units * spu);
-  const int nst = (r.s1 - r.s0 + ST_SLICES - 1) / ST_SLICES;   // stages of this phase (as the producer issues)
+  const SliceRange r{pl.s0, pl.s1};
+  const int nst = pl.nst;   // stages of this phase (as the producer issues)
   const int n0 = c.n;
   const uint8_t* xh = reinterpret_cast<const uint8_t*>(sm.xh);
   // Work is handed out in groups of ST_QUAD consecutive slices: grab p is slices ST_QUAD * (p % NQ) .. +ST_QUAD-1
@@ -620,13 +658,12 @@ __device__ void gemv_phase(Consumer& c, GemvPhase ph) {
   // leaves its share to the others; each grab counts ST_WARPS / NQ arrivals on the stage's `empty` barrier. A
   // finished slice adds 1 to its unit's counter (sm.done, per slot); unit u is folded by warp
   // (u - u_lo) % ST_WARPS once all its slices in this CTA are done.
-  const int u_lo = r.s0 / spu, u_hi = r.s1 > r.s0 ? (r.s1 - 1) / spu : u_lo - 1;
+  const int u_lo = pl.u_lo, u_hi = pl.u_hi;
   int fu = u_lo + c.warp;                                       // next unit this warp folds
   // slices of unit u that this CTA computes and folds (none for a unit an earlier CTA started, which folds it)
   auto local_count = [&](int u) { return u * spu < r.s0 ? 0 : min((u + 1) * spu, r.s1) - u * spu; };
   FoldPre pre = fold_prefetch(c, ph, fu, fu <= u_hi);
-  const TailUnit tu = tail_unit(ph.N, KB, NG);
-  const int tail_use = tu.any ? c.tail_n++ : -1;
+  const int tail_use = pl.tu_any ? c.tail_n++ : -1;
   auto fold_ready = [&](int u) { return *reinterpret_cast<volatile int*>(&sm.done[u % nslots]) >= local_count(u); };
   auto fold_next = [&]() {   // fold unit fu, move on to this warp's next unit and prefetch its row inputs
     const long long t0 = clock64();
@@ -1268,6 +1305,11 @@ __global__ void __launch_bounds__(ST_THREADS, 1) decode_step_kernel(const __grid
       mbar_init(&sm.empty[s], ST_WARPS);
     }
     sm.grab = 0;
+    sm.plan[0] = make_plan(6144 / TP, HIDDEN / QB, 1);            // qkv
+    sm.plan[1] = make_plan(HIDDEN, HIDDEN / TP / QB, 1);          // o_proj
+    sm.plan[2] = make_plan(2 * 12288 / TP, HIDDEN / QB, 2);       // gate_up
+    sm.plan[3] = make_plan(HIDDEN, 12288 / TP / QB, 1);           // down
+    sm.plan[4] = make_plan(p.vocab, HIDDEN / QB, 1);              // lm_head (FP8)
     for (int i = 0; i < ST_BD_FLOATS / (4 * 16); ++i) sm.done[i] = 0;
     for (int b = 0; b < 2; ++b) {
       mbar_init(&sm.tail_full[b], 32 * ST_FETCH_WARPS);   // every fetcher lane, after its words are in smem
@@ -1319,13 +1361,14 @@ __global__ void __launch_bounds__(ST_THREADS, 1) decode_step_kernel(const __grid
       }
     } else if (warp >= ST_WARPS + 1) {   // tail fetchers: the split units' remote block dots, phase by phase
       const int part = warp - (ST_WARPS + 1);   // this warp copies passes part, part + ST_FETCH_WARPS, ...
-      const unsigned epoch = __ldcg(p.sync + 2);
+      const unsigned long long tb = tag_base(__ldcg(p.sync + 2), p.n_layers);
       int n = 0;
       for (int g = 0; g < n_gemv; ++g) {
         const int k = (g >> 2) == p.n_layers ? 0 : g & 3;
-        const int N = (g >> 2) == p.n_layers ? p.vocab : k == 0 ? QKV_N : k == 2 ? 2 * I : H;
         const int KB = k == 1 ? KO / QB : k == 3 ? I / QB : H / QB;
-        tail_fetch(sm, p, N, KB, k == 2 ? 2 : 1, gemv_timeline_phase(g), epoch, n, lane, part);
+        const int ph = gemv_timeline_phase(g);
+        tail_fetch(sm, p, sm.plan[(g >> 2) == p.n_layers ? 4 : k], KB, k == 2 ? 2 : 1, ph, phase_tag(tb, ph), n, lane,
+                   part);
       }
     }
     return;
@@ -1334,6 +1377,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) decode_step_kernel(const __grid
   asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(ST_CONSUMER_REGS) : "memory");
   Consumer c{&sm, &p, 0, lane, warp, lane >> 2, lane & 3, -INFINITY, 0x7FFFFFFF, 0, 0};
   c.epoch = __ldcg(p.sync + 2);
+  c.tag_base = tag_base(c.epoch, p.n_layers);
   unsigned nbar = 0;
   const int tok = p.token[0];
   const bool tok_ok = tok >= 0 && tok < p.vocab * TP;
@@ -1376,7 +1420,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) decode_step_kernel(const __grid
     c.tl_phase = ph;
     step_prologue(c, x, nw, d.K, p.eps, embed_dst);
     if (tl) step_stamp(p, ph, 1);
-    gemv_phase(c, d);
+    gemv_phase(c, d, sm.plan[head ? 4 : k]);
     if (tl) { step_put(p, ph, 4, c.wait_cycles); step_put(p, ph, 5, c.fold_cycles); }
     if (head) break;
     if (TP > 1 && row_par) {   // the tags tell a reducer when every rank's partial of its row has arrived

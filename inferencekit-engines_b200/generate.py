@@ -63,7 +63,7 @@ class Engine:
         self.lm_head_ctas = lm_head_ctas
         self.graph = None
         self.fused = fused
-        self.step_timeline = None     # fused step only: int64 [#SMs, 5*layers+1, 24] stamps (include/qwen3_b200.h)
+        self.step_timeline = None     # fused step only: int64 [#SMs, 5*layers+1, 32] stamps (include/qwen3_b200.h)
         if fused:
             if attn_chunk != 64 or m.batch != 1:
                 raise ValueError("the fused step needs 64-key attention splits and batch 1")
