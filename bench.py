@@ -867,6 +867,70 @@ def run_attention_sweep(args):
     return out
 
 
+def run_prefill(args):
+    """Prompt processing on the benchmarked model (36 layers, per-channel FP8 scales, FP8 head): a P-token
+    synthetic prompt through Engine.prefill_chunked (the batched forward, 64 positions per pass: the tcgen05
+    FP8 linear plus the row-wise prefill kernels) against the same prompt fed position by position through the
+    fused decode step (Engine.prefill). Prints one JSON line: prompt tokens/s of each path, the chunked path's
+    algorithmic weight stream (every layer's weights once per chunk, the head once) in GB/s and as a fraction
+    of the measured HBM peak, and whether both paths pick the same first token. The weights (7.5 GB per pass
+    over the layers) are far larger than L2, so no flush is needed between passes."""
+    import model as M
+    from generate import Engine
+    peak, peak_kind = peaks()
+    P, chunk = args.prompt, 64
+    K, W = max(1, min(args.steps, 8)), max(args.warmup, 3)
+    cfg = M.Config()
+    m = M.Qwen3FP8Decode.synthetic(cfg, max_seq=4096, device="cuda", seed=args.seed, scale_mode=args.scale,
+                                   head_dtype=args.head, norm_init="ones")
+    eng = Engine(m, fused=True)
+    ids = torch.randint(0, cfg.vocab, (P,), generator=torch.Generator().manual_seed(7)).tolist()
+    eng.rowmajor_weights()
+    for _ in range(W):
+        eng.prefill_chunked(ids, chunk)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(K):
+            tok_c = eng.prefill_chunked(ids, chunk)
+        e1.record()
+        torch.cuda.synchronize()
+    t_chunked = e0.elapsed_time(e1) * 1e-3 / K
+    tok_c = int(tok_c)
+    eng.check()
+
+    # the decode-path prefill: one warm call (captures the step graph), then one timed
+    eng.prefill(ids)
+    torch.cuda.synchronize()
+    e0.record()
+    tok_d = eng.prefill(ids)
+    e1.record()
+    torch.cuda.synchronize()
+    t_decode = e0.elapsed_time(e1) * 1e-3
+    tok_d = int(tok_d)
+    eng.check()
+
+    layer_bytes = sum(lin.N * lin.K + lin.scale.numel() * 4 for L in m.layers for lin in (L.qkv, L.o, L.gu, L.down))
+    head_bytes = cfg.vocab * cfg.hidden + (cfg.vocab * 4 if args.head == "fp8" else cfg.vocab * cfg.hidden)
+    chunks = -(-P // chunk)
+    nbytes = chunks * layer_bytes + head_bytes
+    gbs = nbytes / t_chunked / 1e9
+    rec = {"metric": "prefill_tokens_per_s", "value": P / t_chunked, "unit": "tok/s", "higher_is_better": True,
+           "prompt": P, "chunk": chunk, "ms_per_prompt": t_chunked * 1e3, "steps": K, "warmup": W,
+           "decode_path": {"value": P / t_decode, "unit": "tok/s", "ms_per_prompt": t_decode * 1e3},
+           "speedup_vs_decode_path": t_decode / t_chunked, "same_first_token": tok_c == tok_d,
+           "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                        "algorithmic_bytes": nbytes, "peak_kind": peak_kind},
+           "dtype": "fp8 weights, bf16 activations", "data": "synthetic",
+           "config": {"workload": f"Qwen3-8B FP8 prompt of {P} tokens (36 layers, {args.scale} scales, "
+                                  f"{args.head} head), chunks of {chunk}", "l2": "weights > L2, no flush"},
+           "clocks": clk.summary()}
+    print(json.dumps(rec), flush=True)
+    return rec
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--profile-kernel", choices=["qkv", "o_proj", "gate_up", "down", "lm_head", "attention", "decode_step",
@@ -895,11 +959,16 @@ def main():
     ap.add_argument("--shapes", default="", help="--sweep gemv: comma-separated KxN shapes instead of the five")
     ap.add_argument("--rows", default="", help="--sweep gemv: comma-separated row counts instead of 1,4,16,64")
     ap.add_argument("--timeline-out", default="", help="--timeline: also save the raw stamps (torch.save) here")
+    ap.add_argument("--prefill", action="store_true",
+                    help="prompt processing: chunked prefill against the decode-path prefill (--prompt tokens)")
+    ap.add_argument("--prompt", type=int, default=512, help="--prefill: prompt length")
     ap.add_argument("--timeline", action="store_true",
                     help="one fused-step launch with per-phase timeline stamps, summarised (36 layers unless --layers)")
     args = ap.parse_args()
     if args.timeline:
         return run_timeline(args)
+    if args.prefill:
+        return run_prefill(args)
     if args.sweep == "attention":
         return run_attention_sweep(args)
     if args.sweep == "gemv":

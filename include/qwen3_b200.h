@@ -235,8 +235,8 @@ int qk_embed(const int* token, const void* table, void* resid, int vocab, int ba
 int qk_finalize(unsigned long long* best, int* token, int* out_tokens, int* state, int out_len, int batch,
                 qk_stream_t stream);
 
-/* Batched FP8 W8A8 linear on the tcgen05 tensor cores (BASELINE's batched GEMV rows; the reference's batched
- * path is its Triton fp8_matmul, prefill.py:121-156, with act_quant :23-41): out[m][n] = bf16(sum over K blocks
+/* Batched FP8 W8A8 linear on the tcgen05 tensor cores (1-64 rows: the batched GEMV rows and prefill chunks; the
+ * reference's batched path is its Triton fp8_matmul, prefill.py:121-156, with act_quant :23-41): out[m][n] = bf16(sum over K blocks
  * kb of dot_kb(q(x[m]), w[n]) * s_x[m][kb] * s_w[n][kb]) for M = 1..64 rows, where q() is the per-128-group e4m3
  * quantizer of the GEMV (optionally after RMSNorm with norm_w). x bf16 [M][K]; w fp8 row-major [N][K] (plain
  * matrix, TMA boxes; not the GEMV's packed layout); w_scale fp32 [N] (QK_SCALE_CHANNEL) or [N/128][K/128];
@@ -248,6 +248,32 @@ long long qk_fp8_gemm_rows_scratch_bytes(int M, int N, int K);
 int qk_fp8_gemm_rows(const void* x, const void* norm_w, int M, int K, const void* w, const float* w_scale,
                      int scale_mode, int N, float eps, void* out, void* scratch, long long scratch_bytes,
                      qk_stream_t stream);
+
+/* Chunked prefill: the row-wise steps of the reference's batched forward (Q/model.py:243-281, with the fused
+ * prefill kernels of Q/kernels/prefill_fused.py:57-183), run on a chunk of M prompt positions p0 .. p0+M-1
+ * around four qk_fp8_gemm_rows calls per layer. All tensors bf16, row-major, on the device.
+ *
+ * qk_embed_rows: out[m] = table[tokens[m]] (HIDDEN values) for m < M; a token outside [0, vocab) sets the
+ *   error word's bad-state bit and copies row 0.
+ * qk_prefill_qkv: from qkv [M][(n_q + 2 n_kv) * 128] (the qkv projection of the chunk), per row m at position
+ *   p0 + m: q_out[m][h] = RoPE(RMSNorm(q_h, q_norm)), k_cache[g][p0+m] = RoPE(RMSNorm(k_g, k_norm)),
+ *   v_cache[g][p0+m] = v_g, with the decode step's bf16 roundings (the rows written equal what the decode step
+ *   writes for that position from the same qkv row). k_cache/v_cache: one layer, [n_kv][max_seq][128];
+ *   cos_tab/sin_tab: [max_seq][128]. n_q = 4 n_kv; p0 + M <= max_seq.
+ * qk_prefill_attention: out[m][h] = softmax(q[m][h] . K[g][0..p0+m] * scale) . V[g][0..p0+m] with g = h / 4
+ *   (causal GQA); fp32 scores, probabilities and sums, one online-softmax pass; matches an fp32 reference to
+ *   rounding. q and out: [M][n_q * 128]; the caches as above, rows 0 .. p0+M-1 written.
+ * qk_add_rows: resid[i] = bf16(resid[i] + y[i]) for i < n (the decode step's residual epilogue).
+ * qk_swiglu_rows: h[m][i] = bf16(bf16(silu(gu[m][i])) * gu[m][I + i]) for gu [M][2I], h [M][I] (the decode
+ *   step's SwiGLU epilogue). */
+int qk_embed_rows(const int* tokens, int M, const void* table, int vocab, void* out, qk_stream_t stream);
+int qk_prefill_qkv(const void* qkv, int M, int p0, int n_q, int n_kv, const void* q_norm, const void* k_norm,
+                   const void* cos_tab, const void* sin_tab, float eps, void* k_cache, void* v_cache, int max_seq,
+                   void* q_out, qk_stream_t stream);
+int qk_prefill_attention(const void* q, int M, int p0, int n_q, int n_kv, const void* k_cache, const void* v_cache,
+                         int max_seq, float scale, void* out, qk_stream_t stream);
+int qk_add_rows(void* resid, const void* y, long long n, qk_stream_t stream);
+int qk_swiglu_rows(const void* gu, int M, int I, void* h, qk_stream_t stream);
 
 /* Tensor-parallel helpers (no counterpart in the single-GPU reference; the TP plan of its decode step):
  * resid[i] = bf16(resid[i] + bf16(sum[i])) for the fp32 all-reduced partial of a row-parallel GEMV (the

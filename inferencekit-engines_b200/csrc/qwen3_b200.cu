@@ -2,6 +2,7 @@
 // the device symbols (error word) are shared by every kernel without relocatable device code.
 #include <cudaTypedefs.h>   // PFN_cuTensorMapEncodeTiled
 
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -12,6 +13,7 @@
 #include "common.cuh"
 #include "gemm_tc.cuh"
 #include "gemv.cuh"
+#include "prefill.cuh"
 #include "step.cuh"
 
 static_assert(sizeof(qk_layer_t) == sizeof(qk::StepLayer), "qk_layer_t must mirror StepLayer");
@@ -745,3 +747,67 @@ extern "C" int qk_fp8_gemv_noalloc(int kind, const void* w, const float* w_scale
   return qk_fp8_gemv(kind, w, w_scale, scale_mode, x, norm_w, resadd, resid_out, out, N, K, eps, part_ptr, counters,
                      0, 0, 0, -1, 0, stream);
 }
+
+// ---- chunked prefill: the row-wise kernels around the batched linear ------------------------------------------
+namespace {
+int plain_launch_status(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? QK_OK : cuda_fail(e, what);
+}
+int elementwise_blocks(long long n) { return (int)std::min<long long>((n + 255) / 256, 4096); }
+}  // namespace
+
+extern "C" {
+
+int qk_embed_rows(const int* tokens, int M, const void* table, int vocab, void* out, qk_stream_t stream) {
+  if (!tokens || !table || !out || M < 1 || vocab < 1) return fail(QK_EINVAL, "bad embed_rows arguments");
+  if (!aligned(table, 16) || !aligned(out, 16)) return fail(QK_EINVAL, "table/out must be 16-byte aligned");
+  embed_rows_kernel<<<M, 256, 0, static_cast<cudaStream_t>(stream)>>>(tokens, vocab, static_cast<const bf16*>(table),
+                                                                      HIDDEN, static_cast<bf16*>(out));
+  return plain_launch_status("embed_rows launch");
+}
+
+int qk_prefill_qkv(const void* qkv, int M, int p0, int n_q, int n_kv, const void* q_norm, const void* k_norm,
+                   const void* cos_tab, const void* sin_tab, float eps, void* k_cache, void* v_cache, int max_seq,
+                   void* q_out, qk_stream_t stream) {
+  if (!qkv || !q_norm || !k_norm || !cos_tab || !sin_tab || !k_cache || !v_cache || !q_out)
+    return fail(QK_EINVAL, "null pointer argument");
+  if (M < 1 || p0 < 0 || n_kv < 1 || n_q != GQA * n_kv) return fail(QK_EINVAL, "M=%d p0=%d n_q=%d n_kv=%d", M, p0, n_q, n_kv);
+  if ((long long)p0 + M > max_seq) return fail(QK_EINVAL, "positions %d..%d past max_seq %d", p0, p0 + M - 1, max_seq);
+  if (!aligned(qkv, 8) || !aligned(k_cache, 8) || !aligned(v_cache, 8) || !aligned(q_out, 8))
+    return fail(QK_EINVAL, "qkv, caches and q_out must be 8-byte aligned");
+  const dim3 grid(M, (n_q + 2 * n_kv + 7) / 8);
+  prefill_qkv_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const bf16*>(qkv), p0, n_q, n_kv, static_cast<const bf16*>(q_norm), static_cast<const bf16*>(k_norm),
+      static_cast<const bf16*>(cos_tab), static_cast<const bf16*>(sin_tab), eps, static_cast<bf16*>(k_cache),
+      static_cast<bf16*>(v_cache), max_seq, static_cast<bf16*>(q_out));
+  return plain_launch_status("prefill_qkv launch");
+}
+
+int qk_prefill_attention(const void* q, int M, int p0, int n_q, int n_kv, const void* k_cache, const void* v_cache,
+                         int max_seq, float scale, void* out, qk_stream_t stream) {
+  if (!q || !k_cache || !v_cache || !out) return fail(QK_EINVAL, "null pointer argument");
+  if (M < 1 || p0 < 0 || n_kv < 1 || n_q != GQA * n_kv) return fail(QK_EINVAL, "M=%d p0=%d n_q=%d n_kv=%d", M, p0, n_q, n_kv);
+  if ((long long)p0 + M > max_seq) return fail(QK_EINVAL, "positions %d..%d past max_seq %d", p0, p0 + M - 1, max_seq);
+  if (!aligned(k_cache, 16) || !aligned(v_cache, 16)) return fail(QK_EINVAL, "caches must be 16-byte aligned");
+  prefill_attention_kernel<<<dim3(M, n_kv), PF_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const bf16*>(q), p0, n_q, static_cast<const bf16*>(k_cache), static_cast<const bf16*>(v_cache),
+      max_seq, scale, static_cast<bf16*>(out));
+  return plain_launch_status("prefill_attention launch");
+}
+
+int qk_add_rows(void* resid, const void* y, long long n, qk_stream_t stream) {
+  if (!resid || !y || n < 1) return fail(QK_EINVAL, "bad add_rows arguments");
+  add_rows_kernel<<<elementwise_blocks(n), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<bf16*>(resid), static_cast<const bf16*>(y), n);
+  return plain_launch_status("add_rows launch");
+}
+
+int qk_swiglu_rows(const void* gu, int M, int I, void* h, qk_stream_t stream) {
+  if (!gu || !h || M < 1 || I < 1) return fail(QK_EINVAL, "bad swiglu_rows arguments");
+  swiglu_rows_kernel<<<elementwise_blocks((long long)M * I), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const bf16*>(gu), M, I, static_cast<bf16*>(h));
+  return plain_launch_status("swiglu_rows launch");
+}
+
+}  // extern "C"

@@ -4,17 +4,20 @@ Mirrors the reference engine (qwen3-8b-fp8_rtx-5090/generate.py:39-197): device-
 `[pos, step]`, static activation buffers, `decode_step()` (the hot path, 183 launches), `capture()` into one
 CUDA graph, and `generate()`, which replays the graph without a host sync per token.
 
-Prompt processing: the reference runs a Triton prefill (outside this path's scope). Here a prompt is fed
-through the same decode graph one position at a time (teacher forcing), which writes the same KV rows a
-prefill would and leaves the first generated token in `token`; synthetic long-context setups instead fill
-the cache directly (`Qwen3FP8Decode.fill_cache_random`).
+Prompt processing, two ways:
+* `prefill()` feeds the prompt through the decode graph one position at a time (teacher forcing), which
+  writes the KV rows and leaves the first generated token in `token`;
+* `prefill_chunked()` runs the reference's batched forward (qwen3-8b-fp8_rtx-5090/model.py:243-281) on chunks
+  of up to 64 positions: the tcgen05 batched FP8 linear for the projections, the row-wise prefill kernels
+  (csrc/prefill.cuh) around it. It reads every weight once per chunk instead of once per position.
+Synthetic long-context setups instead fill the cache directly (`Qwen3FP8Decode.fill_cache_random`).
 """
 from __future__ import annotations
 
 import torch
 
 from kernels import ops
-from model import Qwen3FP8Decode, Linear
+from model import Qwen3FP8Decode, Linear, unpack_fp8
 
 # Per-kind GEMV launch shape: ring stages per warp, warps per CTA, stages issued before the wait,
 # tiles per stage (2 KiB = 16 rows x 128 k; 4 KiB for gate|up), CTAs per SM. Kinds: qkv, o_proj, gate_up, down.
@@ -163,6 +166,71 @@ class Engine:
                 self.token.copy_(ids[i:i + 1])
             self.step(1, use_graph)
         self.state[1].fill_(0)
+        return self.token.clone()
+
+    def rowmajor_weights(self):
+        """Per layer, the (qkv, o, gate_up, down) weights as row-major fp8 [N, K] matrices (the batched linear
+        streams TMA boxes of the plain matrix), unpacked once from the decode layout and cached: 8.2 GB more
+        device memory for Qwen3-8B, as the reference's prefill keeps its own row-major copy
+        (model.py `rowmajor_copy`)."""
+        if getattr(self, "_rowmajor", None) is None:
+            self._rowmajor = [tuple(unpack_fp8(lin.packed, lin.N, lin.K, lin.pairs)
+                                    for lin in (L.qkv, L.o, L.gu, L.down)) for L in self.m.layers]
+        return self._rowmajor
+
+    @torch.no_grad()
+    def prefill_chunked(self, prompt_ids, chunk: int = 64) -> torch.Tensor:
+        """Prompt positions 0..P-1 through the batched forward, `chunk` (<= 64) positions per pass: per layer
+        qkv = W_qkv . q(RMSNorm(h)), per-head norm + RoPE with K/V appended to the cache, causal attention over
+        the cache, h += W_o . q(attn), h += W_down . q(SwiGLU(W_gu . q(RMSNorm(h)))). The last position's
+        hidden row then goes through the head and argmax. Leaves state = [P, 0] and the first generated token
+        in `token`, like `prefill()`, and returns it as a device tensor (no host sync)."""
+        m, k, cfg = self.m, self.k, self.m.cfg
+        if m.batch != 1:
+            raise ValueError("prefill_chunked runs batch 1")
+        if not 1 <= chunk <= 64:
+            raise ValueError("chunk must be 1..64 positions")
+        ids = torch.as_tensor(prompt_ids, dtype=torch.int32, device=m.device)
+        P = ids.numel()
+        assert 0 < P < self.max_seq
+        nq, nkv, hd = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
+        bf = dict(dtype=torch.bfloat16, device=m.device)
+        if getattr(self, "_pf", None) is None or self._pf["resid"].shape[0] < chunk:
+            self._pf = dict(resid=torch.empty(chunk, cfg.hidden, **bf),
+                            qkv=torch.empty(chunk, (nq + 2 * nkv) * hd, **bf),
+                            q=torch.empty(chunk, nq, hd, **bf), attn=torch.empty(chunk, nq * hd, **bf),
+                            y=torch.empty(chunk, cfg.hidden, **bf), gu=torch.empty(chunk, 2 * cfg.inter, **bf),
+                            h=torch.empty(chunk, cfg.inter, **bf))
+        b = self._pf
+        weights = self.rowmajor_weights()
+        for p0 in range(0, P, chunk):
+            M = min(chunk, P - p0)
+            resid, qkv, q, attn = b["resid"][:M], b["qkv"][:M], b["q"][:M], b["attn"][:M]
+            y, gu, h = b["y"][:M], b["gu"][:M], b["h"][:M]
+            k.embed_rows(ids[p0:p0 + M], m.embed, resid)
+            for li, L in enumerate(m.layers):
+                wq, wo, wgu, wd = weights[li]
+                kc, vc = m.k_cache[li, 0], m.v_cache[li, 0]
+                k.fp8_gemm_rows(resid, wq, L.qkv.scale, qkv, norm_w=L.ln1, eps=cfg.eps)
+                k.prefill_qkv(qkv, p0, L.q_norm, L.k_norm, m.cos, m.sin, cfg.eps, kc, vc, q)
+                k.prefill_attention(q, p0, kc, vc, hd ** -0.5, attn)
+                k.fp8_gemm_rows(attn, wo, L.o.scale, y)
+                k.add_rows(resid, y)
+                k.fp8_gemm_rows(resid, wgu, L.gu.scale, gu, norm_w=L.ln2, eps=cfg.eps)
+                k.swiglu_rows(gu, h)
+                k.fp8_gemm_rows(h, wd, L.down.scale, y)
+                k.add_rows(resid, y)
+        last = b["resid"][(P - 1) % chunk]
+        self.best.zero_()
+        if isinstance(m.lm_head, Linear):
+            k.lm_head_argmax(m.lm_head.packed, last, m.norm, self.logits, self.best, cfg.eps, self.lm_head_ctas,
+                             w_scale=m.lm_head.scale)
+        else:
+            k.lm_head_argmax(m.lm_head, last, m.norm, self.logits, self.best, cfg.eps, self.lm_head_ctas)
+        self.state[0] = P - 1
+        self.state[1] = 0
+        k.finalize(self.best, self.token, self.out_tokens, self.state)
+        self.state[1] = 0
         return self.token.clone()
 
     def check(self):

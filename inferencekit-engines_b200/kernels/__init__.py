@@ -67,6 +67,11 @@ _SIGS = {
     "qk_finalize": ([_VP, _VP, _VP, _VP, _I, _I, _VP], _I),
     "qk_fp8_gemm_rows_scratch_bytes": ([_I, _I, _I], ctypes.c_longlong),
     "qk_fp8_gemm_rows": ([_VP, _VP, _I, _I, _VP, _VP, _I, _I, _F, _VP, _VP, ctypes.c_longlong, _VP], _I),
+    "qk_embed_rows": ([_VP, _I, _VP, _I, _VP, _VP], _I),
+    "qk_prefill_qkv": ([_VP, _I, _I, _I, _I, _VP, _VP, _VP, _VP, _F, _VP, _VP, _I, _VP, _VP], _I),
+    "qk_prefill_attention": ([_VP, _I, _I, _I, _I, _VP, _VP, _I, _F, _VP, _VP], _I),
+    "qk_add_rows": ([_VP, _VP, ctypes.c_longlong, _VP], _I),
+    "qk_swiglu_rows": ([_VP, _I, _I, _VP, _VP], _I),
 }
 
 
@@ -306,6 +311,42 @@ class DecodeOps:
         st = self.lib.qk_fp8_gemm_rows(_p(x), _p(norm_w), M, K, _p(w), _p(w_scale), scale_mode, N, float(eps),
                                        _p(out), _p(sc), sc.numel(), _stream())
         self._check(st, "fp8_gemm_rows")
+
+    # ---- chunked prefill (row-wise steps around fp8_gemm_rows) ----
+
+    def embed_rows(self, tokens, table, out):
+        """out[m] = table[tokens[m]] for the chunk's int32 tokens [M]; out bf16 [M, H]."""
+        M = tokens.numel()
+        self._check(self.lib.qk_embed_rows(_p(tokens), M, _p(table), table.shape[0], _p(out), _stream()),
+                    "embed_rows")
+
+    def prefill_qkv(self, qkv, p0, q_norm, k_norm, cos, sin, eps, k_cache, v_cache, q_out):
+        """Per-head RMSNorm + RoPE of the chunk's q and k rows (positions p0 .. p0+M-1), K and V appended to
+        one layer's cache [n_kv, max_seq, 128]; q_out bf16 [M, n_q, 128]."""
+        M = qkv.shape[0]
+        n_kv, max_seq = k_cache.shape[0], k_cache.shape[1]
+        n_q = q_out.shape[1]
+        st = self.lib.qk_prefill_qkv(_p(qkv), M, int(p0), n_q, n_kv, _p(q_norm), _p(k_norm), _p(cos), _p(sin),
+                                     float(eps), _p(k_cache), _p(v_cache), max_seq, _p(q_out), _stream())
+        self._check(st, "prefill_qkv")
+
+    def prefill_attention(self, q, p0, k_cache, v_cache, scale, out):
+        """Causal GQA attention of the chunk's queries q [M, n_q, 128] over cache rows 0 .. p0+m; out bf16
+        [M, n_q * 128] (or [M, n_q, 128])."""
+        M, n_q = q.shape[0], q.shape[1]
+        n_kv, max_seq = k_cache.shape[0], k_cache.shape[1]
+        st = self.lib.qk_prefill_attention(_p(q), M, int(p0), n_q, n_kv, _p(k_cache), _p(v_cache), max_seq,
+                                           float(scale), _p(out), _stream())
+        self._check(st, "prefill_attention")
+
+    def add_rows(self, resid, y):
+        """resid = bf16(resid + y), elementwise."""
+        self._check(self.lib.qk_add_rows(_p(resid), _p(y), resid.numel(), _stream()), "add_rows")
+
+    def swiglu_rows(self, gu, h):
+        """h[m] = bf16(bf16(silu(gate)) * up) for gu = [gate | up] rows [M, 2I]; h [M, I]."""
+        M, I = h.shape
+        self._check(self.lib.qk_swiglu_rows(_p(gu), M, I, _p(h), _stream()), "swiglu_rows")
 
     def finalize(self, best, token, out_tokens, state):
         b = token.numel()

@@ -20,6 +20,9 @@ It restates, in plain torch CPU ops, the arithmetic of the reference engine
                    462-567): fp32 scores, fp32 softmax with the probabilities kept in fp32, fp32 P @ V,
                    rounded to bf16 once. `attn_impl="sdpa"` instead uses torch SDPA exactly as
                    model.py:271-272 does (bf16 probabilities), which is what the golden fixtures pin.
+* `prefill_layer`  Q/model.py:255-279 for M prompt positions at once (start..start+M-1): the same layer with
+                   the KV rows written for every position and causal attention (row m sees cache rows
+                   0..start+m), fp32 scores and probabilities, rounded to bf16 once.
 * `lm_head_argmax` Q/model.py:280-281 (final RMSNorm + linear) and Q/kernels/decode.cu:572-661: greedy
                    argmax over bf16 logits, ties to the lowest index.
 
@@ -158,6 +161,36 @@ def decode_layer(h: torch.Tensor, L: LayerW, k_cache: torch.Tensor, v_cache: tor
         trace.update(qkv=qkv, attn=attn, h_mid=h.clone(), act=a)
     h = h + fp8_linear(a[None].contiguous(), L.w_d, L.s_d)[0]
     return h
+
+
+def prefill_layer(h: torch.Tensor, L: LayerW, k_cache: torch.Tensor, v_cache: torch.Tensor, start: int,
+                  cos: torch.Tensor, sin: torch.Tensor, eps: float, n_heads: int = 32, n_kv: int = 8,
+                  head_dim: int = 128) -> torch.Tensor:
+    """M positions through one layer (the reference's batched forward). h bf16 [M, H]; k_cache/v_cache bf16
+    [n_kv, max_seq, 128] are written at start..start+M-1 in place. Returns the residual stream bf16 [M, H]."""
+    M, hd = h.shape[0], head_dim
+    x = rms_norm(h, L.ln1, eps)
+    qkv = fp8_linear(x, L.w_qkv, L.s_qkv)
+    q, k, v = qkv.split([n_heads * hd, n_kv * hd, n_kv * hd], dim=-1)
+    c, s = cos[start:start + M][:, None, :], sin[start:start + M][:, None, :]
+    q = norm_rope(q.reshape(M, n_heads, hd), L.q_norm, c, s, eps)
+    k = norm_rope(k.reshape(M, n_kv, hd), L.k_norm, c, s, eps)
+    k_cache[:, start:start + M] = k.transpose(0, 1)
+    v_cache[:, start:start + M] = v.reshape(M, n_kv, hd).transpose(0, 1)
+    ctx = start + M
+    K = k_cache[:, :ctx].float().repeat_interleave(n_heads // n_kv, 0)     # [n_heads, ctx, 128]
+    V = v_cache[:, :ctx].float().repeat_interleave(n_heads // n_kv, 0)
+    sc = torch.einsum("mhd,hjd->hmj", q.float(), K) * hd ** -0.5
+    pos = start + torch.arange(M, device=h.device)
+    sc = sc.masked_fill((torch.arange(ctx, device=h.device)[None, :] > pos[:, None])[None], float("-inf"))
+    attn = torch.einsum("hmj,hjd->mhd", torch.softmax(sc, dim=-1), V).reshape(M, n_heads * hd).to(torch.bfloat16)
+    h = h + fp8_linear(attn, L.w_o, L.s_o)
+    x = rms_norm(h, L.ln2, eps)
+    gu = fp8_linear(x, L.w_gu, L.s_gu)
+    I = gu.shape[-1] // 2
+    g, u = gu.split([I, I], dim=-1)
+    a = F.silu(g) * u
+    return h + fp8_linear(a.contiguous(), L.w_d, L.s_d)
 
 
 def lm_head_logits(h: torch.Tensor, norm_w: torch.Tensor, head_w: torch.Tensor, head_scale, eps: float):

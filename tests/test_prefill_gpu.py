@@ -1,0 +1,244 @@
+"""Chunked prefill (csrc/prefill.cuh, Engine.prefill_chunked) on the GPU.
+
+* The row-wise kernels: the residual add and SwiGLU round like the decode step's epilogues; the prompt
+  attention matches an fp32 causal GQA attention restated in torch (1983 + 64 positions included); the q/k
+  norm + RoPE + cache append writes the same K/V rows, bit for bit, as the decode step's attention op run at
+  each position on the same qkv row.
+* The whole prefill: a 2-layer synthetic model, prompt through `prefill_chunked` and, separately, fed
+  position by position through the decode graph (`prefill`), both against the reference's batched forward
+  restated in torch (oracle.prefill_layer). The three compute the same function with different fp32
+  summation orders (tensor-core GEMM with split K, the GEMV, torch's bmm; one-pass fp32 attention, the decode
+  step's split-and-merge), and an fp32 difference moves an e4m3 or bf16 rounding now and then; one e4m3 step
+  is 6 % of a value and later layers inherit every earlier flip (the two engine paths differ by 3.7e-2 rel-L2
+  in layer 1's K/V rows and 5e-2 in the logits). So the bar is relative: every layer's K/V rows and the
+  logits of the chunked path are no further from the restatement than the decode path's (1.5x plus a
+  rounding allowance), layer 0's K rows within 5e-3. The token streams (the first token, then 6 decode
+  steps) must agree wherever the decode path's top-2 logit gap is more than twice the largest logit
+  difference of that step.
+"""
+import pytest
+import torch
+
+import model as M
+from oracle import qwen3_ref as O
+
+pytestmark = pytest.mark.gpu
+EPS = 1e-6
+
+
+def rel(a, b):
+    a, b = a.float().flatten(), b.float().flatten()
+    return ((a - b).norm() / b.norm()).item()
+
+
+def ulp_diff(a, b):
+    """Distance in bf16 units in the last place (same-sign finite values)."""
+    ai = a.contiguous().view(torch.int16).to(torch.int32)
+    bi = b.contiguous().view(torch.int16).to(torch.int32)
+    return (ai - bi).abs()
+
+
+def test_add_rows_and_swiglu_rows_round_like_the_epilogues():
+    from kernels import ops
+    k = ops()
+    g = torch.Generator(device="cuda").manual_seed(5)
+    M_, H, I = 37, 4096, 12288
+    resid = torch.randn(M_, H, generator=g, device="cuda").to(torch.bfloat16)
+    y = (torch.randn(M_, H, generator=g, device="cuda") * 0.1).to(torch.bfloat16)
+    want = (resid.float() + y.float()).to(torch.bfloat16)
+    k.add_rows(resid, y)
+    torch.cuda.synchronize()
+    assert torch.equal(resid, want)
+
+    gu = (torch.randn(M_, 2 * I, generator=g, device="cuda") * 3).to(torch.bfloat16)
+    h = torch.empty(M_, I, dtype=torch.bfloat16, device="cuda")
+    k.swiglu_rows(gu, h)
+    torch.cuda.synchronize()
+    gt, up = gu[:, :I].float(), gu[:, I:].float()
+    act = (gt / (1.0 + torch.exp(-gt))).to(torch.bfloat16).float()
+    ref = (act * up).to(torch.bfloat16)
+    d = ulp_diff(h, ref)
+    same_sign = (h.float() * ref.float() > 0) | (ref.float() == h.float())
+    assert bool(same_sign.all())
+    assert int(d.max()) <= 1            # expf may differ from torch's exp in the last bit of a value
+    assert (d > 0).float().mean().item() < 1e-3
+    assert k.device_error() == 0
+
+
+def attention_fp32(q, kc, vc, p0, scale):
+    """Causal GQA attention in fp32: q [M, n_q, 128], caches [n_kv, max_seq, 128]; row m sees keys 0..p0+m."""
+    Mq, n_q, hd = q.shape
+    n_kv = kc.shape[0]
+    ctx = p0 + Mq
+    K = kc[:, :ctx].float().repeat_interleave(n_q // n_kv, 0)      # [n_q, ctx, 128]
+    V = vc[:, :ctx].float().repeat_interleave(n_q // n_kv, 0)
+    s = torch.einsum("mhd,hjd->hmj", q.float(), K) * scale          # [n_q, M, ctx]
+    pos = p0 + torch.arange(Mq, device=q.device)
+    mask = torch.arange(ctx, device=q.device)[None, :] > pos[:, None]
+    s = s.masked_fill(mask[None], float("-inf"))
+    p = torch.softmax(s, dim=-1)
+    o = torch.einsum("hmj,hjd->mhd", p, V)
+    return o.reshape(Mq, n_q * hd)
+
+
+@pytest.mark.parametrize("p0,Mq", [(0, 64), (700, 40), (1983, 64)])
+def test_prefill_attention_matches_fp32(p0, Mq):
+    from kernels import ops
+    k = ops()
+    n_q, n_kv, hd, max_seq = 32, 8, 128, 2048
+    g = torch.Generator(device="cuda").manual_seed(p0 + Mq)
+    kc = torch.randn(n_kv, max_seq, hd, generator=g, device="cuda").to(torch.bfloat16)
+    vc = torch.randn(n_kv, max_seq, hd, generator=g, device="cuda").to(torch.bfloat16)
+    q = (torch.randn(Mq, n_q, hd, generator=g, device="cuda") * 2).to(torch.bfloat16)
+    out = torch.empty(Mq, n_q * hd, dtype=torch.bfloat16, device="cuda")
+    k.prefill_attention(q, p0, kc, vc, hd ** -0.5, out)
+    torch.cuda.synchronize()
+    assert k.device_error() == 0
+    ref = attention_fp32(q, kc, vc, p0, hd ** -0.5)
+    e = rel(out, ref)
+    assert e < 5e-3, e
+    # row by row too: the causal mask must hold for the first rows, whose outputs are a few keys' values
+    per_row = [rel(out[m], ref[m]) for m in range(Mq)]
+    assert max(per_row) < 1e-2, max(per_row)
+
+
+def test_prefill_qkv_writes_the_decode_steps_cache_rows():
+    from kernels import ops
+    k = ops()
+    cfg = M.Config()
+    n_q, n_kv, hd, max_seq = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, 256
+    p0, Mq = 100, 40
+    g = torch.Generator(device="cuda").manual_seed(11)
+    qkv = torch.randn(Mq, (n_q + 2 * n_kv) * hd, generator=g, device="cuda").to(torch.bfloat16)
+    q_norm = M.synth_norm(0, "pf.qn", hd, "random", device="cuda")
+    k_norm = M.synth_norm(0, "pf.kn", hd, "random", device="cuda")
+    cos, sin = M.rope_tables(max_seq, hd, cfg.rope_theta, "cuda")
+    base_k = torch.randn(n_kv, max_seq, hd, generator=g, device="cuda").to(torch.bfloat16)
+    base_v = torch.randn(n_kv, max_seq, hd, generator=g, device="cuda").to(torch.bfloat16)
+
+    kc, vc = base_k.clone(), base_v.clone()
+    q = torch.empty(Mq, n_q, hd, dtype=torch.bfloat16, device="cuda")
+    k.prefill_qkv(qkv, p0, q_norm, k_norm, cos, sin, EPS, kc, vc, q)
+    torch.cuda.synchronize()
+    assert k.device_error() == 0
+
+    # the decode step's attention op, once per position, writes its K/V row from the same qkv row
+    kd, vd = base_k.clone(), base_v.clone()
+    splits = (max_seq + 63) // 64
+    o_part = torch.zeros(n_q, splits, hd, dtype=torch.float32, device="cuda")
+    ml_part = torch.zeros(n_q, splits, 2, dtype=torch.float32, device="cuda")
+    counters = torch.zeros(n_kv, dtype=torch.int32, device="cuda")
+    out = torch.empty(n_q * hd, dtype=torch.bfloat16, device="cuda")
+    for m in range(Mq):
+        state = torch.tensor([p0 + m, 0], dtype=torch.int32, device="cuda")
+        k.attention(qkv[m].contiguous(), q_norm, k_norm, cos, sin, state, kd, vd, o_part, ml_part, counters, out,
+                    hd ** -0.5, EPS)
+    torch.cuda.synchronize()
+    assert k.device_error() == 0
+    assert torch.equal(kc, kd)
+    assert torch.equal(vc, vd)
+    # rows outside p0 .. p0+M-1 untouched
+    assert torch.equal(kc[:, :p0], base_k[:, :p0]) and torch.equal(kc[:, p0 + Mq:], base_k[:, p0 + Mq:])
+
+    # q: the oracle's per-head RMSNorm + RoPE within one bf16 step of the head's largest value
+    qc, cc, sc = qkv.cpu(), cos.cpu(), sin.cpu()
+    for m in (0, 17, Mq - 1):
+        pos = p0 + m
+        want = O.norm_rope(qc[m, :n_q * hd].view(n_q, hd), q_norm.cpu(), cc[pos], sc[pos], EPS)
+        got = q[m].cpu()
+        tol = 2 ** -7 * want.float().abs().amax(dim=1, keepdim=True)
+        assert bool(((got.float() - want.float()).abs() <= tol).all())
+
+
+def decode_steps(eng, n):
+    """n graph replays of the decode step: each step's token and logits."""
+    toks, logits = [], []
+    for _ in range(n):
+        eng.step(1)
+        toks.append(eng.token.clone())
+        logits.append(eng.logits.clone())
+    torch.cuda.synchronize()
+    return [int(t) for t in toks], logits
+
+
+def check_streams(toks_a, logits_a, toks_b, logits_b):
+    """Token streams agree until the first step whose decode-path top-2 gap is within twice that step's largest
+    logit difference (a near-tie); after a tie the streams may diverge and are not compared."""
+    for i, (ta, tb) in enumerate(zip(toks_a, toks_b)):
+        la, lb = logits_a[i].float(), logits_b[i].float()
+        assert rel(lb, la) < 1e-1, (i, rel(lb, la))
+        top2 = la.topk(2).values
+        gap, err = float(top2[0] - top2[1]), float((la - lb).abs().max())
+        if ta != tb:
+            assert gap <= 2 * err, f"step {i}: tokens {ta} vs {tb}, top-2 gap {gap:.4f}, logit error {err:.4f}"
+            return
+
+
+def restated_prefill(eng, ids):
+    """The reference's batched forward restated in torch on the GPU (oracle.prefill_layer over the whole
+    prompt, then the final norm and head on the last row): per layer K/V rows [n_kv, P, 128] and the logits."""
+    m, cfg = eng.m, eng.m.cfg
+    P = len(ids)
+    h = m.embed[torch.as_tensor(ids, device="cuda")]
+    kv = []
+    for li, L in enumerate(m.layers):
+        wq, wo, wgu, wd = eng.rowmajor_weights()[li]
+        LW = O.LayerW(L.ln1, L.ln2, L.q_norm, L.k_norm, wq, L.qkv.scale, wo, L.o.scale, wgu, L.gu.scale, wd,
+                      L.down.scale)
+        kc = torch.zeros(cfg.n_kv_heads, P, cfg.head_dim, dtype=torch.bfloat16, device="cuda")
+        vc = torch.zeros_like(kc)
+        h = O.prefill_layer(h, LW, kc, vc, 0, m.cos, m.sin, cfg.eps)
+        kv.append((kc, vc))
+    if isinstance(m.lm_head, M.Linear):
+        head_w = M.unpack_fp8(m.lm_head.packed, m.lm_head.N, m.lm_head.K)
+        logits = O.lm_head_logits(h[-1], m.norm, head_w, m.lm_head.scale, cfg.eps)
+    else:
+        logits = O.lm_head_logits(h[-1], m.norm, m.lm_head, None, cfg.eps)
+    return kv, logits
+
+
+@pytest.mark.parametrize("scale_mode,head,P,chunk", [("channel", "fp8", 100, 64), ("block", "bf16", 64, 64),
+                                                     ("channel", "fp8", 7, 64), ("channel", "bf16", 45, 16)])
+def test_prefill_chunked_matches_decode_prefill(scale_mode, head, P, chunk):
+    from generate import Engine
+    cfg = M.Config(layers=2, vocab=4096)
+    m = M.Qwen3FP8Decode.synthetic(cfg, max_seq=512, seed=3, scale_mode=scale_mode, head_dtype=head,
+                                   norm_init="random")
+    eng = Engine(m)
+    g = torch.Generator().manual_seed(P)
+    ids = torch.randint(0, cfg.vocab, (P,), generator=g).tolist()
+    ref_kv, ref_logits = restated_prefill(eng, ids)
+
+    tok_a = int(eng.prefill(ids))
+    torch.cuda.synchronize()
+    state_a = eng.state.cpu()
+    logits_a0 = eng.logits.clone()
+    kc_a, vc_a = m.k_cache[:, 0, :, :P].clone(), m.v_cache[:, 0, :, :P].clone()
+    toks_a, logits_a = decode_steps(eng, 6)
+
+    m.k_cache.zero_()
+    m.v_cache.zero_()
+    tok_b = int(eng.prefill_chunked(ids, chunk=chunk))
+    torch.cuda.synchronize()
+    eng.check()
+    assert state_a.tolist() == [P, 0]
+    assert eng.state.cpu().tolist() == [P, 0]
+    logits_b0 = eng.logits.clone()
+    # Against the restated forward: the chunked path's K/V rows and logits are no further from it than the
+    # decode path's (which is checked bit for bit against the reference's own decode kernels elsewhere).
+    report = []
+    for li in range(cfg.layers):
+        for name, got_c, got_d, want in (("k", m.k_cache[li, 0, :, :P], kc_a[li], ref_kv[li][0]),
+                                         ("v", m.v_cache[li, 0, :, :P], vc_a[li], ref_kv[li][1])):
+            e_c, e_d = rel(got_c, want), rel(got_d, want)
+            report.append((li, name, round(e_c, 5), round(e_d, 5)))
+            assert e_c <= 1.5 * e_d + 2e-3, report
+    e_c, e_d = rel(logits_b0, ref_logits), rel(logits_a0, ref_logits)
+    report.append(("logits", round(e_c, 5), round(e_d, 5)))
+    assert e_c <= 1.5 * e_d + 5e-3, report
+    assert rel(m.k_cache[0, 0, :, :P], ref_kv[0][0]) < 5e-3, report   # layer 0: rounding flips only
+    # nothing written past the prompt
+    assert not bool(m.k_cache[:, 0, :, P:].any()) and not bool(m.v_cache[:, 0, :, P:].any())
+    toks_b, logits_b = decode_steps(eng, 6)
+    eng.check()
+    check_streams([tok_a] + toks_a, [logits_a0] + logits_a, [tok_b] + toks_b, [logits_b0] + logits_b)
