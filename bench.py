@@ -571,10 +571,11 @@ def run_profile_kernel(args):
         print(f"profiled decode_step ({args.layers} layers, vocab 16384) x{args.launches}; algorithmic bytes per "
               f"launch {alg:.0f}")
         return
-    if args.profile_kernel == "gemm_rows":   # the tcgen05 batched linear, gate_up shape, 64 rows
+    if args.profile_kernel == "gemm_rows":   # the tcgen05 batched linear, gate_up shape, 64 rows (or --rows)
+        rows = int(args.rows) if args.rows else 64
         w, s = M.synth_linear(0, "prof.gemm", 24576, 4096, "channel", device=dev)
-        x = torch.randn(64, 4096, device=dev).to(torch.bfloat16)
-        out = torch.empty(64, 24576, dtype=torch.bfloat16, device=dev)
+        x = torch.randn(rows, 4096, device=dev).to(torch.bfloat16)
+        out = torch.empty(rows, 24576, dtype=torch.bfloat16, device=dev)
         for _ in range(args.launches):
             k.fp8_gemm_rows(x, w, s, out)
         torch.cuda.synchronize()
@@ -869,7 +870,7 @@ def run_attention_sweep(args):
 
 def run_prefill(args):
     """Prompt processing on the benchmarked model (36 layers, per-channel FP8 scales, FP8 head): a P-token
-    synthetic prompt through Engine.prefill_chunked (the batched forward, 64 positions per pass: the tcgen05
+    synthetic prompt through Engine.prefill_chunked (the batched forward, 128 positions per pass: the tcgen05
     FP8 linear plus the row-wise prefill kernels) against the same prompt fed position by position through the
     fused decode step (Engine.prefill). Prints one JSON line: prompt tokens/s of each path, the chunked path's
     algorithmic weight stream (every layer's weights once per chunk, the head once) in GB/s and as a fraction
@@ -878,14 +879,14 @@ def run_prefill(args):
     import model as M
     from generate import Engine
     peak, peak_kind = peaks()
-    P, chunk = args.prompt, 64
+    P, chunk = args.prompt, args.prefill_chunk
     K, W = max(1, min(args.steps, 8)), max(args.warmup, 3)
     cfg = M.Config()
     m = M.Qwen3FP8Decode.synthetic(cfg, max_seq=4096, device="cuda", seed=args.seed, scale_mode=args.scale,
                                    head_dtype=args.head, norm_init="ones")
     eng = Engine(m, fused=True)
     ids = torch.randint(0, cfg.vocab, (P,), generator=torch.Generator().manual_seed(7)).tolist()
-    eng.rowmajor_weights()
+    eng.prefill_weights()
     for _ in range(W):
         eng.prefill_chunked(ids, chunk)
     torch.cuda.synchronize()
@@ -962,6 +963,7 @@ def main():
     ap.add_argument("--prefill", action="store_true",
                     help="prompt processing: chunked prefill against the decode-path prefill (--prompt tokens)")
     ap.add_argument("--prompt", type=int, default=512, help="--prefill: prompt length")
+    ap.add_argument("--prefill-chunk", type=int, default=128, help="--prefill: positions per batched pass (1..128)")
     ap.add_argument("--timeline", action="store_true",
                     help="one fused-step launch with per-phase timeline stamps, summarised (36 layers unless --layers)")
     args = ap.parse_args()

@@ -235,12 +235,13 @@ int qk_embed(const int* token, const void* table, void* resid, int vocab, int ba
 int qk_finalize(unsigned long long* best, int* token, int* out_tokens, int* state, int out_len, int batch,
                 qk_stream_t stream);
 
-/* Batched FP8 W8A8 linear on the tcgen05 tensor cores (1-64 rows: the batched GEMV rows and prefill chunks; the
+/* Batched FP8 W8A8 linear on the tcgen05 tensor cores (1-128 rows: the batched GEMV rows and prefill chunks; the
  * reference's batched path is its Triton fp8_matmul, prefill.py:121-156, with act_quant :23-41): out[m][n] = bf16(sum over K blocks
- * kb of dot_kb(q(x[m]), w[n]) * s_x[m][kb] * s_w[n][kb]) for M = 1..64 rows, where q() is the per-128-group e4m3
+ * kb of dot_kb(q(x[m]), w[n]) * s_x[m][kb] * s_w[n][kb]) for M = 1..128 rows (per-channel scales: the sum of
+ * dot_kb * s_x[m][kb], times s_w[n]), where q() is the per-128-group e4m3
  * quantizer of the GEMV (optionally after RMSNorm with norm_w). x bf16 [M][K]; w fp8 row-major [N][K] (plain
  * matrix, TMA boxes; not the GEMV's packed layout); w_scale fp32 [N] (QK_SCALE_CHANNEL) or [N/128][K/128];
- * out bf16 [M][N]; N and K multiples of 128, N <= 1,048,576, K <= 16384. scratch: at least
+ * out bf16 [M][N]; N and K multiples of 128, N <= 1,048,576, K <= 16384 (12288 above 64 rows). scratch: at least
  * qk_fp8_gemm_rows_scratch_bytes(M, N, K) bytes, 256-byte aligned, zeroed once before the first call (its first
  * 32 KiB hold the tile counters, which every call leaves zero, so one buffer serves calls of any shape). Results match the oracle's
  * recipe to rounding (split-K boundaries reorder the fp32 sum), not bit for bit. */
@@ -248,6 +249,13 @@ long long qk_fp8_gemm_rows_scratch_bytes(int M, int N, int K);
 int qk_fp8_gemm_rows(const void* x, const void* norm_w, int M, int K, const void* w, const float* w_scale,
                      int scale_mode, int N, float eps, void* out, void* scratch, long long scratch_bytes,
                      qk_stream_t stream);
+/* The same linear with the weights tile-packed (no tensor maps): w_tiles is [N/128][K/128] tiles of 128 rows x
+ * 128 k, 16,384 bytes each, row r of a tile at byte 128 r and its 16-byte chunk c at chunk c ^ (r % 8) (the
+ * image a 128-byte-swizzled TMA box would leave in shared memory; `model.pack_fp8_tiles` builds it). Each CTA's
+ * weight range is then one contiguous stream of bulk copies. Same arguments, scratch and results otherwise. */
+int qk_fp8_gemm_tiles(const void* x, const void* norm_w, int M, int K, const void* w_tiles, const float* w_scale,
+                      int scale_mode, int N, float eps, void* out, void* scratch, long long scratch_bytes,
+                      qk_stream_t stream);
 
 /* Chunked prefill: the row-wise steps of the reference's batched forward (Q/model.py:243-281, with the fused
  * prefill kernels of Q/kernels/prefill_fused.py:57-183), run on a chunk of M prompt positions p0 .. p0+M-1

@@ -1,5 +1,5 @@
 // Batched FP8 W8A8 linear on the 5th-generation tensor cores (tcgen05), for a few activation rows at a time
-// (decode batches of 2..64 sequences, or a prefill chunk of up to 64 positions):
+// (decode batches of 2..128 sequences, or a prefill chunk of up to 128 positions):
 //
 //   Y[m, n] = bf16( sum over K blocks kb, in order, of  D_kb[m, n] * s_x[m, kb] * s_w[n (, kb)] ),
 //   D_kb[m, n] = the fp32 dot of the e4m3 activations and weights over the 128 k of block kb,
@@ -18,9 +18,10 @@
 //    reading both operands straight from shared memory, then commits to the stage's `empty` barrier and to
 //    the accumulator's `dfull` barrier;
 //  * warps 2-9 (TMEM lane quarters 2, 3, 0, 1, twice: warps 2-5 take activation rows [0, MP/2), warps 6-9 the
-//    rest) read each K block's dots with tcgen05.ld, free the accumulator, and fold them into fp32 registers,
-//    acc[m] += (D * s_x[m, kb]) * s_w, in K order (the activation scales staged in shared memory once, K-block
-//    major, and each pair's weight scale fetched one pair ahead).
+//    rest) read each K block's dots with tcgen05.ld, free the accumulator, and fold them into fp32 registers in
+//    K order: acc[m] += (D * s_x[m, kb]) * s_w[n, kb] for block scales; for per-channel scales, which do not
+//    change with kb, acc[m] += D * s_x[m, kb] and the CTA's piece of the tile is multiplied by s_w[n] once
+//    (the activation scales staged in shared memory once, K-block major, the weight scales per CTA).
 // A tile whose pairs lie in one CTA is stored directly (bf16). A tile split between consecutive CTAs: every
 // piece stores its fp32 partial in `part` (slot 0 for a CTA's first tile, 1 for its last) and counts itself on
 // the tile's counter; the CTA that completes the count adds the pieces in CTA order and stores the tile.
@@ -36,13 +37,21 @@ constexpr int TC_TILE = 128;          // weight rows per tile (the UMMA M)
 constexpr int TC_BK = 128;            // K per pair: one activation quant group, one weight scale block
 constexpr int TC_EPI_WARPS = 8;       // two per TMEM lane quarter, each folding half of the activation rows
 constexpr int TC_THREADS = (2 + TC_EPI_WARPS) * 32;   // warp 0 producer, warp 1 MMA issuer and TMEM owner
-constexpr int TC_MAX_ROWS = 64;
+constexpr int TC_MAX_ROWS = 128;
 constexpr int TC_MAX_KB = 16384 / TC_BK;
+constexpr int TC_MAX_KB_128 = 12288 / TC_BK;   // 128 padded rows: K up to 12,288 (the activation scales' room)
 constexpr int TC_MAX_TILES = 8192;    // the tile counters' fixed region: N up to 1,048,576 rows
+constexpr int TC_SW_MAX = 2048;       // weight scales staged in shared memory per CTA (16 tiles' channels)
 
 struct TcGemmParams {
   CUtensorMap tm_w;     // weights fp8 [N][K] row-major: box {128, 128}, 128-byte swizzle
   CUtensorMap tm_x;     // activations fp8 [M][K]: box {128, MP}, 128-byte swizzle, rows >= M read as zero
+  // Tile-packed operands (both set, or both null for the tensor maps above): the weights as
+  // [N/128][K/128] tiles of 16 KiB and the activations as [K/128] tiles of MP x 128 B, each tile already in
+  // the 128-byte-swizzle K-major image the MMAs read, so one bulk copy per operand and pair fills a stage
+  // and a CTA's weight range is one contiguous stream.
+  const uint8_t* w_tiles;
+  const uint8_t* x_tiles;
   const float* sx;      // activation scales [M][K/128]
   const float* sw;      // weight scales [N] (per channel) or [N/128][K/128] (block)
   bf16* out;            // [M][N]
@@ -52,11 +61,15 @@ struct TcGemmParams {
   int scale_block;
 };
 
-// Ring depth and accumulator count per padded row count: the ring fills ~200 KiB of shared memory, the
-// accumulators at most 256 of the 512 TMEM columns.
+// Ring depth and accumulator count per padded row count: the ring fills 160-200 KiB of shared memory, the
+// accumulators at most 512 TMEM columns (128 rows: four of 128 columns).
 template <int MP>
 __host__ __device__ constexpr int tc_stages() {
-  return MP >= 64 ? 7 : (MP >= 32 ? 8 : 9);
+  return MP >= 128 ? 5 : (MP >= 64 ? 7 : (MP >= 32 ? 8 : 9));
+}
+template <int MP>
+__host__ __device__ constexpr int tc_max_kb() {
+  return MP >= 128 ? TC_MAX_KB_128 : TC_MAX_KB;
 }
 template <int MP>
 __host__ __device__ constexpr int tc_naccs() {
@@ -72,7 +85,8 @@ struct TcSmem {
   uint64_t dfull[A], dempty[A];
   uint32_t tmem_base;
   int last;
-  alignas(16) float sxs[TC_MAX_KB * MP];   // the activation scales, K-block major: sxs[kb * MP + m] (zero for m >= M)
+  alignas(16) float sxs[tc_max_kb<MP>() * MP];   // the activation scales, K-block major: sxs[kb * MP + m] (0 for m >= M)
+  float sws[TC_SW_MAX];   // the CTA's weight scales: per channel, its tiles' rows; per block, one per pair
 };
 
 // Instruction descriptor of tcgen05.mma.kind::f8f6f4: D fp32, A and B e4m3, both K-major, M = 128, N = MP.
@@ -155,7 +169,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) fp8_gemm_tc_kernel(const __grid
     for (int i = 0; i < min(S, nu); ++i) {
       const int u = u0 + i, t = u / KB, kb = u - t * KB;
       mbar_arrive_expect_tx(&sm.full[i], TC_TILE * TC_BK + MP * TC_BK);
-      tma_load_2d(sm.w[i], &p.tm_w, kb * TC_BK, t * TC_TILE, &sm.full[i]);
+      if (p.w_tiles)
+        bulk_g2s(sm.w[i], p.w_tiles + (size_t)u * (TC_TILE * TC_BK), TC_TILE * TC_BK, &sm.full[i], policy_evict_first());
+      else
+        tma_load_2d(sm.w[i], &p.tm_w, kb * TC_BK, t * TC_TILE, &sm.full[i]);
     }
   }
   if (warp == 1) {
@@ -164,6 +181,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) fp8_gemm_tc_kernel(const __grid
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
+  // The weight scales of the CTA's pairs go to shared memory before the wait (like the weights, they are no
+  // earlier kernel's output), so the epilogue's fold never waits on a global load. Ranges too long to stage
+  // (more than 16 tiles per CTA) read them from global memory.
+  const int t_first = u0 / KB, t_last = nu > 0 ? (u1 - 1) / KB : t_first;
+  const int n_sw = p.scale_block ? nu : (t_last - t_first + 1) * TC_TILE;
+  const bool sw_staged = n_sw <= TC_SW_MAX;
+  if (sw_staged)
+    for (int i = threadIdx.x; i < n_sw; i += TC_THREADS)
+      sm.sws[i] = p.scale_block ? __ldg(p.sw + u0 + i) : __ldg(p.sw + (size_t)t_first * TC_TILE + i);
   grid_dep_wait();   // the quantized activations, their scales and the output buffer are the previous kernels'
   for (int i = threadIdx.x; i < MP * KB; i += TC_THREADS) {
     const int kb = i / MP, m = i - kb * MP;
@@ -176,14 +202,24 @@ __global__ void __launch_bounds__(TC_THREADS, 1) fp8_gemm_tc_kernel(const __grid
 
   if (warp == 0) {
     if (lane == 0) {   // producer
-      for (int i = 0; i < min(S, nu); ++i) tma_load_2d(sm.x[i], &p.tm_x, ((u0 + i) % KB) * TC_BK, 0, &sm.full[i]);
+      const uint64_t pol = policy_evict_first();
+      auto load_x = [&](int s, int kb) {
+        if (p.x_tiles)
+          bulk_g2s(sm.x[s], p.x_tiles + (size_t)kb * (MP * TC_BK), MP * TC_BK, &sm.full[s]);
+        else
+          tma_load_2d(sm.x[s], &p.tm_x, kb * TC_BK, 0, &sm.full[s]);
+      };
+      for (int i = 0; i < min(S, nu); ++i) load_x(i, (u0 + i) % KB);
       for (int i = S; i < nu; ++i) {
         const int s = i % S;
         if (i >= S && !mbar_wait(&sm.empty[s], (uint32_t)(((i / S) - 1) & 1))) break;
         const int u = u0 + i, t = u / KB, kb = u - t * KB;
         mbar_arrive_expect_tx(&sm.full[s], TC_TILE * TC_BK + MP * TC_BK);
-        tma_load_2d(sm.w[s], &p.tm_w, kb * TC_BK, t * TC_TILE, &sm.full[s]);
-        tma_load_2d(sm.x[s], &p.tm_x, kb * TC_BK, 0, &sm.full[s]);
+        if (p.w_tiles)
+          bulk_g2s(sm.w[s], p.w_tiles + (size_t)u * (TC_TILE * TC_BK), TC_TILE * TC_BK, &sm.full[s], pol);
+        else
+          tma_load_2d(sm.w[s], &p.tm_w, kb * TC_BK, t * TC_TILE, &sm.full[s]);
+        load_x(s, kb);
       }
     }
   } else if (warp == 1) {
@@ -206,10 +242,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) fp8_gemm_tc_kernel(const __grid
              // activation rows [h * MP / 2, (h + 1) * MP / 2) with h = (warp - 2) / 4
     constexpr int HM = MP / 2;
     const int q = warp & 3, r = 32 * q + lane, h = (warp - 2) / 4, m0 = h * HM;
-    const int t_first = u0 / KB;
-    auto w_scale = [&](int u) {
-      const int t = u / KB;
-      return p.scale_block ? __ldg(p.sw + (size_t)t * KB + (u - t * KB)) : __ldg(p.sw + t * TC_TILE + r);
+    auto w_scale = [&](int u) {   // block scales [N/128][K/128]: pair u = t * KB + kb is element u
+      if (sw_staged) return p.scale_block ? sm.sws[u - u0] : sm.sws[(u / KB - t_first) * TC_TILE + r];
+      return p.scale_block ? __ldg(p.sw + u) : __ldg(p.sw + (u / KB) * TC_TILE + r);
     };
     float acc[HM];
 #pragma unroll
@@ -232,15 +267,31 @@ __global__ void __launch_bounds__(TC_THREADS, 1) fp8_gemm_tc_kernel(const __grid
       const float swv = sw_next;
       if (i + 1 < nu) sw_next = w_scale(u + 1);
       const float* sxk = sm.sxs + kb * MP + m0;
+      // rows past M fold zeros (their scale is 0) and are never stored
+      if (p.scale_block) {   // the block's weight scale varies with kb: acc += (D * s_x) * s_w per block
 #pragma unroll
-      for (int mm = 0; mm < HM; mm += 4) {   // rows past M fold zeros (their scale is 0) and are never stored
-        const float4 sx4 = *reinterpret_cast<const float4*>(sxk + mm);
-        acc[mm] += (__uint_as_float(d[mm / 8][mm % 8]) * sx4.x) * swv;
-        acc[mm + 1] += (__uint_as_float(d[mm / 8][mm % 8 + 1]) * sx4.y) * swv;
-        acc[mm + 2] += (__uint_as_float(d[mm / 8][mm % 8 + 2]) * sx4.z) * swv;
-        acc[mm + 3] += (__uint_as_float(d[mm / 8][mm % 8 + 3]) * sx4.w) * swv;
+        for (int mm = 0; mm < HM; mm += 4) {
+          const float4 sx4 = *reinterpret_cast<const float4*>(sxk + mm);
+          acc[mm] += (__uint_as_float(d[mm / 8][mm % 8]) * sx4.x) * swv;
+          acc[mm + 1] += (__uint_as_float(d[mm / 8][mm % 8 + 1]) * sx4.y) * swv;
+          acc[mm + 2] += (__uint_as_float(d[mm / 8][mm % 8 + 2]) * sx4.z) * swv;
+          acc[mm + 3] += (__uint_as_float(d[mm / 8][mm % 8 + 3]) * sx4.w) * swv;
+        }
+      } else {               // one weight scale per row: acc += D * s_x, times s_w once the piece is summed
+#pragma unroll
+        for (int mm = 0; mm < HM; mm += 4) {
+          const float4 sx4 = *reinterpret_cast<const float4*>(sxk + mm);
+          acc[mm] = fmaf(__uint_as_float(d[mm / 8][mm % 8]), sx4.x, acc[mm]);
+          acc[mm + 1] = fmaf(__uint_as_float(d[mm / 8][mm % 8 + 1]), sx4.y, acc[mm + 1]);
+          acc[mm + 2] = fmaf(__uint_as_float(d[mm / 8][mm % 8 + 2]), sx4.z, acc[mm + 2]);
+          acc[mm + 3] = fmaf(__uint_as_float(d[mm / 8][mm % 8 + 3]), sx4.w, acc[mm + 3]);
+        }
       }
       if (kb != KB - 1 && i != nu - 1) continue;
+      if (!p.scale_block) {
+#pragma unroll
+        for (int mm = 0; mm < HM; ++mm) acc[mm] *= swv;
+      }
       // the end of this CTA's piece of tile t
       const bool whole = max(u0, t * KB) == t * KB && u == t * KB + KB - 1;
       if (whole) {
@@ -300,15 +351,27 @@ __global__ void __launch_bounds__(TC_THREADS, 1) fp8_gemm_tc_kernel(const __grid
 }
 
 // x bf16 [M][K] -> optional RMSNorm per row (as the GEMV prologue: bf16(w * bf16(x * rstd))) -> e4m3 per 128-group
-// (s = amax / 448 with div.full, round to nearest even, saturating; a zero group gives zeros) -> qx [M][K], sx
-// [M][K/128]. One CTA of 256 threads per row.
+// (s = amax / 448 with div.full, round to nearest even, saturating; a zero group gives zeros) -> qx, sx [M][K/128].
+// qx is row-major [M][K] (tiled_mp = 0), or tiles [K/128][tiled_mp][128 B] in the 128-byte-swizzle image (16-byte
+// chunk c of row m at chunk c ^ (m % 8)), rows M .. tiled_mp - 1 zero. One CTA of 256 threads per row (grid M, or
+// tiled_mp when tiled).
 __global__ void __launch_bounds__(256) quantize_rows_kernel(const bf16* __restrict__ x, const bf16* __restrict__ norm_w,
-                                                            int K, float eps, uint8_t* __restrict__ qx,
-                                                            float* __restrict__ sx) {
+                                                            int M, int K, float eps, uint8_t* __restrict__ qx,
+                                                            float* __restrict__ sx, int tiled_mp) {
   __shared__ float red[8];
   const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   grid_dep_wait();     // x is the previous kernel's output
   grid_dep_launch();   // the GEMM may start its weight stream now; it waits for this grid before reading qx
+  // byte offset of k (a multiple of 4) of this row in qx
+  auto qx_at = [&](int k) -> size_t {
+    if (!tiled_mp) return (size_t)row * K + k;
+    const int kb = k / QB, c = (k % QB) / 16;
+    return ((size_t)kb * tiled_mp + row) * QB + ((c ^ (row & 7)) * 16) + (k & 15);
+  };
+  if (row >= M) {   // a padding row of the tiled layout
+    for (int k = tid * 4; k < K; k += 256 * 4) *reinterpret_cast<uint32_t*>(qx + qx_at(k)) = 0u;
+    return;
+  }
   const bf16* xr = x + (size_t)row * K;
   float rstd = 1.f;
   if (norm_w) {
@@ -337,7 +400,7 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const bf16* __restri
     float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
     amax = warp_max(amax);
     const float s = div_full(amax, 448.0f);
-    *reinterpret_cast<uint32_t*>(qx + (size_t)row * K + k0) = quant4(v[0], v[1], v[2], v[3], s);
+    *reinterpret_cast<uint32_t*>(qx + qx_at(k0)) = quant4(v[0], v[1], v[2], v[3], s);
     if (lane == 0) sx[(size_t)row * KB + g] = s;
   }
 }

@@ -1,4 +1,4 @@
-// Chunked prefill: a prompt chunk of up to 64 positions through the decoder layers, with the tcgen05 batched
+// Chunked prefill: a prompt chunk of up to 128 positions through the decoder layers, with the tcgen05 batched
 // linear (gemm_tc.cuh) for the four projections and these row-wise kernels around it:
 //
 //   resid[M]    = embed rows of the chunk's tokens                              embed_rows_kernel

@@ -630,7 +630,7 @@ int qk_argmax_key_flip(unsigned long long* keys, int n, qk_stream_t stream) {
 
 // ---- batched FP8 linear on the tcgen05 tensor cores ----------------------------------------------------------
 namespace {
-int gemm_rows_pad(int M) { return M <= 16 ? 16 : (M <= 32 ? 32 : 64); }
+int gemm_rows_pad(int M) { return M <= 16 ? 16 : (M <= 32 ? 32 : (M <= 64 ? 64 : 128)); }
 struct GemmScratch { size_t qx, sx, part, counters, total; };
 // The tile counters come first, in a region of fixed size, so that they stay zero from call to call whatever
 // the shapes (every call leaves them zero); the quantized activations, their scales and the split-tile partials
@@ -641,7 +641,7 @@ GemmScratch gemm_scratch_layout(int M, int N, int K, int grid) {
   (void)N;
   L.counters = 0;
   L.qx = up((size_t)TC_MAX_TILES * 4);
-  L.sx = L.qx + up((size_t)M * K);
+  L.sx = L.qx + up((size_t)gemm_rows_pad(M) * K);   // room for the tiled layout's padding rows
   L.part = L.sx + up((size_t)M * (K / QB) * 4);
   L.total = L.part + up((size_t)grid * 2 * TC_TILE * gemm_rows_pad(M) * 4);
   return L;
@@ -650,18 +650,22 @@ GemmScratch gemm_scratch_layout(int M, int N, int K, int grid) {
 
 extern "C" long long qk_fp8_gemm_rows_scratch_bytes(int M, int N, int K) {
   if (M < 1 || M > TC_MAX_ROWS || N < TC_TILE || N % TC_TILE || N / TC_TILE > TC_MAX_TILES || K < TC_BK ||
-      K % TC_BK || K > 16384)
+      K % TC_BK || K > (M > 64 ? 12288 : 16384))
     return -1;
   return (long long)gemm_scratch_layout(M, N, K, device_sms()).total;
 }
 
-extern "C" int qk_fp8_gemm_rows(const void* x, const void* norm_w, int M, int K, const void* w, const float* w_scale,
-                                int scale_mode, int N, float eps, void* out, void* scratch, long long scratch_bytes,
-                                qk_stream_t stream) {
+namespace {
+// The batched linear with row-major operands through tensor maps (tiles == false) or tile-packed operands
+// through bulk copies (tiles == true).
+int gemm_rows_impl(bool tiles, const void* x, const void* norm_w, int M, int K, const void* w, const float* w_scale,
+                   int scale_mode, int N, float eps, void* out, void* scratch, long long scratch_bytes,
+                   qk_stream_t stream) {
   if (!x || !w || !w_scale || !out || !scratch) return fail(QK_EINVAL, "null pointer argument");
   if (M < 1 || M > TC_MAX_ROWS) return fail(QK_EINVAL, "M=%d rows: 1..%d per call", M, TC_MAX_ROWS);
-  if (N < TC_TILE || N % TC_TILE || N / TC_TILE > TC_MAX_TILES || K < TC_BK || K % TC_BK || K > 16384)
-    return fail(QK_EINVAL, "N=%d, K=%d: both multiples of 128 (N at most %d, K at most 16384)", N, K, TC_MAX_TILES * TC_TILE);
+  if (N < TC_TILE || N % TC_TILE || N / TC_TILE > TC_MAX_TILES || K < TC_BK || K % TC_BK || K > (M > 64 ? 12288 : 16384))
+    return fail(QK_EINVAL, "N=%d, K=%d: both multiples of 128 (N at most %d, K at most 16384, or 12288 above 64 rows)", N,
+                K, TC_MAX_TILES * TC_TILE);
   if (scale_mode != QK_SCALE_BLOCK128 && scale_mode != QK_SCALE_CHANNEL) return fail(QK_EINVAL, "bad scale_mode %d", scale_mode);
   if (!aligned(x, 16) || !aligned(w, 16) || !aligned(out, 16) || !aligned(scratch, 256) || (norm_w && !aligned(norm_w, 16)))
     return fail(QK_EINVAL, "x, w and out must be 16-byte aligned, scratch 256-byte aligned");
@@ -673,9 +677,14 @@ extern "C" int qk_fp8_gemm_rows(const void* x, const void* norm_w, int M, int K,
     return fail(QK_EINVAL, "scratch too small: %lld bytes, need qk_fp8_gemm_rows_scratch_bytes = %zu", scratch_bytes, L.total);
   unsigned char* sc = static_cast<unsigned char*>(scratch);
   TcGemmParams p = {};
-  if (int r = encode_fp8_rows_map(&p.tm_w, w, N, K, TC_TILE)) return r;
   const int mp = gemm_rows_pad(M);
-  if (int r = encode_fp8_rows_map(&p.tm_x, sc + L.qx, M, K, mp)) return r;
+  if (tiles) {
+    p.w_tiles = static_cast<const uint8_t*>(w);
+    p.x_tiles = sc + L.qx;
+  } else {
+    if (int r = encode_fp8_rows_map(&p.tm_w, w, N, K, TC_TILE)) return r;
+    if (int r = encode_fp8_rows_map(&p.tm_x, sc + L.qx, M, K, mp)) return r;
+  }
   p.sx = reinterpret_cast<const float*>(sc + L.sx);
   p.sw = w_scale;
   p.out = static_cast<bf16*>(out);
@@ -686,8 +695,9 @@ extern "C" int qk_fp8_gemm_rows(const void* x, const void* norm_w, int M, int K,
   p.K = K;
   p.scale_block = scale_mode == QK_SCALE_BLOCK128;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (int r = launch(quantize_rows_kernel, dim3(M), dim3(256), 0, st, static_cast<const bf16*>(x),
-                     static_cast<const bf16*>(norm_w), K, eps, sc + L.qx, reinterpret_cast<float*>(sc + L.sx)))
+  if (int r = launch(quantize_rows_kernel, dim3(tiles ? mp : M), dim3(256), 0, st, static_cast<const bf16*>(x),
+                     static_cast<const bf16*>(norm_w), M, K, eps, sc + L.qx, reinterpret_cast<float*>(sc + L.sx),
+                     tiles ? mp : 0))
     return r;
   auto run = [&](auto kernel, size_t smem) -> int {
     if (int r = ensure_smem((const void*)kernel, (int)smem)) return r;
@@ -695,7 +705,22 @@ extern "C" int qk_fp8_gemm_rows(const void* x, const void* norm_w, int M, int K,
   };
   if (mp == 16) return run(fp8_gemm_tc_kernel<16>, tc_smem_bytes<16>());
   if (mp == 32) return run(fp8_gemm_tc_kernel<32>, tc_smem_bytes<32>());
-  return run(fp8_gemm_tc_kernel<64>, tc_smem_bytes<64>());
+  if (mp == 64) return run(fp8_gemm_tc_kernel<64>, tc_smem_bytes<64>());
+  return run(fp8_gemm_tc_kernel<128>, tc_smem_bytes<128>());
+}
+}  // namespace
+
+extern "C" int qk_fp8_gemm_rows(const void* x, const void* norm_w, int M, int K, const void* w, const float* w_scale,
+                                int scale_mode, int N, float eps, void* out, void* scratch, long long scratch_bytes,
+                                qk_stream_t stream) {
+  return gemm_rows_impl(false, x, norm_w, M, K, w, w_scale, scale_mode, N, eps, out, scratch, scratch_bytes, stream);
+}
+
+extern "C" int qk_fp8_gemm_tiles(const void* x, const void* norm_w, int M, int K, const void* w_tiles,
+                                 const float* w_scale, int scale_mode, int N, float eps, void* out, void* scratch,
+                                 long long scratch_bytes, qk_stream_t stream) {
+  return gemm_rows_impl(true, x, norm_w, M, K, w_tiles, w_scale, scale_mode, N, eps, out, scratch, scratch_bytes,
+                        stream);
 }
 
 // ---- GEMV without caller-provided scratch --------------------------------------------------------------------

@@ -8,7 +8,7 @@ Prompt processing, two ways:
 * `prefill()` feeds the prompt through the decode graph one position at a time (teacher forcing), which
   writes the KV rows and leaves the first generated token in `token`;
 * `prefill_chunked()` runs the reference's batched forward (qwen3-8b-fp8_rtx-5090/model.py:243-281) on chunks
-  of up to 64 positions: the tcgen05 batched FP8 linear for the projections, the row-wise prefill kernels
+  of up to 128 positions: the tcgen05 batched FP8 linear for the projections, the row-wise prefill kernels
   (csrc/prefill.cuh) around it. It reads every weight once per chunk instead of once per position.
 Synthetic long-context setups instead fill the cache directly (`Qwen3FP8Decode.fill_cache_random`).
 """
@@ -17,7 +17,7 @@ from __future__ import annotations
 import torch
 
 from kernels import ops
-from model import Qwen3FP8Decode, Linear, unpack_fp8
+from model import Qwen3FP8Decode, Linear, pack_fp8_tiles, unpack_fp8
 
 # Per-kind GEMV launch shape: ring stages per warp, warps per CTA, stages issued before the wait,
 # tiles per stage (2 KiB = 16 rows x 128 k; 4 KiB for gate|up), CTAs per SM. Kinds: qkv, o_proj, gate_up, down.
@@ -168,19 +168,19 @@ class Engine:
         self.state[1].fill_(0)
         return self.token.clone()
 
-    def rowmajor_weights(self):
-        """Per layer, the (qkv, o, gate_up, down) weights as row-major fp8 [N, K] matrices (the batched linear
-        streams TMA boxes of the plain matrix), unpacked once from the decode layout and cached: 8.2 GB more
-        device memory for Qwen3-8B, as the reference's prefill keeps its own row-major copy
+    def prefill_weights(self):
+        """Per layer, the (qkv, o, gate_up, down) weights in the batched linear's tile-packed layout
+        (`pack_fp8_tiles`: 16 KiB tiles a CTA streams contiguously), built once from the decode layout and
+        cached: 7.0 GB more device memory for Qwen3-8B, as the reference's prefill keeps its own row-major copy
         (model.py `rowmajor_copy`)."""
-        if getattr(self, "_rowmajor", None) is None:
-            self._rowmajor = [tuple(unpack_fp8(lin.packed, lin.N, lin.K, lin.pairs)
-                                    for lin in (L.qkv, L.o, L.gu, L.down)) for L in self.m.layers]
-        return self._rowmajor
+        if getattr(self, "_prefill_w", None) is None:
+            self._prefill_w = [tuple(pack_fp8_tiles(unpack_fp8(lin.packed, lin.N, lin.K, lin.pairs))
+                                     for lin in (L.qkv, L.o, L.gu, L.down)) for L in self.m.layers]
+        return self._prefill_w
 
     @torch.no_grad()
-    def prefill_chunked(self, prompt_ids, chunk: int = 64) -> torch.Tensor:
-        """Prompt positions 0..P-1 through the batched forward, `chunk` (<= 64) positions per pass: per layer
+    def prefill_chunked(self, prompt_ids, chunk: int = 128) -> torch.Tensor:
+        """Prompt positions 0..P-1 through the batched forward, `chunk` (<= 128) positions per pass: per layer
         qkv = W_qkv . q(RMSNorm(h)), per-head norm + RoPE with K/V appended to the cache, causal attention over
         the cache, h += W_o . q(attn), h += W_down . q(SwiGLU(W_gu . q(RMSNorm(h)))). The last position's
         hidden row then goes through the head and argmax. Leaves state = [P, 0] and the first generated token
@@ -188,8 +188,8 @@ class Engine:
         m, k, cfg = self.m, self.k, self.m.cfg
         if m.batch != 1:
             raise ValueError("prefill_chunked runs batch 1")
-        if not 1 <= chunk <= 64:
-            raise ValueError("chunk must be 1..64 positions")
+        if not 1 <= chunk <= 128:
+            raise ValueError("chunk must be 1..128 positions")
         ids = torch.as_tensor(prompt_ids, dtype=torch.int32, device=m.device)
         P = ids.numel()
         assert 0 < P < self.max_seq
@@ -202,7 +202,7 @@ class Engine:
                             y=torch.empty(chunk, cfg.hidden, **bf), gu=torch.empty(chunk, 2 * cfg.inter, **bf),
                             h=torch.empty(chunk, cfg.inter, **bf))
         b = self._pf
-        weights = self.rowmajor_weights()
+        weights = self.prefill_weights()
         for p0 in range(0, P, chunk):
             M = min(chunk, P - p0)
             resid, qkv, q, attn = b["resid"][:M], b["qkv"][:M], b["q"][:M], b["attn"][:M]

@@ -67,6 +67,7 @@ _SIGS = {
     "qk_finalize": ([_VP, _VP, _VP, _VP, _I, _I, _VP], _I),
     "qk_fp8_gemm_rows_scratch_bytes": ([_I, _I, _I], ctypes.c_longlong),
     "qk_fp8_gemm_rows": ([_VP, _VP, _I, _I, _VP, _VP, _I, _I, _F, _VP, _VP, ctypes.c_longlong, _VP], _I),
+    "qk_fp8_gemm_tiles": ([_VP, _VP, _I, _I, _VP, _VP, _I, _I, _F, _VP, _VP, ctypes.c_longlong, _VP], _I),
     "qk_embed_rows": ([_VP, _I, _VP, _I, _VP, _VP], _I),
     "qk_prefill_qkv": ([_VP, _I, _I, _I, _I, _VP, _VP, _VP, _VP, _F, _VP, _VP, _I, _VP, _VP], _I),
     "qk_prefill_attention": ([_VP, _I, _I, _I, _I, _VP, _VP, _I, _F, _VP, _VP], _I),
@@ -79,6 +80,11 @@ class PackedFP8(torch.Tensor):
     """uint8 weights in the `model.pack_fp8` layout (16-row units of 2 KiB tiles). The type survives
     `.to()`, `.cuda()`, views and slicing, so the ops can tell packed weights from any other fp8/uint8
     tensor of the same size."""
+
+
+class PackedTiles(torch.Tensor):
+    """fp8 [N, K] weights in the `model.pack_fp8_tiles` layout: 128 x 128 tiles, each in the 128-byte-swizzle
+    image the tcgen05 linear's MMAs read, tile-major. Keeps its type through `.to()` and views."""
 
 
 class PackedFP8Pairs(PackedFP8):
@@ -292,27 +298,30 @@ class DecodeOps:
 
     def fp8_gemm_rows(self, x, w, w_scale, out, norm_w=None, eps=1e-6):
         """Batched FP8 linear on the tcgen05 tensor cores: out[m] = bf16 W8A8 linear of x[m] (optionally
-        RMS-normalised with norm_w first), for M = 1..64 rows. x bf16 [M, K]; w row-major fp8 [N, K] (this op
-        streams TMA boxes of the plain matrix, not the pack_fp8 layout); w_scale fp32 [N] or [N/128, K/128];
-        out bf16 [M, N]. Scratch is owned by this object (zeroed once per size and device)."""
-        if isinstance(w, PackedFP8) or w.dtype != torch.float8_e4m3fn or w.dim() != 2 or not w.is_contiguous():
-            raise RuntimeError("fp8_gemm_rows: w must be a row-major float8_e4m3fn [N, K] matrix (not pack_fp8)")
+        RMS-normalised with norm_w first), for M = 1..128 rows (K <= 12288 above 64). x bf16 [M, K]; w fp8 [N, K],
+        either a plain row-major matrix (read through TMA boxes) or a `PackedTiles` tensor from
+        `model.pack_fp8_tiles` (read as contiguous tiles; not the GEMV's pack_fp8 layout); w_scale fp32 [N] or
+        [N/128, K/128]; out bf16 [M, N]. Scratch is owned by this object (zeroed once per size and device)."""
+        tiles = isinstance(w, PackedTiles)
+        if (isinstance(w, PackedFP8) or w.dtype != torch.float8_e4m3fn or w.dim() != 2 or not w.is_contiguous()):
+            raise RuntimeError("fp8_gemm_rows: w must be a row-major float8_e4m3fn [N, K] matrix or "
+                               "model.pack_fp8_tiles(w) (not pack_fp8)")
         M, K = x.shape
         N = w.shape[0]
         nbytes = self.lib.qk_fp8_gemm_rows_scratch_bytes(M, N, K)
         if nbytes < 0:
-            raise RuntimeError(f"fp8_gemm_rows: unsupported shape M={M} N={N} K={K}")
+            raise RuntimeError(f"fp8_gemm_rows: unsupported shape M={M} N={N} K={K} (M 1..128; N, K multiples of "
+                               "128; K at most 16384, or 12288 above 64 rows)")
         key = ("gemm", x.device.index if x.device.index is not None else torch.cuda.current_device())
         sc = self._scratch.get(key)
         if sc is None or sc.numel() < nbytes:
             sc = torch.zeros(nbytes, dtype=torch.uint8, device=x.device)
             self._scratch[key] = sc
         scale_mode = SCALE_CHANNEL if w_scale.dim() == 1 else SCALE_BLOCK128
-        st = self.lib.qk_fp8_gemm_rows(_p(x), _p(norm_w), M, K, _p(w), _p(w_scale), scale_mode, N, float(eps),
-                                       _p(out), _p(sc), sc.numel(), _stream())
+        fn = self.lib.qk_fp8_gemm_tiles if tiles else self.lib.qk_fp8_gemm_rows
+        st = fn(_p(x), _p(norm_w), M, K, _p(w), _p(w_scale), scale_mode, N, float(eps), _p(out), _p(sc), sc.numel(),
+                _stream())
         self._check(st, "fp8_gemm_rows")
-
-    # ---- chunked prefill (row-wise steps around fp8_gemm_rows) ----
 
     def embed_rows(self, tokens, table, out):
         """out[m] = table[tokens[m]] for the chunk's int32 tokens [M]; out bf16 [M, H]."""

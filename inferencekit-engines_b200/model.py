@@ -25,7 +25,7 @@ from dataclasses import dataclass, field
 
 import torch
 
-from kernels import PackedFP8, PackedFP8Pairs
+from kernels import PackedFP8, PackedFP8Pairs, PackedTiles
 
 FP8 = torch.float8_e4m3fn
 FP8_MAX = 448.0
@@ -139,6 +139,35 @@ def pack_fp8(w: torch.Tensor, pairs: bool = False) -> torch.Tensor:
     v = u8.view(N // 16, 2, 8, KB, 4, 2, 4, 4)           # [u, hh, g, kb, c, hi, t, b]
     v = v.permute(0, 3, 4, 2, 6, 5, 1, 7)                 # [u, kb, c, g, t, hi, hh, b]
     return v.contiguous().view(-1).as_subclass(PackedFP8)
+
+
+def _tile_swizzle_index(device):
+    """[128, 8] chunk gather index of one tile: row r's chunk position c holds source chunk c ^ (r % 8)."""
+    r = torch.arange(128, device=device)[:, None]
+    c = torch.arange(8, device=device)[None, :]
+    return r.expand(128, 8), (c ^ (r % 8))
+
+
+def pack_fp8_tiles(w: torch.Tensor) -> torch.Tensor:
+    """Row-major fp8 [N, K] -> the tcgen05 linear's tile-packed layout (`qk_fp8_gemm_tiles`), same bytes:
+    [N/128][K/128] tiles of 128 rows x 128 k (16 KiB), tile-major; inside a tile row r at byte 128 r with its
+    16-byte chunk c stored at chunk position c ^ (r % 8) (the 128-byte swizzle). Returned as an fp8 [N, K]
+    `PackedTiles` tensor."""
+    N, K = w.shape
+    assert N % 128 == 0 and K % 128 == 0, (N, K)
+    v = w.contiguous().view(torch.uint8).view(N // 128, 128, K // 128, 8, 16).permute(0, 2, 1, 3, 4)  # [t, kb, r, c, b]
+    ri, ci = _tile_swizzle_index(w.device)
+    out = v[:, :, ri, ci, :]               # out[.., r, c'] = in[.., r, c' ^ (r % 8)]
+    return out.contiguous().view(FP8).view(N, K).as_subclass(PackedTiles)
+
+
+def unpack_fp8_tiles(p: torch.Tensor) -> torch.Tensor:
+    """Inverse of pack_fp8_tiles (tests)."""
+    N, K = p.shape
+    v = p.as_subclass(torch.Tensor).contiguous().view(torch.uint8).view(N // 128, K // 128, 128, 8, 16)
+    ri, ci = _tile_swizzle_index(p.device)
+    v = v[:, :, ri, ci, :]                 # the swizzle is its own inverse
+    return v.permute(0, 2, 1, 3, 4).contiguous().view(FP8).view(N, K)
 
 
 def pack_reference_tiled(wt: torch.Tensor, kmajor: bool, pairs: bool = False) -> torch.Tensor:

@@ -173,3 +173,20 @@ def test_noalloc_rejects_bad_arguments_before_enqueuing_anything(lib):
     # the unknown kind is refused too
     st = lib.qk_fp8_gemv_noalloc(4, p, p, 1, p, p, None, None, p, 4096, 4096, 1e-6, None)
     assert st == 1 and b"kind" in lib.qk_last_error()
+
+
+def test_pack_fp8_tiles_round_trip_and_swizzle():
+    """The tcgen05 linear's tile-packed weight layout: a permutation of the bytes (round trip), with chunk c
+    of row r of tile (t, kb) at chunk position c ^ (r % 8)."""
+    import torch
+    import model as M
+    g = torch.Generator().manual_seed(0)
+    w = torch.randint(0, 0x7F, (384, 256), generator=g, dtype=torch.uint8).view(torch.float8_e4m3fn)
+    p = M.pack_fp8_tiles(w)
+    assert p.shape == w.shape and p.dtype == w.dtype
+    assert torch.equal(M.unpack_fp8_tiles(p).view(torch.uint8), w.view(torch.uint8))
+    flat = p.as_subclass(torch.Tensor).view(torch.uint8).reshape(-1)
+    wb = w.view(torch.uint8)
+    for t, kb, r, c in ((0, 0, 0, 0), (2, 1, 13, 6), (1, 0, 127, 7)):
+        off = ((t * 2 + kb) * 128 + r) * 128 + (c ^ (r % 8)) * 16
+        assert torch.equal(flat[off:off + 16], wb[t * 128 + r, kb * 128 + c * 16: kb * 128 + c * 16 + 16])

@@ -182,7 +182,7 @@ def restated_prefill(eng, ids):
     h = m.embed[torch.as_tensor(ids, device="cuda")]
     kv = []
     for li, L in enumerate(m.layers):
-        wq, wo, wgu, wd = eng.rowmajor_weights()[li]
+        wq, wo, wgu, wd = (M.unpack_fp8_tiles(w) for w in eng.prefill_weights()[li])
         LW = O.LayerW(L.ln1, L.ln2, L.q_norm, L.k_norm, wq, L.qkv.scale, wo, L.o.scale, wgu, L.gu.scale, wd,
                       L.down.scale)
         kc = torch.zeros(cfg.n_kv_heads, P, cfg.head_dim, dtype=torch.bfloat16, device="cuda")
