@@ -17,8 +17,8 @@
 //    values the decode step writes for that position given the same qkv row;
 //  * SwiGLU and the residual add round exactly as the decode epilogues.
 // The attention is fp32 throughout (scores, softmax probabilities, P.V) with one online-softmax pass over 64-key
-// chunks. Its sums run in a different order from the decode path's split-and-merge, so it matches an fp32
-// reference to rounding, not the decode step bit for bit.
+// chunks, 8 rows of a KV head per CTA. Its sums run in a different order from the decode path's
+// split-and-merge, so it matches an fp32 reference to rounding, not the decode step bit for bit.
 #pragma once
 #include "attention.cuh"
 #include "common.cuh"
@@ -73,98 +73,162 @@ __global__ void __launch_bounds__(256) prefill_qkv_kernel(const bf16* __restrict
   }
 }
 
-// Causal GQA attention of the chunk's queries. CTA (m, g): row m (position p0 + m), KV head g and its GQA = 4
-// query heads, over keys 0 .. p0 + m in chunks of PF_KEYS; 128 threads. Per chunk: K and V rows into shared
-// memory, scores s = (q . k) * scale (thread = key, two heads; each dot summed over the dims in order), a running
-// softmax per head (max, rescale by exp(m_old - m_new), sum of exponentials), and P.V with thread = dim, 4 heads.
-// The output is bf16(acc / l). All fp32.
+// Causal GQA attention of the chunk's queries. CTA (row block, g): PA_ROWS consecutive rows m0 .. m0 + 7
+// (positions p0 + m) and KV head g, i.e. PA_Q = 32 query vectors (head h = 4 g + qi / 8 of row m0 + qi % 8),
+// over keys 0 .. p0 + m in chunks of PF_KEYS; 256 threads. The chunk's K and V rows arrive in shared memory by
+// 16-byte cp.async copies, double-buffered (the next chunk loads while this one is computed), so each K/V row
+// crosses L2 once per 8 rows instead of once per row. Per chunk, all fp32:
+//  * scores s = (q . k) * scale, thread = (4 queries, keys j and j + 32), each dot summed over the dims in order;
+//    keys past a query's position are -inf;
+//  * a running softmax per query (one warp per 4 queries): the chunk's max, the rescale of the old sums by
+//    exp(m_old - m_new), the exponentials and their sum;
+//  * P.V with thread = (2 queries, 8 dims), the chunk's keys in order, after rescaling the accumulators.
+// The output is bf16(acc / l). Every query has key 0 in its first chunk, so no running max stays -inf.
 constexpr int PF_KEYS = 64;
-constexpr int PF_THREADS = 128;
+constexpr int PF_THREADS = 256;
+constexpr int PA_ROWS = 8;
+constexpr int PA_Q = PA_ROWS * GQA;   // 32
 struct PrefillAttnSmem {
-  float q[GQA][HEAD_DIM];
-  bf16 k[PF_KEYS][HEAD_DIM + 8];   // +8: consecutive rows start 16 bytes apart in bank order
-  bf16 v[PF_KEYS][HEAD_DIM];
-  float p[GQA][PF_KEYS];
-  float m_run[GQA], l_run[GQA], scale_old[GQA];
+  bf16 k[2][PF_KEYS][HEAD_DIM + 8];   // +8: consecutive rows start 16 bytes apart in bank order
+  bf16 v[2][PF_KEYS][HEAD_DIM];
+  float q[PA_Q][HEAD_DIM + 4];
+  float p[PA_Q][PF_KEYS + 4];
+  float m_run[PA_Q], l_run[PA_Q], scale_old[PA_Q];
 };
-__global__ void __launch_bounds__(PF_THREADS) prefill_attention_kernel(const bf16* __restrict__ q, int p0, int n_q,
-                                                                       const bf16* __restrict__ k_cache,
+__device__ __forceinline__ void pf_cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__global__ void __launch_bounds__(PF_THREADS) prefill_attention_kernel(const bf16* __restrict__ q, int M, int p0,
+                                                                       int n_q, const bf16* __restrict__ k_cache,
                                                                        const bf16* __restrict__ v_cache, int max_seq,
                                                                        float scale, bf16* __restrict__ out) {
-  __shared__ __align__(16) PrefillAttnSmem sm;
-  const int m = blockIdx.x, g = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int ctx = p0 + m + 1;
-  for (int i = tid; i < GQA * HEAD_DIM; i += PF_THREADS)
-    sm.q[i / HEAD_DIM][i % HEAD_DIM] = __bfloat162float(q[((size_t)m * n_q + g * GQA) * HEAD_DIM + i]);
-  if (tid < GQA) {
+  extern __shared__ __align__(16) uint8_t pf_smem[];
+  PrefillAttnSmem& sm = *reinterpret_cast<PrefillAttnSmem*>(pf_smem);
+  const int g = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int m0 = blockIdx.x * PA_ROWS, rows = min(PA_ROWS, M - m0);
+  const int ctx = p0 + m0 + rows;                        // keys 0 .. ctx - 1 cover the block's last row
+  const bf16* kc = k_cache + (size_t)g * max_seq * HEAD_DIM;
+  const bf16* vc = v_cache + (size_t)g * max_seq * HEAD_DIM;
+  auto load_chunk = [&](int buf, int j0) {               // 2 x 64 rows x 16 pieces of 16 bytes, 8 per thread
+    const int nj = min(PF_KEYS, ctx - j0);
+    for (int i = tid; i < nj * (HEAD_DIM / 8); i += PF_THREADS) {
+      const int r = i / (HEAD_DIM / 8), c8 = (i % (HEAD_DIM / 8)) * 8;
+      pf_cp_async16(&sm.k[buf][r][c8], kc + (size_t)(j0 + r) * HEAD_DIM + c8);
+      pf_cp_async16(&sm.v[buf][r][c8], vc + (size_t)(j0 + r) * HEAD_DIM + c8);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  load_chunk(0, 0);
+  for (int i = tid; i < PA_Q * HEAD_DIM; i += PF_THREADS) {   // query qi = h * 8 + r, h = 0..3 within the group
+    const int qi = i / HEAD_DIM, d = i % HEAD_DIM, r = qi % PA_ROWS, h = qi / PA_ROWS;
+    sm.q[qi][d] = r < rows ? __bfloat162float(q[((size_t)(m0 + r) * n_q + g * GQA + h) * HEAD_DIM + d]) : 0.f;
+  }
+  if (tid < PA_Q) {
     sm.m_run[tid] = -INFINITY;
     sm.l_run[tid] = 0.f;
   }
-  const bf16* kc = k_cache + (size_t)g * max_seq * HEAD_DIM;
-  const bf16* vc = v_cache + (size_t)g * max_seq * HEAD_DIM;
-  float acc[GQA] = {0.f, 0.f, 0.f, 0.f};   // thread = dim tid, the 4 heads
-  __syncthreads();
-  for (int j0 = 0; j0 < ctx; j0 += PF_KEYS) {
+  // P.V ownership: queries 2 * (tid / 16) and +1, dims 8 * (tid % 16) .. +7
+  const int pq = (tid >> 4) * 2, pd = (tid & 15) * 8;
+  float acc[2][8];
+#pragma unroll
+  for (int a = 0; a < 2; ++a)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[a][e] = 0.f;
+  // score ownership: queries 4 * warp .. +3, keys lane and lane + 32
+  const int sq = warp * 4;
+  int buf = 0;
+  for (int j0 = 0; j0 < ctx; j0 += PF_KEYS, buf ^= 1) {
     const int nj = min(PF_KEYS, ctx - j0);
-    for (int i = tid; i < nj * (HEAD_DIM / 8); i += PF_THREADS) {   // 16-byte pieces of the chunk's K and V rows
-      const int r = i / (HEAD_DIM / 8), c8 = i % (HEAD_DIM / 8);
-      *reinterpret_cast<uint4*>(&sm.k[r][c8 * 8]) =
-          *reinterpret_cast<const uint4*>(kc + (size_t)(j0 + r) * HEAD_DIM + c8 * 8);
-      *reinterpret_cast<uint4*>(&sm.v[r][c8 * 8]) =
-          *reinterpret_cast<const uint4*>(vc + (size_t)(j0 + r) * HEAD_DIM + c8 * 8);
+    if (j0 + PF_KEYS < ctx) {
+      load_chunk(buf ^ 1, j0 + PF_KEYS);   // the buffer freed by the previous chunk's final barrier
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
     }
     __syncthreads();
-    {   // scores: thread = (key tid % 64, heads 2 (tid / 64) .. +1)
-      const int j = tid & (PF_KEYS - 1), h0 = (tid >> 6) * 2;
-      float d0 = 0.f, d1 = 0.f;
-      if (j < nj) {
-        for (int d = 0; d < HEAD_DIM; d += 8) {
-          const uint4 kv = *reinterpret_cast<const uint4*>(&sm.k[j][d]);
-          const float kf[8] = {bf16lo(kv.x), bf16hi(kv.x), bf16lo(kv.y), bf16hi(kv.y),
-                               bf16lo(kv.z), bf16hi(kv.z), bf16lo(kv.w), bf16hi(kv.w)};
+    {   // scores
+      float s[4][2];
+#pragma unroll
+      for (int a = 0; a < 4; ++a) s[a][0] = s[a][1] = 0.f;
+      const int ja = lane, jb = lane + 32;
+      for (int d = 0; d < HEAD_DIM; d += 8) {
+        const uint4 ka = *reinterpret_cast<const uint4*>(&sm.k[buf][ja][d]);
+        const uint4 kb = *reinterpret_cast<const uint4*>(&sm.k[buf][jb][d]);
+        const float fa[8] = {bf16lo(ka.x), bf16hi(ka.x), bf16lo(ka.y), bf16hi(ka.y),
+                             bf16lo(ka.z), bf16hi(ka.z), bf16lo(ka.w), bf16hi(ka.w)};
+        const float fb[8] = {bf16lo(kb.x), bf16hi(kb.x), bf16lo(kb.y), bf16hi(kb.y),
+                             bf16lo(kb.z), bf16hi(kb.z), bf16lo(kb.w), bf16hi(kb.w)};
+#pragma unroll
+        for (int a = 0; a < 4; ++a) {
+          const float4 q0 = *reinterpret_cast<const float4*>(&sm.q[sq + a][d]);
+          const float4 q1 = *reinterpret_cast<const float4*>(&sm.q[sq + a][d + 4]);
+          const float qv[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
-            d0 += sm.q[h0][d + e] * kf[e];
-            d1 += sm.q[h0 + 1][d + e] * kf[e];
+            s[a][0] += qv[e] * fa[e];
+            s[a][1] += qv[e] * fb[e];
           }
         }
       }
-      sm.p[h0][j] = j < nj ? d0 * scale : -INFINITY;
-      sm.p[h0 + 1][j] = j < nj ? d1 * scale : -INFINITY;
+#pragma unroll
+      for (int a = 0; a < 4; ++a) {
+        const int pos = p0 + m0 + (sq + a) % PA_ROWS;
+        sm.p[sq + a][ja] = (ja < nj && j0 + ja <= pos) ? s[a][0] * scale : -INFINITY;
+        sm.p[sq + a][jb] = (jb < nj && j0 + jb <= pos) ? s[a][1] * scale : -INFINITY;
+      }
     }
-    __syncthreads();
-    {   // running softmax, warp h takes head h: the chunk's max, the rescale of the old sums, the exponentials
-      const int h = warp;
-      const float a = sm.p[h][lane], b = sm.p[h][lane + 32];
-      const float cmax = warp_max(fmaxf(a, b));
-      const float m_old = sm.m_run[h], m_new = fmaxf(m_old, cmax);
-      const float ea = expf(a - m_new), eb = expf(b - m_new);
-      sm.p[h][lane] = ea;
-      sm.p[h][lane + 32] = eb;
-      const float csum = warp_sum(ea + eb);
-      __syncwarp();
+    __syncwarp();
+    // running softmax: warp w owns queries 4w .. 4w + 3, exactly the rows its lanes just scored
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+      const int qi = sq + a;
+      const float x0 = sm.p[qi][lane], x1 = sm.p[qi][lane + 32];
+      const float cmax = warp_max(fmaxf(x0, x1));
+      const float m_old = sm.m_run[qi], m_new = fmaxf(m_old, cmax);
+      const float e0 = expf(x0 - m_new), e1 = expf(x1 - m_new);
+      sm.p[qi][lane] = e0;
+      sm.p[qi][lane + 32] = e1;
+      const float csum = warp_sum(e0 + e1);
       if (lane == 0) {
         const float r = m_old == -INFINITY ? 0.f : expf(m_old - m_new);
-        sm.scale_old[h] = r;
-        sm.l_run[h] = sm.l_run[h] * r + csum;
-        sm.m_run[h] = m_new;
+        sm.scale_old[qi] = r;
+        sm.l_run[qi] = sm.l_run[qi] * r + csum;
+        sm.m_run[qi] = m_new;
       }
     }
     __syncthreads();
-    {   // P.V: thread = dim tid, the 4 heads, the chunk's keys in order
+    {   // P.V
+      const float r0 = sm.scale_old[pq], r1 = sm.scale_old[pq + 1];
 #pragma unroll
-      for (int h = 0; h < GQA; ++h) acc[h] *= sm.scale_old[h];
+      for (int e = 0; e < 8; ++e) {
+        acc[0][e] *= r0;
+        acc[1][e] *= r1;
+      }
       for (int j = 0; j < nj; ++j) {
-        const float v = __bfloat162float(sm.v[j][tid]);
+        const uint4 vv = *reinterpret_cast<const uint4*>(&sm.v[buf][j][pd]);
+        const float vf[8] = {bf16lo(vv.x), bf16hi(vv.x), bf16lo(vv.y), bf16hi(vv.y),
+                             bf16lo(vv.z), bf16hi(vv.z), bf16lo(vv.w), bf16hi(vv.w)};
+        const float w0 = sm.p[pq][j], w1 = sm.p[pq + 1][j];
 #pragma unroll
-        for (int h = 0; h < GQA; ++h) acc[h] += sm.p[h][j] * v;
+        for (int e = 0; e < 8; ++e) {
+          acc[0][e] += w0 * vf[e];
+          acc[1][e] += w1 * vf[e];
+        }
       }
     }
-    __syncthreads();
+    __syncthreads();   // this chunk's K/V buffer and p are free for the next load and scores
   }
 #pragma unroll
-  for (int h = 0; h < GQA; ++h)
-    out[((size_t)m * n_q + g * GQA + h) * HEAD_DIM + tid] = __float2bfloat16_rn(acc[h] / sm.l_run[h]);
+  for (int a = 0; a < 2; ++a) {
+    const int qi = pq + a, r = qi % PA_ROWS, h = qi / PA_ROWS;
+    if (r >= rows) continue;
+    const float inv_l = 1.f / sm.l_run[qi];
+    bf16 o[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[e] = __float2bfloat16_rn(acc[a][e] * inv_l);
+    *reinterpret_cast<uint4*>(out + ((size_t)(m0 + r) * n_q + g * GQA + h) * HEAD_DIM + pd) =
+        *reinterpret_cast<const uint4*>(o);
+  }
 }
 
 // resid[i] = bf16(resid[i] + y[i]) for y = bf16(W . x): the decode step's residual epilogue, bf16(resid + bf16(a)).

@@ -814,9 +814,13 @@ int qk_prefill_attention(const void* q, int M, int p0, int n_q, int n_kv, const 
   if (!q || !k_cache || !v_cache || !out) return fail(QK_EINVAL, "null pointer argument");
   if (M < 1 || p0 < 0 || n_kv < 1 || n_q != GQA * n_kv) return fail(QK_EINVAL, "M=%d p0=%d n_q=%d n_kv=%d", M, p0, n_q, n_kv);
   if ((long long)p0 + M > max_seq) return fail(QK_EINVAL, "positions %d..%d past max_seq %d", p0, p0 + M - 1, max_seq);
-  if (!aligned(k_cache, 16) || !aligned(v_cache, 16)) return fail(QK_EINVAL, "caches must be 16-byte aligned");
-  prefill_attention_kernel<<<dim3(M, n_kv), PF_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const bf16*>(q), p0, n_q, static_cast<const bf16*>(k_cache), static_cast<const bf16*>(v_cache),
+  if (!aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(out, 16))
+    return fail(QK_EINVAL, "caches and out must be 16-byte aligned");
+  const int smem = (int)sizeof(PrefillAttnSmem);
+  if (int r = ensure_smem((const void*)prefill_attention_kernel, smem)) return r;
+  prefill_attention_kernel<<<dim3((M + PA_ROWS - 1) / PA_ROWS, n_kv), PF_THREADS, smem,
+                             static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const bf16*>(q), M, p0, n_q, static_cast<const bf16*>(k_cache), static_cast<const bf16*>(v_cache),
       max_seq, scale, static_cast<bf16*>(out));
   return plain_launch_status("prefill_attention launch");
 }

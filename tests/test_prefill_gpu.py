@@ -81,7 +81,7 @@ def attention_fp32(q, kc, vc, p0, scale):
     return o.reshape(Mq, n_q * hd)
 
 
-@pytest.mark.parametrize("p0,Mq", [(0, 64), (700, 40), (1983, 64)])
+@pytest.mark.parametrize("p0,Mq", [(0, 64), (700, 40), (1983, 64), (1900, 128), (5, 3)])
 def test_prefill_attention_matches_fp32(p0, Mq):
     from kernels import ops
     k = ops()
