@@ -10,6 +10,7 @@
 
 #include "../../include/qwen3_b200.h"
 #include "attention.cuh"
+#include "attention_fp8kv.cuh"
 #include "common.cuh"
 #include "gemm_tc.cuh"
 #include "gemv.cuh"
@@ -840,3 +841,58 @@ int qk_swiglu_rows(const void* gu, int M, int I, void* h, qk_stream_t stream) {
 }
 
 }  // extern "C"
+
+// ---- decode attention over an FP8 KV cache ---------------------------------------------------------------------
+extern "C" int qk_attention_fp8kv(const void* qkv, const void* q_norm_w, const void* k_norm_w, const void* cos_tab,
+                                  const void* sin_tab, const int* state, void* k_cache, float* k_scale, void* v_cache,
+                                  float* v_scale, float* o_part, float* ml_part, void* out, int batch, int n_kv,
+                                  int max_seq, int max_splits, int qkv_stride, int state_stride, float scale,
+                                  float eps, qk_stream_t stream) {
+  if (!qkv || !q_norm_w || !k_norm_w || !cos_tab || !sin_tab || !state || !k_cache || !k_scale || !v_cache ||
+      !v_scale || !o_part || !ml_part || !out)
+    return fail(QK_EINVAL, "null pointer argument");
+  if (batch < 1 || batch > 65535 || n_kv < 1 || n_kv > 64 || max_seq < 1) return fail(QK_EINVAL, "bad batch/n_kv/max_seq");
+  if ((long long)max_splits * KV8_SPLIT < max_seq) return fail(QK_EINVAL, "o_part too small: max_splits*64 < max_seq");
+  if (max_splits > 4096) return fail(QK_EINVAL, "max_splits %d > 4096", max_splits);
+  if (qkv_stride < n_kv * 6 * HEAD_DIM || state_stride < 1) return fail(QK_EINVAL, "bad qkv_stride/state_stride");
+  if (!aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(qkv, 8) || !aligned(k_scale, 4) || !aligned(v_scale, 4))
+    return fail(QK_EINVAL, "caches must be 16-byte aligned, qkv 8-byte");
+  if ((long long)n_kv * ((max_seq + KV8_KEYS - 1) / KV8_KEYS) > 0x7fffffff) return fail(QK_EINVAL, "max_seq too large");
+  Kv8Params p = {};
+  p.qkv = static_cast<const bf16*>(qkv);
+  p.q_norm_w = static_cast<const bf16*>(q_norm_w);
+  p.k_norm_w = static_cast<const bf16*>(k_norm_w);
+  p.cos_tab = static_cast<const bf16*>(cos_tab);
+  p.sin_tab = static_cast<const bf16*>(sin_tab);
+  p.state = state;
+  p.k_cache = static_cast<uint8_t*>(k_cache);
+  p.v_cache = static_cast<uint8_t*>(v_cache);
+  p.k_scale = k_scale;
+  p.v_scale = v_scale;
+  p.o_part = o_part;
+  p.ml_part = ml_part;
+  p.n_kv = n_kv;
+  p.max_seq = max_seq;
+  p.max_splits = max_splits;
+  p.qkv_stride = qkv_stride;
+  p.state_stride = state_stride;
+  p.scale = scale;
+  p.eps = eps;
+  const dim3 grid(n_kv * ((max_seq + KV8_KEYS - 1) / KV8_KEYS), batch);
+  if (int r = launch(attn_fp8kv_partials_kernel, grid, dim3(KV8_THREADS), 0, stream, p)) return r;
+  AttnParams m = {};   // the merge reads the partials in the bf16 kernel's layout, 64-key splits
+  m.state = state;
+  m.o_part = o_part;
+  m.ml_part = ml_part;
+  m.out = static_cast<bf16*>(out);
+  m.n_kv = n_kv;
+  m.max_seq = max_seq;
+  m.max_splits = max_splits;
+  m.state_stride = state_stride;
+  m.chunk = KV8_SPLIT;
+  m.tl_slot = -1;
+  const int smem_m = (int)attn_merge_smem_bytes(max_splits);
+  if (int r = ensure_smem((const void*)attn_merge_kernel, smem_m)) return r;
+  return launch(attn_merge_kernel, dim3(2 * n_kv * GQA, batch), dim3(ATT_MERGE_THREADS), smem_m, stream, m);
+}
+
