@@ -812,15 +812,21 @@ def run_attention_sweep(args):
                 g = torch.Generator().manual_seed(L)
                 lengths = [int(x) for x in torch.randint(L // 2, L + 1, (batch,), generator=g)]
             max_seq = L + 1
-            kv_bytes = sum((p + 1) * 8 * 128 * 2 * 2 for p in lengths)
-            per_layer = 2 * batch * 8 * max_seq * 128 * 2
+            fp8 = args.kv == "fp8"
+            row_bytes = 128 + 4 if fp8 else 128 * 2       # an FP8 row carries its fp32 scale
+            kv_bytes = sum((p + 1) * 8 * row_bytes * 2 for p in lengths)
+            per_layer = 2 * batch * 8 * max_seq * row_bytes
             n_layers = max(1, -(-256 * 2 ** 20 // per_layer))           # > 2 x L2 of caches, cycled
             g = torch.Generator(device="cuda").manual_seed(L + batch)
             caches = []
             for _ in range(n_layers):
                 kc = torch.randn(batch, 8, max_seq, 128, generator=g, device="cuda").to(torch.bfloat16)
                 vc = torch.randn(batch, 8, max_seq, 128, generator=g, device="cuda").to(torch.bfloat16)
-                caches.append((kc, vc))
+                if fp8:
+                    (k8, ks), (v8, vs) = M.quantize_kv_rows(kc), M.quantize_kv_rows(vc)
+                    caches.append((k8.view(torch.uint8), ks, v8.view(torch.uint8), vs))
+                else:
+                    caches.append((kc, vc))
             qkv = (torch.randn(batch, 6144, generator=g, device="cuda") * 2).to(torch.bfloat16)
             qn = torch.ones(128, dtype=torch.bfloat16, device="cuda")
             cos, sin = M.rope_tables(max_seq, 128, 1e6, "cuda")
@@ -832,6 +838,11 @@ def run_attention_sweep(args):
             att = torch.empty(batch, 4096, dtype=torch.bfloat16, device="cuda")
 
             def call(i):
+                if fp8:
+                    k8, ks, v8, vs = caches[i % n_layers]
+                    k.attention_fp8kv(qkv, qn, qn, cos, sin, state, k8, ks, v8, vs, o_part, ml_part, att,
+                                      128 ** -0.5, 1e-6, batch=batch)
+                    return
                 kc, vc = caches[i % n_layers]
                 k.attention(qkv, qn, qn, cos, sin, state, kc, vc, o_part, ml_part, counters, att, 128 ** -0.5,
                             1e-6, 0, 64, batch=batch)
@@ -858,7 +869,7 @@ def run_attention_sweep(args):
             us = e0.elapsed_time(e1) / K * 1e3
             del graph
             gbs = kv_bytes / (us * 1e-6) / 1e9
-            rec = {"sweep": "attention", "ctx": L, "batch": batch, "lengths": lengths, "us_per_call": us,
+            rec = {"sweep": "attention", "kv": args.kv, "ctx": L, "batch": batch, "lengths": lengths, "us_per_call": us,
                    "kv_bytes": kv_bytes, "gbs": gbs, "frac_of_peak": gbs / peak, "layers_cycled": n_layers}
             print(json.dumps(rec), flush=True)
             out.append(rec)
@@ -966,6 +977,8 @@ def main():
                     help="reference arm: skip timing the reference's own decode kernels on the GPU")
     ap.add_argument("--sweep", choices=["attention", "gemv"],
                     help="attention: BASELINE config 4 (contexts x batches); gemv: config 3 (shapes x rows)")
+    ap.add_argument("--kv", default="bf16", choices=["bf16", "fp8"],
+                    help="--sweep attention: the KV cache format (fp8: e4m3 rows + fp32 row scales)")
     ap.add_argument("--shapes", default="", help="--sweep gemv: comma-separated KxN shapes instead of the five")
     ap.add_argument("--rows", default="", help="--sweep gemv: comma-separated row counts instead of 1,4,16,64")
     ap.add_argument("--timeline-out", default="", help="--timeline: also save the raw stamps (torch.save) here")

@@ -67,6 +67,8 @@ class Engine:
         self.graph = None
         self.fused = fused
         self.step_timeline = None     # fused step only: int64 [#SMs, 5*layers+1, 32] stamps (include/qwen3_b200.h)
+        if m.kv_dtype == "fp8" and (fused or attn_chunk != 64):
+            raise ValueError("an FP8 KV cache runs on the op path (fused=False) with 64-key splits")
         if fused:
             if attn_chunk != 64 or m.batch != 1:
                 raise ValueError("the fused step needs 64-key attention splits and batch 1")
@@ -109,9 +111,14 @@ class Engine:
         k.embed(self.token, m.embed, self.resid)
         for li, L in enumerate(m.layers):
             self._gemv(0, L.qkv, self.resid, L.ln1, self.qkv)
-            k.attention(self.qkv, L.q_norm, L.k_norm, m.cos, m.sin, self.state, m.k_cache[li], m.v_cache[li],
-                        self.o_part, self.ml_part, self.counters, self.attn, cfg.head_dim ** -0.5, cfg.eps, 0,
-                        self.attn_chunk)
+            if m.kv_dtype == "fp8":
+                k.attention_fp8kv(self.qkv, L.q_norm, L.k_norm, m.cos, m.sin, self.state, m.k_cache[li],
+                                  m.k_scale[li], m.v_cache[li], m.v_scale[li], self.o_part, self.ml_part, self.attn,
+                                  cfg.head_dim ** -0.5, cfg.eps)
+            else:
+                k.attention(self.qkv, L.q_norm, L.k_norm, m.cos, m.sin, self.state, m.k_cache[li], m.v_cache[li],
+                            self.o_part, self.ml_part, self.counters, self.attn, cfg.head_dim ** -0.5, cfg.eps, 0,
+                            self.attn_chunk)
             self._gemv(1, L.o, self.attn, None, self.resid)
             self._gemv(2, L.gu, self.resid, L.ln2, self.h)
             self._gemv(3, L.down, self.h, None, self.resid)
@@ -186,8 +193,9 @@ class Engine:
         hidden row then goes through the head and argmax. Leaves state = [P, 0] and the first generated token
         in `token`, like `prefill()`, and returns it as a device tensor (no host sync)."""
         m, k, cfg = self.m, self.k, self.m.cfg
-        if m.batch != 1:
-            raise ValueError("prefill_chunked runs batch 1")
+        if m.batch != 1 or m.kv_dtype != "bf16":
+            raise ValueError("prefill_chunked runs batch 1 over a bf16 KV cache (an FP8 cache prefills through "
+                             "the decode step: prefill())")
         if not 1 <= chunk <= 128:
             raise ValueError("chunk must be 1..128 positions")
         ids = torch.as_tensor(prompt_ids, dtype=torch.int32, device=m.device)

@@ -68,6 +68,7 @@ _SIGS = {
     "qk_fp8_gemm_rows_scratch_bytes": ([_I, _I, _I], ctypes.c_longlong),
     "qk_fp8_gemm_rows": ([_VP, _VP, _I, _I, _VP, _VP, _I, _I, _F, _VP, _VP, ctypes.c_longlong, _VP], _I),
     "qk_fp8_gemm_tiles": ([_VP, _VP, _I, _I, _VP, _VP, _I, _I, _F, _VP, _VP, ctypes.c_longlong, _VP], _I),
+    "qk_attention_fp8kv": ([_VP] * 13 + [_I, _I, _I, _I, _I, _I, _F, _F, _VP], _I),
     "qk_embed_rows": ([_VP, _I, _VP, _I, _VP, _VP], _I),
     "qk_prefill_qkv": ([_VP, _I, _I, _I, _I, _VP, _VP, _VP, _VP, _F, _VP, _VP, _I, _VP, _VP], _I),
     "qk_prefill_attention": ([_VP, _I, _I, _I, _I, _VP, _VP, _I, _F, _VP, _VP], _I),
@@ -208,6 +209,27 @@ class DecodeOps:
                                    float(eps), int(chunk), _stream())
         self._check(st, "attention")
         self._tl("attention")
+
+    def attention_fp8kv(self, qkv, q_norm_w, k_norm_w, cos_tab, sin_tab, state, k_cache, k_scale, v_cache, v_scale,
+                        o_part, ml_part, out, scale, eps, batch=None, state_stride=2):
+        """Decode attention over an FP8 KV cache (e4m3 rows + one fp32 scale per row), 64-key splits.
+        k_cache/v_cache: one layer, uint8 or float8_e4m3fn [n_kv, max_seq, 128] (batch 1) or
+        [batch, n_kv, max_seq, 128]; k_scale/v_scale: fp32 [n_kv, max_seq] or [batch, n_kv, max_seq]."""
+        if k_cache.dim() == 3:
+            b, n_kv, max_seq = 1, k_cache.shape[0], k_cache.shape[1]
+        else:
+            b, n_kv, max_seq = k_cache.shape[0], k_cache.shape[1], k_cache.shape[2]
+        if batch is not None:
+            b = batch
+        if k_cache.element_size() != 1 or v_cache.element_size() != 1 or k_scale.dtype != torch.float32:
+            raise RuntimeError("attention_fp8kv: caches must be 1-byte e4m3 rows, scales fp32")
+        max_splits = o_part.shape[-2]
+        qkv_stride = qkv.shape[-1] if qkv.dim() > 1 else qkv.numel()
+        st = self.lib.qk_attention_fp8kv(_p(qkv), _p(q_norm_w), _p(k_norm_w), _p(cos_tab), _p(sin_tab), _p(state),
+                                         _p(k_cache), _p(k_scale), _p(v_cache), _p(v_scale), _p(o_part), _p(ml_part),
+                                         _p(out), b, n_kv, max_seq, max_splits, qkv_stride, int(state_stride),
+                                         float(scale), float(eps), _stream())
+        self._check(st, "attention_fp8kv")
 
     def lm_head_argmax(self, w, x, norm_w, logits, best, eps, ctas=0, w_scale=None, row_offset=0):
         V = logits.numel()

@@ -199,6 +199,17 @@ def unpack_fp8(p: torch.Tensor, N: int, K: int, pairs: bool = False) -> torch.Te
     return v.contiguous().view(N, K).view(FP8)
 
 
+def quantize_kv_rows(x: torch.Tensor):
+    """bf16 rows [..., 128] -> (e4m3 [..., 128], fp32 scales [...]): s = amax / 448, q = e4m3(x / s) round to
+    nearest even, saturating, s = 0 -> 0 (the FP8 KV cache's row format; the kernels divide with div.full, so
+    a quotient at a rounding tie can land one e4m3 step away). For cache set-up and tests."""
+    xf = x.float()
+    s = xf.abs().amax(-1) / FP8_MAX
+    safe = torch.where(s > 0, s, torch.ones_like(s))
+    q = torch.where(s[..., None] > 0, xf / safe[..., None], torch.zeros_like(xf))
+    return q.clamp(-FP8_MAX, FP8_MAX).to(FP8), s
+
+
 def rope_tables(max_seq: int, head_dim: int, theta: float, device) -> tuple[torch.Tensor, torch.Tensor]:
     """bf16 cos/sin tables [max_seq, head_dim], same ops as the reference (model.py:213-219)."""
     inv_freq = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.int64).float() / head_dim))
@@ -236,6 +247,7 @@ class Qwen3FP8Decode:
     device: str
     scale_mode: str = "channel"
     head_dtype: str = "fp8"       # "fp8" (per-channel scales) or "bf16" (reference format)
+    kv_dtype: str = "bf16"        # "bf16" (the reference's cache) or "fp8" (e4m3 rows + fp32 row scales)
     layers: list = field(default_factory=list)
     batch: int = 1
 
@@ -318,18 +330,39 @@ class Qwen3FP8Decode:
     def alloc_cache(self):
         cfg = self.cfg
         shape = (len(self.layers), self.batch, cfg.n_kv_heads, self.max_seq, cfg.head_dim)
-        self.k_cache = torch.zeros(shape, dtype=torch.bfloat16, device=self.device)
-        self.v_cache = torch.zeros(shape, dtype=torch.bfloat16, device=self.device)
+        if self.kv_dtype == "fp8":   # e4m3 rows [.., 128] + one fp32 scale per row
+            self.k_cache = torch.zeros(shape, dtype=torch.uint8, device=self.device)
+            self.v_cache = torch.zeros(shape, dtype=torch.uint8, device=self.device)
+            self.k_scale = torch.zeros(shape[:-1], dtype=torch.float32, device=self.device)
+            self.v_scale = torch.zeros(shape[:-1], dtype=torch.float32, device=self.device)
+        else:
+            self.k_cache = torch.zeros(shape, dtype=torch.bfloat16, device=self.device)
+            self.v_cache = torch.zeros(shape, dtype=torch.bfloat16, device=self.device)
+            self.k_scale = self.v_scale = None
         self.cos, self.sin = rope_tables(self.max_seq, cfg.head_dim, cfg.rope_theta, self.device)
 
+    def set_kv_dtype(self, kv_dtype: str):
+        """Reallocate the KV cache as "bf16" or "fp8" (zeroed; the cache's contents are not converted)."""
+        if kv_dtype not in ("bf16", "fp8"):
+            raise ValueError(f"kv_dtype must be bf16 or fp8, got {kv_dtype!r}")
+        self.kv_dtype = kv_dtype
+        self.alloc_cache()
+
     def fill_cache_random(self, upto: int, seed: int = 1234):
-        """KV positions [0, upto) = N(0, 1) bf16 (the synthetic long-context setups), generated in slices."""
+        """KV positions [0, upto) = N(0, 1) bf16 (the synthetic long-context setups), generated in slices; an
+        FP8 cache gets those rows quantized (`quantize_kv_rows`)."""
         g = torch.Generator(device=self.device)
         g.manual_seed(seed)
         for li in range(len(self.layers)):
-            for c in (self.k_cache, self.v_cache):
+            for ci, c in enumerate((self.k_cache, self.v_cache)):
                 t = c[li, :, :, :upto]
-                t.copy_(torch.randn(t.shape, generator=g, device=self.device, dtype=torch.float32))
+                x = torch.randn(t.shape, generator=g, device=self.device, dtype=torch.float32)
+                if self.kv_dtype == "fp8":
+                    q, sc = quantize_kv_rows(x.to(torch.bfloat16))
+                    t.copy_(q.view(torch.uint8))
+                    (self.k_scale, self.v_scale)[ci][li, :, :, :upto].copy_(sc)
+                else:
+                    t.copy_(x)
 
     def weight_bytes(self) -> dict:
         """Algorithmic bytes one decode token reads (weights, scales, norms, embedding row)."""

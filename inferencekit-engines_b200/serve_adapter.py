@@ -94,7 +94,7 @@ class EngineModel:
         P = len(prompt_ids)
         if P < 1 or max_tokens < 1 or P + max_tokens > self.max_seq:
             raise ValueError(f"prompt of {P} tokens + {max_tokens} new tokens does not fit max_seq {self.max_seq}")
-        chunked = P >= self.chunk_min
+        chunked = P >= self.chunk_min and getattr(getattr(eng, "m", None), "kv_dtype", "bf16") == "bf16"
         first = eng.prefill_chunked(prompt_ids) if chunked else eng.prefill(prompt_ids)   # device tensor, no sync
         info["prefill"] = "chunked" if chunked else "decode_graph"
         want_lp = bool(logprobs) and self.logprobs_supported

@@ -23,6 +23,8 @@ It restates, in plain torch CPU ops, the arithmetic of the reference engine
 * `prefill_layer`  Q/model.py:255-279 for M prompt positions at once (start..start+M-1): the same layer with
                    the KV rows written for every position and causal attention (row m sees cache rows
                    0..start+m), fp32 scores and probabilities, rounded to bf16 once.
+* `quant_kv_rows`, `attention_fp8kv_f32`: the FP8 KV cache's contract (an extension with no reference
+                   counterpart): e4m3 rows with one fp32 scale each, scores and probabilities in fp32.
 * `lm_head_argmax` Q/model.py:280-281 (final RMSNorm + linear) and Q/kernels/decode.cu:572-661: greedy
                    argmax over bf16 logits, ties to the lowest index.
 
@@ -114,6 +116,30 @@ def attention_f32(q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, scale: floa
     s = torch.einsum("ghd,gjd->ghj", qf, K.float()) * scale
     p = torch.softmax(s, dim=-1)
     o = torch.einsum("ghj,gjd->ghd", p, V.float())
+    return o.reshape(nq * hd).to(torch.bfloat16)
+
+
+def quant_kv_rows(x: torch.Tensor):
+    """The FP8 KV cache's row format (this engine's extension; the reference keeps bf16 rows): bf16 [..., 128]
+    -> (e4m3 [..., 128], fp32 [...]) with s = amax / 448, q = e4m3(x / s) round to nearest even, saturating,
+    s = 0 -> 0. IEEE division here; the kernels use div.full, so a quotient on a tie may round one step apart."""
+    xf = x.float()
+    s = xf.abs().amax(-1) / FP8_MAX
+    safe = torch.where(s > 0, s, torch.ones_like(s))
+    q = torch.where(s[..., None] > 0, xf / safe[..., None], torch.zeros_like(xf))
+    return q.clamp(-FP8_MAX, FP8_MAX).to(FP8), s
+
+
+def attention_fp8kv_f32(q: torch.Tensor, K8: torch.Tensor, ks: torch.Tensor, V8: torch.Tensor, vs: torch.Tensor,
+                        scale: float) -> torch.Tensor:
+    """GQA decode attention over an FP8 KV cache in fp32: q [32, 128] (bf16 values), K8/V8 e4m3 [8, ctx, 128],
+    ks/vs fp32 [8, ctx]. Scores (q . k8_j) * ks_j * scale, softmax, sum_j (p_j * vs_j) * v8_j -> bf16 [32*128]."""
+    nq, hd = q.shape
+    nkv = K8.shape[0]
+    qf = q.float().view(nkv, nq // nkv, hd)
+    s = torch.einsum("ghd,gjd->ghj", qf, K8.float()) * ks.float()[:, None, :] * scale
+    p = torch.softmax(s, dim=-1) * vs.float()[:, None, :]
+    o = torch.einsum("ghj,gjd->ghd", p, V8.float())
     return o.reshape(nq * hd).to(torch.bfloat16)
 
 
