@@ -952,6 +952,64 @@ def run_prefill(args):
     return rec
 
 
+def run_batch(args):
+    """The batch-16, 32k-context case of the tensor-parallel configuration, on one GPU: the 36-layer model
+    (per-channel FP8, FP8 head), `--batch` sequences with their caches pre-filled with N(0,1) rows up to
+    `--ctx` (bf16 or, with --kv fp8, the FP8 cache), then K greedy steps of generate.BatchEngine from seeded
+    random tokens, CUDA graph replays timed with CUDA events. Prints one JSON line: tokens/s over all sequences,
+    and the step's algorithmic bytes (every weight once, each sequence's KV rows up to its position, the
+    appended rows) against the measured HBM peak. The KV cache alone is ~78 GB (bf16), far above L2."""
+    import model as M
+    from generate import BatchEngine
+    peak, peak_kind = peaks()
+    B, ctx, K, W = args.batch, args.ctx, args.steps, max(args.warmup, 3)
+    cfg = M.Config()
+    m = M.Qwen3FP8Decode.synthetic(cfg, max_seq=ctx + K + W + 8, device="cuda", seed=args.seed,
+                                   scale_mode=args.scale, head_dtype="fp8", norm_init="ones", batch=B)
+    if args.kv == "fp8":
+        m.set_kv_dtype("fp8")
+    m.fill_cache_random(ctx, seed=1234)
+    eng = BatchEngine(m)
+    g = torch.Generator().manual_seed(args.seed)
+    toks = torch.randint(0, cfg.vocab, (B,), generator=g, dtype=torch.int32)
+    start = torch.tensor([[ctx, 0]] * B, dtype=torch.int32)
+    eng.token.copy_(toks)
+    eng.state.copy_(start)
+    eng.capture()
+    eng.step(W)
+    torch.cuda.synchronize()
+    eng.token.copy_(toks)
+    eng.state.copy_(start)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        torch.cuda.synchronize()
+        e0.record()
+        eng.step(K)
+        e1.record()
+        torch.cuda.synchronize()
+    t = e0.elapsed_time(e1) * 1e-3
+    eng.check()
+    wb = m.weight_bytes()
+    weights = sum(v for v in wb.values())
+    row = (128 + 4) if args.kv == "fp8" else 256
+    kv_per_step = sum(B * 2 * cfg.layers * cfg.n_kv_heads * (ctx + i + 1) * row for i in range(K)) / K
+    step_bytes = weights + kv_per_step
+    gbs = step_bytes / (t / K) / 1e9
+    rec = {"metric": "batched decode tokens/s", "value": B * K / t, "unit": "tokens/s", "batch": B, "ctx": ctx,
+           "kv": args.kv, "steps": K, "warmup": W, "ms_per_step": t / K * 1e3, "higher_is_better": True,
+           "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                        "bytes_per_step": step_bytes, "weight_bytes": weights, "kv_bytes": kv_per_step,
+                        "peak_kind": peak_kind},
+           "tokens_head": eng.out_tokens[:2, :4].tolist(), "dtype": "fp8 weights, bf16 activations",
+           "data": "synthetic", "config": {"workload": f"Qwen3-8B FP8, batch {B}, context {ctx}, {args.kv} KV, "
+                                                       "1 GPU (the batch-16 case of the TP configuration)",
+                                           "l2": "weights and KV far above L2, no flush"},
+           "clocks": clk.summary()}
+    print(json.dumps(rec), flush=True)
+    return rec
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--profile-kernel", choices=["qkv", "o_proj", "gate_up", "down", "lm_head", "attention", "decode_step",
@@ -982,6 +1040,9 @@ def main():
     ap.add_argument("--shapes", default="", help="--sweep gemv: comma-separated KxN shapes instead of the five")
     ap.add_argument("--rows", default="", help="--sweep gemv: comma-separated row counts instead of 1,4,16,64")
     ap.add_argument("--timeline-out", default="", help="--timeline: also save the raw stamps (torch.save) here")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="batched decode (generate.BatchEngine) of this many sequences at --ctx, one GPU")
+    ap.add_argument("--ctx", type=int, default=32768, help="--batch: the context the caches are filled to")
     ap.add_argument("--prefill", action="store_true",
                     help="prompt processing: chunked prefill against the decode-path prefill (--prompt tokens)")
     ap.add_argument("--prompt", type=int, default=512, help="--prefill: prompt length")
@@ -993,6 +1054,8 @@ def main():
         return run_timeline(args)
     if args.prefill:
         return run_prefill(args)
+    if args.batch:
+        return run_batch(args)
     if args.sweep == "attention":
         return run_attention_sweep(args)
     if args.sweep == "gemv":

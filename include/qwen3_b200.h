@@ -296,6 +296,9 @@ int qk_prefill_attention(const void* q, int M, int p0, int n_q, int n_kv, const 
                          int max_seq, float scale, void* out, qk_stream_t stream);
 int qk_add_rows(void* resid, const void* y, long long n, qk_stream_t stream);
 int qk_swiglu_rows(const void* gu, int M, int I, void* h, qk_stream_t stream);
+/* best[r] = the packed argmax key (the lm_head's: order-preserving value bits, then ~index, so ties go to the
+ * lowest index) of bf16 logits row r of [rows][V]; qk_finalize decodes it. The batched decode step's argmax. */
+int qk_argmax_rows(const void* logits, int rows, int V, unsigned long long* best, qk_stream_t stream);
 
 /* Tensor-parallel helpers (no counterpart in the single-GPU reference; the TP plan of its decode step):
  * resid[i] = bf16(resid[i] + bf16(sum[i])) for the fp32 all-reduced partial of a row-parallel GEMV (the

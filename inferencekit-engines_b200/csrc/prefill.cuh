@@ -251,4 +251,35 @@ __global__ void swiglu_rows_kernel(const bf16* __restrict__ gu, int M, int I, bf
   }
 }
 
+// Greedy argmax of each row of bf16 logits [rows][V] (ties to the lowest index), as the packed u64 key of the
+// decode step's lm_head (argmax_key), written to best[row]; finalize_kernel decodes it. One CTA of 1024 threads
+// per row.
+__global__ void __launch_bounds__(1024) argmax_rows_kernel(const bf16* __restrict__ logits, int V,
+                                                           unsigned long long* __restrict__ best) {
+  __shared__ unsigned long long red[32];
+  const int row = blockIdx.x, tid = threadIdx.x;
+  const bf16* x = logits + (size_t)row * V;
+  unsigned long long key = 0ull;
+  for (int i = tid; i < V; i += 1024) {
+    const unsigned long long k = argmax_key(__bfloat162float(x[i]), i);
+    key = k > key ? k : key;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+    key = other > key ? other : key;
+  }
+  if ((tid & 31) == 0) red[tid >> 5] = key;
+  __syncthreads();
+  if (tid < 32) {
+    key = red[tid];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+      key = other > key ? other : key;
+    }
+    if (tid == 0) best[row] = key;
+  }
+}
+
 }  // namespace qk

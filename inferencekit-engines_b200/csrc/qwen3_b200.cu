@@ -833,6 +833,12 @@ int qk_add_rows(void* resid, const void* y, long long n, qk_stream_t stream) {
   return plain_launch_status("add_rows launch");
 }
 
+int qk_argmax_rows(const void* logits, int rows, int V, unsigned long long* best, qk_stream_t stream) {
+  if (!logits || !best || rows < 1 || V < 1) return fail(QK_EINVAL, "bad argmax_rows arguments");
+  argmax_rows_kernel<<<rows, 1024, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<const bf16*>(logits), V, best);
+  return plain_launch_status("argmax_rows launch");
+}
+
 int qk_swiglu_rows(const void* gu, int M, int I, void* h, qk_stream_t stream) {
   if (!gu || !h || M < 1 || I < 1) return fail(QK_EINVAL, "bad swiglu_rows arguments");
   swiglu_rows_kernel<<<elementwise_blocks((long long)M * I), 256, 0, static_cast<cudaStream_t>(stream)>>>(

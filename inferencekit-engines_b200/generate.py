@@ -277,3 +277,98 @@ class Engine:
         out += self.out_tokens[: gen_len - 1].tolist()
         self.check()
         return out
+
+
+class BatchEngine:
+    """Greedy decode of B sequences per step (the batch-16 case of the tensor-parallel configuration, here on one
+    GPU), the reference engine's step structure with batched ops: per layer the qkv, o_proj, gate_up and down
+    projections through the tcgen05 batched linear (B activation rows; each weight byte streams once per step
+    for all B sequences), the attention op over each sequence's own cache and position (bf16 or FP8 KV), the
+    residual and SwiGLU row kernels; then the final RMSNorm + FP8 lm_head as one more batched linear, the row
+    argmax and finalize. `state` is [B, 2] ([pos, step] per sequence), `token` [B]; one CUDA graph per step.
+    Needs the FP8 (per-channel) head: the batched linear takes FP8 weights only."""
+
+    def __init__(self, model: Qwen3FP8Decode, pdl: bool = True):
+        m = self.m = model
+        if not isinstance(m.lm_head, Linear):
+            raise ValueError("BatchEngine needs the FP8 lm_head (the batched linear takes FP8 weights)")
+        self.k = ops()
+        self.k.set_pdl(pdl)
+        cfg, dev, B = m.cfg, m.device, m.batch
+        self.B, self.max_seq = B, m.max_seq
+        bf = dict(dtype=torch.bfloat16, device=dev)
+        self.token = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.state = torch.zeros(B, 2, dtype=torch.int32, device=dev)
+        self.out_tokens = torch.zeros(B, m.max_seq, dtype=torch.int32, device=dev)
+        self.best = torch.zeros(B, dtype=torch.int64, device=dev)
+        nq, nkv, hd = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
+        self.resid = torch.zeros(B, cfg.hidden, **bf)
+        self.qkv = torch.zeros(B, (nq + 2 * nkv) * hd, **bf)
+        self.attn = torch.zeros(B, nq * hd, **bf)
+        self.y = torch.zeros(B, cfg.hidden, **bf)
+        self.gu = torch.zeros(B, 2 * cfg.inter, **bf)
+        self.h = torch.zeros(B, cfg.inter, **bf)
+        self.logits = torch.zeros(B, cfg.vocab, **bf)
+        self.max_splits = (m.max_seq + 63) // 64
+        self.o_part = torch.zeros(B, nq, self.max_splits, hd, dtype=torch.float32, device=dev)
+        self.ml_part = torch.zeros(B, nq, self.max_splits, 2, dtype=torch.float32, device=dev)
+        self.counters = torch.zeros(B, nkv, dtype=torch.int32, device=dev)
+        self.w = [tuple(pack_fp8_tiles(unpack_fp8(lin.packed, lin.N, lin.K, lin.pairs))
+                        for lin in (L.qkv, L.o, L.gu, L.down)) for L in m.layers]
+        self.head_w = pack_fp8_tiles(unpack_fp8(m.lm_head.packed, m.lm_head.N, m.lm_head.K))
+        self.graph = None
+
+    def decode_step(self):
+        m, k, cfg = self.m, self.k, self.m.cfg
+        k.embed(self.token, m.embed, self.resid)
+        for li, L in enumerate(m.layers):
+            wq, wo, wgu, wd = self.w[li]
+            k.fp8_gemm_rows(self.resid, wq, L.qkv.scale, self.qkv, norm_w=L.ln1, eps=cfg.eps)
+            if m.kv_dtype == "fp8":
+                k.attention_fp8kv(self.qkv, L.q_norm, L.k_norm, m.cos, m.sin, self.state, m.k_cache[li],
+                                  m.k_scale[li], m.v_cache[li], m.v_scale[li], self.o_part, self.ml_part, self.attn,
+                                  cfg.head_dim ** -0.5, cfg.eps, batch=self.B)
+            else:
+                k.attention(self.qkv, L.q_norm, L.k_norm, m.cos, m.sin, self.state, m.k_cache[li], m.v_cache[li],
+                            self.o_part, self.ml_part, self.counters, self.attn, cfg.head_dim ** -0.5, cfg.eps, 0, 64,
+                            batch=self.B)
+            k.fp8_gemm_rows(self.attn, wo, L.o.scale, self.y)
+            k.add_rows(self.resid, self.y)
+            k.fp8_gemm_rows(self.resid, wgu, L.gu.scale, self.gu, norm_w=L.ln2, eps=cfg.eps)
+            k.swiglu_rows(self.gu, self.h)
+            k.fp8_gemm_rows(self.h, wd, L.down.scale, self.y)
+            k.add_rows(self.resid, self.y)
+        k.fp8_gemm_rows(self.resid, self.head_w, m.lm_head.scale, self.logits, norm_w=m.norm, eps=cfg.eps)
+        k.argmax_rows(self.logits, self.best)
+        k.finalize(self.best, self.token, self.out_tokens, self.state)
+
+    def capture(self):
+        """One decode step into a CUDA graph (needs a valid state; the warm-up steps rewrite the KV rows at the
+        current positions with identical values, so only token and state are restored)."""
+        token, state = self.token.clone(), self.state.clone()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                self.token.copy_(token)
+                self.state.copy_(state)
+                self.decode_step()
+        torch.cuda.current_stream().wait_stream(s)
+        self.token.copy_(token)
+        self.state.copy_(state)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.decode_step()
+        torch.cuda.synchronize()
+
+    def step(self, n: int = 1, use_graph: bool = True):
+        for _ in range(n):
+            if use_graph:
+                self.graph.replay()
+            else:
+                self.decode_step()
+
+    def check(self):
+        err = self.k.device_error()
+        if err:
+            raise RuntimeError(f"batched decode step failed on the device (error word {err:#x})")

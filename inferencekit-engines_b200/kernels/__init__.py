@@ -74,6 +74,7 @@ _SIGS = {
     "qk_prefill_attention": ([_VP, _I, _I, _I, _I, _VP, _VP, _I, _F, _VP, _VP], _I),
     "qk_add_rows": ([_VP, _VP, ctypes.c_longlong, _VP], _I),
     "qk_swiglu_rows": ([_VP, _I, _I, _VP, _VP], _I),
+    "qk_argmax_rows": ([_VP, _I, _I, _VP, _VP], _I),
 }
 
 
@@ -378,6 +379,11 @@ class DecodeOps:
         """h[m] = bf16(bf16(silu(gate)) * up) for gu = [gate | up] rows [M, 2I]; h [M, I]."""
         M, I = h.shape
         self._check(self.lib.qk_swiglu_rows(_p(gu), M, I, _p(h), _stream()), "swiglu_rows")
+
+    def argmax_rows(self, logits, best):
+        """best[r] = packed argmax key of bf16 logits row r ([rows, V]; ties to the lowest index)."""
+        rows, V = logits.shape
+        self._check(self.lib.qk_argmax_rows(_p(logits), rows, V, _p(best), _stream()), "argmax_rows")
 
     def finalize(self, best, token, out_tokens, state):
         b = token.numel()
