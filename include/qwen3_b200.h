@@ -261,10 +261,11 @@ int qk_fp8_gemm_tiles(const void* x, const void* norm_w, int M, int K, const voi
  * fewer long-context KV bytes, different numerics). Each cached K and V row (sequence, KV head, position) is 128
  * e4m3 bytes plus one fp32 scale: s = amax/448 (div.full), q = e4m3(x / s) round-to-nearest-even, saturating,
  * s = 0 -> 0, where x is the bf16 row the bf16 cache would hold (K normalised and rotated, V as projected).
- * Scores s_j = (q . k8_j) * ks_j * scale; per 64-key split m = max, p = exp(s - m), l = sum p; o = sum_j
- * (p_j * vs_j) * v8_j; the splits merge as in qk_attention. Appends the new K and V rows (and scales) at pos.
- * k_cache/v_cache: [batch][n_kv][max_seq][128] bytes, k_scale/v_scale: [batch][n_kv][max_seq] fp32; o_part,
- * ml_part, state and out as qk_attention with chunk 64 (max_splits * 64 >= max_seq). */
+ * Scores s_j = (q . k8_j) * ks_j * scale; per split (128 keys, or 512 when max_seq >= 16384) a running
+ * softmax over 128-key blocks (m, l, p = exp(s - m)) and o = sum_j (p_j * vs_j) * v8_j; the splits merge as in
+ * qk_attention. Appends the new K and V rows (and scales) at pos. k_cache/v_cache: [batch][n_kv][max_seq][128]
+ * bytes, k_scale/v_scale: [batch][n_kv][max_seq] fp32; o_part, ml_part, state and out as qk_attention
+ * (max_splits * 128 >= max_seq suffices). */
 int qk_attention_fp8kv(const void* qkv, const void* q_norm_w, const void* k_norm_w, const void* cos_tab,
                        const void* sin_tab, const int* state, void* k_cache, float* k_scale, void* v_cache,
                        float* v_scale, float* o_part, float* ml_part, void* out, int batch, int n_kv, int max_seq,

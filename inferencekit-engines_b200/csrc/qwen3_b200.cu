@@ -858,12 +858,15 @@ extern "C" int qk_attention_fp8kv(const void* qkv, const void* q_norm_w, const v
       !v_scale || !o_part || !ml_part || !out)
     return fail(QK_EINVAL, "null pointer argument");
   if (batch < 1 || batch > 65535 || n_kv < 1 || n_kv > 64 || max_seq < 1) return fail(QK_EINVAL, "bad batch/n_kv/max_seq");
-  if ((long long)max_splits * KV8_SPLIT < max_seq) return fail(QK_EINVAL, "o_part too small: max_splits*64 < max_seq");
+  // long contexts: 4 blocks (512 keys) per split, each CTA streaming them double-buffered; shorter ones one
+  // block per split, for enough CTAs
+  const int blocks = max_seq >= 16384 ? KV8_MAX_BLOCKS : 1, split_keys = KV8_KEYS * blocks;
+  if ((long long)max_splits * split_keys < max_seq) return fail(QK_EINVAL, "o_part too small: max_splits*%d < max_seq", split_keys);
   if (max_splits > 4096) return fail(QK_EINVAL, "max_splits %d > 4096", max_splits);
   if (qkv_stride < n_kv * 6 * HEAD_DIM || state_stride < 1) return fail(QK_EINVAL, "bad qkv_stride/state_stride");
   if (!aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(qkv, 8) || !aligned(k_scale, 4) || !aligned(v_scale, 4))
     return fail(QK_EINVAL, "caches must be 16-byte aligned, qkv 8-byte");
-  if ((long long)n_kv * ((max_seq + KV8_KEYS - 1) / KV8_KEYS) > 0x7fffffff) return fail(QK_EINVAL, "max_seq too large");
+  if ((long long)n_kv * ((max_seq + split_keys - 1) / split_keys) > 0x7fffffff) return fail(QK_EINVAL, "max_seq too large");
   Kv8Params p = {};
   p.qkv = static_cast<const bf16*>(qkv);
   p.q_norm_w = static_cast<const bf16*>(q_norm_w);
@@ -882,11 +885,14 @@ extern "C" int qk_attention_fp8kv(const void* qkv, const void* q_norm_w, const v
   p.max_splits = max_splits;
   p.qkv_stride = qkv_stride;
   p.state_stride = state_stride;
+  p.blocks = blocks;
   p.scale = scale;
   p.eps = eps;
-  const dim3 grid(n_kv * ((max_seq + KV8_KEYS - 1) / KV8_KEYS), batch);
-  if (int r = launch(attn_fp8kv_partials_kernel, grid, dim3(KV8_THREADS), 0, stream, p)) return r;
-  AttnParams m = {};   // the merge reads the partials in the bf16 kernel's layout, 64-key splits
+  const dim3 grid(n_kv * ((max_seq + split_keys - 1) / split_keys), batch);
+  const int smem_p = (int)kv8_smem_bytes();
+  if (int r = ensure_smem((const void*)attn_fp8kv_partials_kernel, smem_p)) return r;
+  if (int r = launch(attn_fp8kv_partials_kernel, grid, dim3(KV8_THREADS), smem_p, stream, p)) return r;
+  AttnParams m = {};   // the merge reads the partials in the bf16 kernel's layout, one per split
   m.state = state;
   m.o_part = o_part;
   m.ml_part = ml_part;
@@ -895,7 +901,7 @@ extern "C" int qk_attention_fp8kv(const void* qkv, const void* q_norm_w, const v
   m.max_seq = max_seq;
   m.max_splits = max_splits;
   m.state_stride = state_stride;
-  m.chunk = KV8_SPLIT;
+  m.chunk = split_keys;
   m.tl_slot = -1;
   const int smem_m = (int)attn_merge_smem_bytes(max_splits);
   if (int r = ensure_smem((const void*)attn_merge_kernel, smem_m)) return r;

@@ -7,7 +7,7 @@ The contract (include/qwen3_b200.h, oracle.quant_kv_rows / attention_fp8kv_f32):
   rounding tie), and no other cache byte or scale changes;
 * the output matches the fp32 restatement over the kernel's own cache within 5e-3 rel-L2 (the bf16 attention
   op's bar against fp32), at contexts across the 64-key split and 128-key block boundaries, ragged batches
-  included;
+  included, for both split sizes (128 keys, and 512 keys streamed as 4 double-buffered blocks);
 * against the bf16 cache the quantization costs a few percent of the output (measured and bounded at 5e-2);
 * a 2-layer model with an FP8 cache decodes through the op path; its first token's logits stay within 0.2
   rel-L2 of the bf16-cache model's (0.127 measured: every attention output moves by a few percent and the W8A8
@@ -83,9 +83,10 @@ def e4m3_close(a8, b8):
     return ((a - b).abs() <= 0.125 * torch.maximum(a.abs(), b.abs()) + 2.0 ** -9).all().item()
 
 
-@pytest.mark.parametrize("lengths", [[0], [63], [64, 127], [128, 1000], [4095, 2049]])
-def test_fp8kv_append_and_attention(lengths):
-    max_seq = 4096
+@pytest.mark.parametrize("lengths,max_seq", [([0], 4096), ([63], 4096), ([64, 127], 4096), ([128, 1000], 4096),
+                                             ([4095, 2049], 4096), ([16383, 700, 5000], 16384)])
+def test_fp8kv_append_and_attention(lengths, max_seq):
+    """max_seq 4096: one 128-key block per split; 16384: 512-key splits of 4 double-buffered blocks."""
     d = setup(lengths, max_seq, seed=sum(lengths) + len(lengths))
     out8, k8, ks, v8, vs = run_fp8(d)
     out16, kb, vb = run_bf16(d)
