@@ -581,6 +581,37 @@ def run_profile_kernel(args):
         torch.cuda.synchronize()
         print(f"profiled gemm_rows x{args.launches}")
         return
+    if args.profile_kernel == "attention_fp8kv":   # 8 sequences at 32k over an FP8 cache (512-key splits)
+        batch, max_seq = 8, 32769
+        kb = torch.randn(batch, 8, max_seq, 128, device=dev).to(torch.bfloat16)
+        k8, ks = M.quantize_kv_rows(kb)
+        v8, vs = M.quantize_kv_rows(kb.flip(2))
+        del kb
+        qkv = torch.randn(batch, 6144, device=dev).to(torch.bfloat16)
+        nw = torch.ones(128, dtype=torch.bfloat16, device=dev)
+        cos, sin = M.rope_tables(max_seq, 128, 1e6, dev)
+        ms = (max_seq + 63) // 64
+        o_part = torch.zeros(batch, 32, ms, 128, device=dev)
+        ml = torch.zeros(batch, 32, ms, 2, device=dev)
+        out = torch.empty(batch, 4096, dtype=torch.bfloat16, device=dev)
+        state = torch.tensor([[max_seq - 1, 0]] * batch, dtype=torch.int32, device=dev).view(-1)
+        for _ in range(args.launches):
+            k.attention_fp8kv(qkv, nw, nw, cos, sin, state, k8.view(torch.uint8), ks, v8.view(torch.uint8), vs, o_part,
+                              ml, out, 128 ** -0.5, 1e-6, batch=batch)
+        torch.cuda.synchronize()
+        print(f"profiled attention_fp8kv x{args.launches}")
+        return
+    if args.profile_kernel == "prefill_attention":   # the last 128-row chunk of a 2,048-token prompt
+        n_kv, max_seq, M_, p0 = 8, 2048, 128, 1920
+        kc = torch.randn(n_kv, max_seq, 128, device=dev).to(torch.bfloat16)
+        vc = torch.randn(n_kv, max_seq, 128, device=dev).to(torch.bfloat16)
+        q = torch.randn(M_, 32, 128, device=dev).to(torch.bfloat16)
+        out = torch.empty(M_, 4096, dtype=torch.bfloat16, device=dev)
+        for _ in range(args.launches):
+            k.prefill_attention(q, p0, kc, vc, 128 ** -0.5, out)
+        torch.cuda.synchronize()
+        print(f"profiled prefill_attention x{args.launches}")
+        return
     if args.profile_kernel == "attention":
         max_seq = 4096
         kc = torch.randn(8, max_seq, 128, device=dev).to(torch.bfloat16)
@@ -1013,7 +1044,7 @@ def run_batch(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--profile-kernel", choices=["qkv", "o_proj", "gate_up", "down", "lm_head", "attention", "decode_step",
-                                                 "gemm_rows"],
+                                                 "gemm_rows", "attention_fp8kv", "prefill_attention"],
                     help="launch one kernel --launches times on synthetic inputs and exit (for ncu)")
     ap.add_argument("--launches", type=int, default=3)
     ap.add_argument("--layers", type=int, default=2, help="decoder layers of the --profile-kernel decode_step model")
