@@ -22,7 +22,9 @@ It restates, in plain torch CPU ops, the arithmetic of the reference engine
                    model.py:271-272 does (bf16 probabilities), which is what the golden fixtures pin.
 * `prefill_layer`  Q/model.py:255-279 for M prompt positions at once (start..start+M-1): the same layer with
                    the KV rows written for every position and causal attention (row m sees cache rows
-                   0..start+m), fp32 scores and probabilities, rounded to bf16 once.
+                   0..start+m), fp32 scores and probabilities, rounded to bf16 once; `attn_impl="sdpa"`
+                   calls SDPA as model.py:271-273 does, which tests/golden/prefill_block.npz pins bit for bit
+                   against the reference's own forward(tokens, 0).
 * `quant_kv_rows`, `attention_fp8kv_f32`: the FP8 KV cache's contract (an extension with no reference
                    counterpart): e4m3 rows with one fp32 scale each, scores and probabilities in fp32.
 * `lm_head_argmax` Q/model.py:280-281 (final RMSNorm + linear) and Q/kernels/decode.cu:572-661: greedy
@@ -191,9 +193,11 @@ def decode_layer(h: torch.Tensor, L: LayerW, k_cache: torch.Tensor, v_cache: tor
 
 def prefill_layer(h: torch.Tensor, L: LayerW, k_cache: torch.Tensor, v_cache: torch.Tensor, start: int,
                   cos: torch.Tensor, sin: torch.Tensor, eps: float, n_heads: int = 32, n_kv: int = 8,
-                  head_dim: int = 128) -> torch.Tensor:
+                  head_dim: int = 128, attn_impl: str = "f32") -> torch.Tensor:
     """M positions through one layer (the reference's batched forward). h bf16 [M, H]; k_cache/v_cache bf16
-    [n_kv, max_seq, 128] are written at start..start+M-1 in place. Returns the residual stream bf16 [M, H]."""
+    [n_kv, max_seq, 128] are written at start..start+M-1 in place. Returns the residual stream bf16 [M, H].
+    attn_impl "f32": causal attention in fp32; "sdpa": torch SDPA exactly as Q/model.py:271-273 calls it
+    (bf16, is_causal for M > 1), which the golden prefill fixture pins."""
     M, hd = h.shape[0], head_dim
     x = rms_norm(h, L.ln1, eps)
     qkv = fp8_linear(x, L.w_qkv, L.s_qkv)
@@ -204,12 +208,17 @@ def prefill_layer(h: torch.Tensor, L: LayerW, k_cache: torch.Tensor, v_cache: to
     k_cache[:, start:start + M] = k.transpose(0, 1)
     v_cache[:, start:start + M] = v.reshape(M, n_kv, hd).transpose(0, 1)
     ctx = start + M
-    K = k_cache[:, :ctx].float().repeat_interleave(n_heads // n_kv, 0)     # [n_heads, ctx, 128]
-    V = v_cache[:, :ctx].float().repeat_interleave(n_heads // n_kv, 0)
-    sc = torch.einsum("mhd,hjd->hmj", q.float(), K) * hd ** -0.5
-    pos = start + torch.arange(M, device=h.device)
-    sc = sc.masked_fill((torch.arange(ctx, device=h.device)[None, :] > pos[:, None])[None], float("-inf"))
-    attn = torch.einsum("hmj,hjd->mhd", torch.softmax(sc, dim=-1), V).reshape(M, n_heads * hd).to(torch.bfloat16)
+    if attn_impl == "sdpa":
+        a = F.scaled_dot_product_attention(q.transpose(0, 1)[None], k_cache[:, :ctx][None], v_cache[:, :ctx][None],
+                                           is_causal=(M > 1), scale=hd ** -0.5, enable_gqa=True)
+        attn = a[0].transpose(0, 1).reshape(M, n_heads * hd)
+    else:
+        K = k_cache[:, :ctx].float().repeat_interleave(n_heads // n_kv, 0)     # [n_heads, ctx, 128]
+        V = v_cache[:, :ctx].float().repeat_interleave(n_heads // n_kv, 0)
+        sc = torch.einsum("mhd,hjd->hmj", q.float(), K) * hd ** -0.5
+        pos = start + torch.arange(M, device=h.device)
+        sc = sc.masked_fill((torch.arange(ctx, device=h.device)[None, :] > pos[:, None])[None], float("-inf"))
+        attn = torch.einsum("hmj,hjd->mhd", torch.softmax(sc, dim=-1), V).reshape(M, n_heads * hd).to(torch.bfloat16)
     h = h + fp8_linear(attn, L.w_o, L.s_o)
     x = rms_norm(h, L.ln2, eps)
     gu = fp8_linear(x, L.w_gu, L.s_gu)

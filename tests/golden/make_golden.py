@@ -8,7 +8,7 @@ What it does: imports the reference's `model.py` (qwen3-8b-fp8_rtx-5090/model.py
 `fp8_linear` (imported from the Triton kernels at model.py:18) with the CPU restatement in
 oracle/qwen3_ref.py, builds a `Qwen3FP8` object around seeded synthetic weights (bypassing the safetensors
 loader, model.py:155-233) and calls the reference's `forward(tokens, start)` (model.py:243-281) on CPU for
-single-token decode steps. Everything except the FP8 GEMM arithmetic is the reference's code: RMSNorm,
+single-token decode steps and one multi-token prefill. Everything except the FP8 GEMM arithmetic is the reference's code: RMSNorm,
 q/k norm, RoPE, KV-cache writes, SDPA attention, residuals, SwiGLU, lm_head.
 
 Fixtures (bf16 tensors stored as uint16 bit patterns):
@@ -17,6 +17,8 @@ Fixtures (bf16 tensors stored as uint16 bit patterns):
   cfg1_block.npz    the same with 128x128 block scales (the reference checkpoint's format).
   steps_block.npz   a 2-layer model (block scales, bf16 lm_head of 1024 rows): 6 teacher-forced prompt
                     tokens then 10 greedy steps, all through forward(M=1); tokens + every step's logits.
+  prefill_block.npz the same model, a 24-token prompt through one forward(tokens, 0) (the batched prefill,
+                    causal SDPA): the last position's logits and both layers' K/V rows 0..23.
 Inputs are regenerated from seeds by the package's synthetic-weight generator; each fixture stores a
 checksum of its inputs so a drift in generation is detected instead of silently changing the baseline.
 """
@@ -177,6 +179,28 @@ def steps(ref_model, out_path: str, seed: int = 7, vocab: int = 1024, n_layers: 
     print(f"wrote {out_path}: tokens {toks}")
 
 
+def prefill(ref_model, out_path: str, seed: int = 7, vocab: int = 1024, n_layers: int = 2, P: int = 24):
+    """The same 2-layer model as `steps`, a P-token prompt through ONE forward(tokens, 0) (the reference's
+    batched prefill: causal SDPA, K/V rows 0..P-1 written per layer); the last position's logits and the K/V
+    rows."""
+    lw = []
+    for li in range(n_layers):
+        w, norms = layer_inputs(seed + li, "block")
+        lw.append((w, norms))
+    embed = M.randn((vocab, 4096), seed, "steps.embed", std=1.0).to(torch.bfloat16)
+    head = M.randn((vocab, 4096), seed, "steps.head", std=0.02).to(torch.bfloat16)
+    norm = M.synth_norm(seed, "steps.norm", 4096, "random")
+    m = make_ref_object(ref_model, lw, embed, head, norm, 32)
+    g = torch.Generator().manual_seed(M.name_seed(seed, "prefill.prompt"))
+    prompt = torch.randint(0, vocab, (P,), generator=g)
+    lg = m.forward(prompt, 0)
+    assert m.last_prefill_path == "ref"
+    np.savez_compressed(out_path, seed=seed, vocab=vocab, n_layers=n_layers, prompt=prompt.numpy(),
+                        logits=u16(lg), k_rows=u16(m.k_cache[:, :, :P]), v_rows=u16(m.v_cache[:, :, :P]),
+                        inputs_sha=checksum(embed, head, norm, *[w["qkv"][0] for w, _ in lw]))
+    print(f"wrote {out_path}: argmax {int(lg.float().argmax())}")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=refpath.engine_dir())
@@ -186,6 +210,7 @@ def main():
     cfg1(ref_model, "channel", os.path.join(HERE, "cfg1_channel.npz"))
     cfg1(ref_model, "block", os.path.join(HERE, "cfg1_block.npz"))
     steps(ref_model, os.path.join(HERE, "steps_block.npz"))
+    prefill(ref_model, os.path.join(HERE, "prefill_block.npz"))
 
 
 if __name__ == "__main__":

@@ -81,6 +81,35 @@ def test_multi_step_tokens_match_reference_forward():
     assert toks == [int(t) for t in fx["tokens"]]
 
 
+def test_prefill_matches_reference_batched_forward():
+    """The oracle's batched layer (prefill_layer, SDPA attention as the reference calls it) over a 24-token
+    prompt == the reference's own forward(tokens, 0): the last position's logits and every K/V row, bit for bit.
+    This pins the restatement the chunked prefill is tested against."""
+    fx = load("prefill_block.npz")
+    seed, vocab, nl = int(fx["seed"]), int(fx["vocab"]), int(fx["n_layers"])
+    layers = []
+    for li in range(nl):
+        w, n = layer_inputs(seed + li, "block")
+        layers.append(O.LayerW(n["ln1"], n["ln2"], n["q_norm"], n["k_norm"], w["qkv"][0], w["qkv"][1],
+                               w["o_proj"][0], w["o_proj"][1], w["gate_up"][0], w["gate_up"][1],
+                               w["down_proj"][0], w["down_proj"][1]))
+    embed = M.randn((vocab, 4096), seed, "steps.embed", std=1.0).to(torch.bfloat16)
+    head = M.randn((vocab, 4096), seed, "steps.head", std=0.02).to(torch.bfloat16)
+    norm = M.synth_norm(seed, "steps.norm", 4096, "random")
+    assert checksum(embed, head, norm, *[L.w_qkv for L in layers]) == str(fx["inputs_sha"])
+    prompt = torch.from_numpy(fx["prompt"]).long()
+    P, max_seq = prompt.numel(), 32
+    kc = torch.zeros(nl, 8, max_seq, 128, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    cos, sin = M.rope_tables(max_seq, 128, 1e6, "cpu")
+    h = embed[prompt]
+    for li, L in enumerate(layers):
+        h = O.prefill_layer(h, L, kc[li], vc[li], 0, cos, sin, 1e-6, attn_impl="sdpa")
+    lg = O.lm_head_logits(h[-1], norm, head, None, 1e-6)
+    assert np.array_equal(u16(kc[:, :, :P]), fx["k_rows"]) and np.array_equal(u16(vc[:, :, :P]), fx["v_rows"])
+    assert np.array_equal(u16(lg), fx["logits"])
+
+
 def test_act_quant_edge_cases():
     """Zero groups quantize to 0 with scale 0 (decode.cu:105); values round to nearest-even and saturate."""
     x = torch.zeros(256, dtype=torch.bfloat16)
