@@ -17,7 +17,7 @@
 //    values the decode step writes for that position given the same qkv row;
 //  * SwiGLU and the residual add round exactly as the decode epilogues.
 // The attention is fp32 throughout (scores, softmax probabilities, P.V) with one online-softmax pass over 64-key
-// chunks, 8 rows of a KV head per CTA. Its sums run in a different order from the decode path's
+// chunks, 4 rows of a KV head per CTA. Its sums run in a different order from the decode path's
 // split-and-merge, so it matches an fp32 reference to rounding, not the decode step bit for bit.
 #pragma once
 #include "attention.cuh"
@@ -73,21 +73,23 @@ __global__ void __launch_bounds__(256) prefill_qkv_kernel(const bf16* __restrict
   }
 }
 
-// Causal GQA attention of the chunk's queries. CTA (row block, g): PA_ROWS consecutive rows m0 .. m0 + 7
-// (positions p0 + m) and KV head g, i.e. PA_Q = 32 query vectors (head h = 4 g + qi / 8 of row m0 + qi % 8),
+// Causal GQA attention of the chunk's queries. CTA (row block, g): PA_ROWS = 4 consecutive rows m0 .. m0 + 3
+// (positions p0 + m) and KV head g, i.e. PA_Q = 16 query vectors (head h = 4 g + qi / 4 of row m0 + qi % 4),
 // over keys 0 .. p0 + m in chunks of PF_KEYS; 256 threads. The chunk's K and V rows arrive in shared memory by
 // 16-byte cp.async copies, double-buffered (the next chunk loads while this one is computed), so each K/V row
-// crosses L2 once per 8 rows instead of once per row. Per chunk, all fp32:
-//  * scores s = (q . k) * scale, thread = (4 queries, keys j and j + 32), each dot summed over the dims in order;
+// crosses L2 once per 4 rows instead of once per row. Per chunk, all fp32:
+//  * scores s = (q . k) * scale, thread = (2 queries, keys j and j + 32), each dot summed over the dims in order;
 //    keys past a query's position are -inf;
-//  * a running softmax per query (one warp per 4 queries): the chunk's max, the rescale of the old sums by
+//  * a running softmax per query (one warp per 2 queries): the chunk's max, the rescale of the old sums by
 //    exp(m_old - m_new), the exponentials and their sum;
-//  * P.V with thread = (2 queries, 8 dims), the chunk's keys in order, after rescaling the accumulators.
+//  * P.V with thread = (1 query, 8 dims), the chunk's keys in order, after rescaling the accumulators.
 // The output is bf16(acc / l). Every query has key 0 in its first chunk, so no running max stays -inf.
 constexpr int PF_KEYS = 64;
 constexpr int PF_THREADS = 256;
-constexpr int PA_ROWS = 8;
-constexpr int PA_Q = PA_ROWS * GQA;   // 32
+constexpr int PA_ROWS = 4;            // rows per CTA: a 128-row chunk gives 32 x 8 = 256 CTAs
+constexpr int PA_Q = PA_ROWS * GQA;   // 16 query vectors per CTA
+constexpr int PA_QPW = PA_Q / 8;      // scores and softmax: queries per warp
+constexpr int PA_QPT = PA_Q / 16;     // P.V: queries per thread (16 thread groups of 16 dims x 8)
 struct PrefillAttnSmem {
   bf16 k[2][PF_KEYS][HEAD_DIM + 8];   // +8: consecutive rows start 16 bytes apart in bank order
   bf16 v[2][PF_KEYS][HEAD_DIM];
@@ -119,7 +121,7 @@ __global__ void __launch_bounds__(PF_THREADS) prefill_attention_kernel(const bf1
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
   load_chunk(0, 0);
-  for (int i = tid; i < PA_Q * HEAD_DIM; i += PF_THREADS) {   // query qi = h * 8 + r, h = 0..3 within the group
+  for (int i = tid; i < PA_Q * HEAD_DIM; i += PF_THREADS) {   // query qi = h * PA_ROWS + r, h = 0..3 in the group
     const int qi = i / HEAD_DIM, d = i % HEAD_DIM, r = qi % PA_ROWS, h = qi / PA_ROWS;
     sm.q[qi][d] = r < rows ? __bfloat162float(q[((size_t)(m0 + r) * n_q + g * GQA + h) * HEAD_DIM + d]) : 0.f;
   }
@@ -127,15 +129,15 @@ __global__ void __launch_bounds__(PF_THREADS) prefill_attention_kernel(const bf1
     sm.m_run[tid] = -INFINITY;
     sm.l_run[tid] = 0.f;
   }
-  // P.V ownership: queries 2 * (tid / 16) and +1, dims 8 * (tid % 16) .. +7
-  const int pq = (tid >> 4) * 2, pd = (tid & 15) * 8;
-  float acc[2][8];
+  // P.V ownership: queries PA_QPT * (tid / 16) .. +PA_QPT-1, dims 8 * (tid % 16) .. +7
+  const int pq = (tid >> 4) * PA_QPT, pd = (tid & 15) * 8;
+  float acc[PA_QPT][8];
 #pragma unroll
-  for (int a = 0; a < 2; ++a)
+  for (int a = 0; a < PA_QPT; ++a)
 #pragma unroll
     for (int e = 0; e < 8; ++e) acc[a][e] = 0.f;
-  // score ownership: queries 4 * warp .. +3, keys lane and lane + 32
-  const int sq = warp * 4;
+  // score ownership: queries PA_QPW * warp .. +PA_QPW-1, keys lane and lane + 32
+  const int sq = warp * PA_QPW;
   int buf = 0;
   for (int j0 = 0; j0 < ctx; j0 += PF_KEYS, buf ^= 1) {
     const int nj = min(PF_KEYS, ctx - j0);
@@ -147,9 +149,9 @@ __global__ void __launch_bounds__(PF_THREADS) prefill_attention_kernel(const bf1
     }
     __syncthreads();
     {   // scores
-      float s[4][2];
+      float s[PA_QPW][2];
 #pragma unroll
-      for (int a = 0; a < 4; ++a) s[a][0] = s[a][1] = 0.f;
+      for (int a = 0; a < PA_QPW; ++a) s[a][0] = s[a][1] = 0.f;
       const int ja = lane, jb = lane + 32;
       for (int d = 0; d < HEAD_DIM; d += 8) {
         const uint4 ka = *reinterpret_cast<const uint4*>(&sm.k[buf][ja][d]);
@@ -159,7 +161,7 @@ __global__ void __launch_bounds__(PF_THREADS) prefill_attention_kernel(const bf1
         const float fb[8] = {bf16lo(kb.x), bf16hi(kb.x), bf16lo(kb.y), bf16hi(kb.y),
                              bf16lo(kb.z), bf16hi(kb.z), bf16lo(kb.w), bf16hi(kb.w)};
 #pragma unroll
-        for (int a = 0; a < 4; ++a) {
+        for (int a = 0; a < PA_QPW; ++a) {
           const float4 q0 = *reinterpret_cast<const float4*>(&sm.q[sq + a][d]);
           const float4 q1 = *reinterpret_cast<const float4*>(&sm.q[sq + a][d + 4]);
           const float qv[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
@@ -171,16 +173,16 @@ __global__ void __launch_bounds__(PF_THREADS) prefill_attention_kernel(const bf1
         }
       }
 #pragma unroll
-      for (int a = 0; a < 4; ++a) {
+      for (int a = 0; a < PA_QPW; ++a) {
         const int pos = p0 + m0 + (sq + a) % PA_ROWS;
         sm.p[sq + a][ja] = (ja < nj && j0 + ja <= pos) ? s[a][0] * scale : -INFINITY;
         sm.p[sq + a][jb] = (jb < nj && j0 + jb <= pos) ? s[a][1] * scale : -INFINITY;
       }
     }
     __syncwarp();
-    // running softmax: warp w owns queries 4w .. 4w + 3, exactly the rows its lanes just scored
+    // running softmax: warp w owns queries PA_QPW w .. +PA_QPW-1, exactly the rows its lanes just scored
 #pragma unroll
-    for (int a = 0; a < 4; ++a) {
+    for (int a = 0; a < PA_QPW; ++a) {
       const int qi = sq + a;
       const float x0 = sm.p[qi][lane], x1 = sm.p[qi][lane + 32];
       const float cmax = warp_max(fmaxf(x0, x1));
@@ -198,28 +200,28 @@ __global__ void __launch_bounds__(PF_THREADS) prefill_attention_kernel(const bf1
     }
     __syncthreads();
     {   // P.V
-      const float r0 = sm.scale_old[pq], r1 = sm.scale_old[pq + 1];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        acc[0][e] *= r0;
-        acc[1][e] *= r1;
+      for (int a = 0; a < PA_QPT; ++a) {
+        const float r = sm.scale_old[pq + a];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[a][e] *= r;
       }
       for (int j = 0; j < nj; ++j) {
         const uint4 vv = *reinterpret_cast<const uint4*>(&sm.v[buf][j][pd]);
         const float vf[8] = {bf16lo(vv.x), bf16hi(vv.x), bf16lo(vv.y), bf16hi(vv.y),
                              bf16lo(vv.z), bf16hi(vv.z), bf16lo(vv.w), bf16hi(vv.w)};
-        const float w0 = sm.p[pq][j], w1 = sm.p[pq + 1][j];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          acc[0][e] += w0 * vf[e];
-          acc[1][e] += w1 * vf[e];
+        for (int a = 0; a < PA_QPT; ++a) {
+          const float w = sm.p[pq + a][j];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[a][e] += w * vf[e];
         }
       }
     }
     __syncthreads();   // this chunk's K/V buffer and p are free for the next load and scores
   }
 #pragma unroll
-  for (int a = 0; a < 2; ++a) {
+  for (int a = 0; a < PA_QPT; ++a) {
     const int qi = pq + a, r = qi % PA_ROWS, h = qi / PA_ROWS;
     if (r >= rows) continue;
     const float inv_l = 1.f / sm.l_run[qi];
