@@ -2,7 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Workload (BASELINE config 2 at "4k ctx"): the 36-layer Qwen3-8B-architecture model with seeded random-init
+Workload (benchmark configuration 2 at "4k ctx"): the 36-layer Qwen3-8B-architecture model with seeded random-init
 FP8 weights (E4M3, per-output-channel fp32 scales), bf16 embeddings, FP8 per-channel lm_head (151936 rows),
 a bf16 KV cache sized for 4096 tokens pre-filled with N(0,1) up to position 4096-K, then K greedy decode
 steps under one CUDA graph (ctx 4096-K .. 4095). One step = one token. Every step reads ~8.2 GB (weights +
@@ -754,7 +754,7 @@ def run_timeline(args):
 
 
 def run_gemv_sweep(args):
-    """the FP8 linear of each decode GEMV shape K -> N in {4096->6144, 4096->4096,
+    """Benchmark configuration 3: the FP8 linear of each decode GEMV shape K -> N in {4096->6144, 4096->4096,
     4096->24576, 12288->4096, 4096->151936} for rows in {1, 4, 16, 64}, x ~ N(0,1) bf16, per-channel scales.
     rows 1: the batch-1 GEMV (qk_fp8_gemv, the decode step's kernel; kind 5 = W8A8 dot to fp32); every row
     count also through the tcgen05 batched linear (qk_fp8_gemm_rows: activation quantization + the tensor-core
@@ -822,7 +822,7 @@ def run_gemv_sweep(args):
 
 
 def run_attention_sweep(args):
-    """BASELINE config 4 through the drop-in attention op (the two kernels of qk_attention: partials, merge):
+    """Benchmark configuration 4 through the drop-in attention op (the two kernels of qk_attention: partials, merge):
     contexts L in {1k, 4k, 8k, 16k, 32k}, batch 1 (length L) and batch 8 (lengths ~ U[L/2, L], seeded), KV
     N(0,1) bf16, the new token at position len. Per point: time per call (CUDA events around one replay of a
     graph of K calls, after W eager ones; the caches of as many independent layers as keep the working set
@@ -1065,7 +1065,7 @@ def main():
     ap.add_argument("--no-ref-gpu", action="store_true",
                     help="reference arm: skip timing the reference's own decode kernels on the GPU")
     ap.add_argument("--sweep", choices=["attention", "gemv"],
-                    help="attention: BASELINE config 4 (contexts x batches); gemv: config 3 (shapes x rows)")
+                    help="attention: benchmark configuration 4 (contexts x batches); gemv: configuration 3 (shapes x rows)")
     ap.add_argument("--kv", default="bf16", choices=["bf16", "fp8"],
                     help="--sweep attention: the KV cache format (fp8: e4m3 rows + fp32 row scales)")
     ap.add_argument("--shapes", default="", help="--sweep gemv: comma-separated KxN shapes instead of the five")

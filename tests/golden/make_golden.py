@@ -12,7 +12,7 @@ single-token decode steps and one multi-token prefill. Everything except the FP8
 q/k norm, RoPE, KV-cache writes, SDPA attention, residuals, SwiGLU, lm_head.
 
 Fixtures (bf16 tensors stored as uint16 bit patterns):
-  cfg1_channel.npz  BASELINE config 1: one layer, per-output-channel scales, input hidden N(0,1), KV 0..1023
+  cfg1_channel.npz  benchmark configuration 1: one layer, per-output-channel scales, input hidden N(0,1), KV 0..1023
                     N(0,1), new token at position 1024. Layer output + K/V rows written at 1024.
   cfg1_block.npz    the same with 128x128 block scales (the reference checkpoint's format).
   steps_block.npz   a 2-layer model (block scales, bf16 lm_head of 1024 rows): 6 teacher-forced prompt

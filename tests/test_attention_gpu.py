@@ -120,7 +120,7 @@ def test_attention_long_context_32k():
 
 
 def sweep_lengths(L: int, batch: int, seed: int = 0):
-    """BASELINE config 4's sequence lengths: batch 1 holds L keys; batch 8 holds lengths ~ U[L/2, L], seeded.
+    """Benchmark configuration 4's sequence lengths: batch 1 holds L keys; batch 8 holds lengths ~ U[L/2, L], seeded.
     The new token goes at position len (so the attention covers len + 1 keys)."""
     if batch == 1:
         return [L]

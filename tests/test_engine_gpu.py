@@ -1,6 +1,6 @@
 """Whole-layer and whole-step parity of the B200 engine (GPU).
 
-* BASELINE config 1 (one layer, both scale layouts): the layer output and the K/V rows appended at 1024
+* Benchmark configuration 1 (one layer, both scale layouts): the layer output and the K/V rows appended at 1024
   against the CPU oracle with the decode kernel's attention arithmetic (fp32 probabilities), and against
   the golden fixture of the reference forward.
 * Multi-step: the golden 2-layer model (block scales, bf16 head) decoded by the engine through its CUDA
