@@ -261,7 +261,7 @@ int qk_fp8_gemm_tiles(const void* x, const void* norm_w, int M, int K, const voi
  * fewer long-context KV bytes, different numerics). Each cached K and V row (sequence, KV head, position) is 128
  * e4m3 bytes plus one fp32 scale: s = amax/448 (div.full), q = e4m3(x / s) round-to-nearest-even, saturating,
  * s = 0 -> 0, where x is the bf16 row the bf16 cache would hold (K normalised and rotated, V as projected).
- * Scores s_j = (q . k8_j) * ks_j * scale; per split (128 keys, or 512 when max_seq >= 16384) a running
+ * Scores s_j = (q . k8_j) * ks_j * scale; per split (128, 256 or 512 keys by max_seq) a running
  * softmax over 128-key blocks (m, l, p = exp(s - m)) and o = sum_j (p_j * vs_j) * v8_j; the splits merge as in
  * qk_attention. Appends the new K and V rows (and scales) at pos. k_cache/v_cache: [batch][n_kv][max_seq][128]
  * bytes, k_scale/v_scale: [batch][n_kv][max_seq] fp32; o_part, ml_part, state and out as qk_attention

@@ -7,8 +7,8 @@
 //                      nearest even, saturating; s = 0 gives q = 0. x is the bf16 value the bf16 cache would
 //                      hold: the normalised and rotated K row, or the V row as projected.
 //   scores             s_j = (sum_d q_h[d] * k8_j[d]: dims 0-63 and 64-127 each in order, then added) * s_kj * scale
-//   softmax            per split of 128 or 512 keys (1 or 4 blocks; 4 when max_seq >= 16384, where a long
-//                      context gives enough splits), over its 128-key blocks in order: the running maximum m, the
+//   softmax            per split of 128, 256 or 512 keys (1, 2 or 4 blocks, by max_seq: below 4096, below
+//                      16384, above), over its 128-key blocks in order: the running maximum m, the
 //                      sums rescaled by exp(m_old - m_new), p_j = exp(s_j - m), l = sum p_j (fp32)
 //   P.V                o[d] = sum_j (p_j * s_vj) * v8_j[d], rescaled with the running maximum; within a block 4
 //                      groups of 32 keys, each in order; the groups added in order at the end

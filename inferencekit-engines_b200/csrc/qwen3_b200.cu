@@ -858,9 +858,9 @@ extern "C" int qk_attention_fp8kv(const void* qkv, const void* q_norm_w, const v
       !v_scale || !o_part || !ml_part || !out)
     return fail(QK_EINVAL, "null pointer argument");
   if (batch < 1 || batch > 65535 || n_kv < 1 || n_kv > 64 || max_seq < 1) return fail(QK_EINVAL, "bad batch/n_kv/max_seq");
-  // long contexts: 4 blocks (512 keys) per split, each CTA streaming them double-buffered; shorter ones one
-  // block per split, for enough CTAs
-  const int blocks = max_seq >= 16384 ? KV8_MAX_BLOCKS : 1, split_keys = KV8_KEYS * blocks;
+  // long contexts: 4 blocks (512 keys) per split, each CTA streaming them double-buffered; medium ones 2,
+  // short ones 1, for enough CTAs
+  const int blocks = max_seq >= 16384 ? KV8_MAX_BLOCKS : (max_seq >= 4096 ? 2 : 1), split_keys = KV8_KEYS * blocks;
   if ((long long)max_splits * split_keys < max_seq) return fail(QK_EINVAL, "o_part too small: max_splits*%d < max_seq", split_keys);
   if (max_splits > 4096) return fail(QK_EINVAL, "max_splits %d > 4096", max_splits);
   if (qkv_stride < n_kv * 6 * HEAD_DIM || state_stride < 1) return fail(QK_EINVAL, "bad qkv_stride/state_stride");
